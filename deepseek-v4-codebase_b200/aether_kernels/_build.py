@@ -1,0 +1,63 @@
+"""In-tree build of the sm_100a C-ABI library (explicit nvcc, no JIT cache).
+
+The kernels are written for B200 only: ``-gencode arch=compute_100a,code=sm_100a``.
+nvcc cross-compiles without a GPU, so this runs on a CPU-only host too.
+"""
+from __future__ import annotations
+
+import os
+import shutil
+import subprocess
+from pathlib import Path
+from typing import List, Optional
+
+PKG = Path(__file__).resolve().parent
+CSRC = PKG.parent / "csrc"
+SOURCES = ["capi.cu", "tq.cu", "compat.cu", "csa_decode.cu"]
+OUT = PKG / "libaether_b200.so"
+
+NVCC_FLAGS = [
+    "-gencode", "arch=compute_100a,code=sm_100a",
+    "-O3", "-lineinfo", "-std=c++17",
+    "-Xcompiler", "-fPIC", "-shared",
+    "--expt-relaxed-constexpr",
+]
+
+
+def find_nvcc() -> Optional[str]:
+    nv = shutil.which("nvcc")
+    if nv:
+        return nv
+    for root in (os.environ.get("CUDA_HOME"), "/usr/local/cuda"):
+        if root and (Path(root) / "bin" / "nvcc").is_file():
+            return str(Path(root) / "bin" / "nvcc")
+    return None
+
+
+def needs_build() -> bool:
+    if not OUT.exists():
+        return True
+    mtime = OUT.stat().st_mtime
+    deps = [CSRC / s for s in SOURCES] + list(CSRC.glob("*.cuh"))
+    return any(p.stat().st_mtime > mtime for p in deps)
+
+
+def build(force: bool = False, verbose: bool = False, extra: Optional[List[str]] = None) -> Path:
+    if not force and not needs_build():
+        return OUT
+    nvcc = find_nvcc()
+    if nvcc is None:
+        raise RuntimeError("nvcc was not found; cannot build the Aether sm_100a kernels")
+    tmp = OUT.with_suffix(".so.tmp")
+    cmd = [nvcc, *NVCC_FLAGS, *(extra or []), "-o", str(tmp), *[str(CSRC / s) for s in SOURCES]]
+    if verbose:
+        print(" ".join(cmd))
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError(f"nvcc failed ({res.returncode}):\n{res.stdout}\n{res.stderr}")
+    os.replace(tmp, OUT)
+    return OUT
+
+
+if __name__ == "__main__":
+    print(build(force=True, verbose=True))

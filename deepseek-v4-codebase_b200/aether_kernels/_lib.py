@@ -1,0 +1,125 @@
+"""ctypes binding of the C-ABI library ``libaether_b200.so`` (sm_100a kernels).
+
+The shared library is built in-tree by ``aether_kernels._build.build()`` (or
+``__graft_entry__.build()``); there is no fallback of any kind: if the
+library is missing or was not built for this device, every op raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+from typing import Optional
+
+LIB_NAME = "libaether_b200.so"
+LIB_PATH = Path(__file__).resolve().parent / LIB_NAME
+
+_c_int = ctypes.c_int
+_c_ll = ctypes.c_longlong
+_c_f = ctypes.c_float
+_p = ctypes.c_void_p
+
+# name -> (restype, argtypes); mirrors include/aether_b200.h
+SIGNATURES = {
+    "aether_last_error": (ctypes.c_char_p, []),
+    "aether_abi_version": (_c_int, []),
+    "aether_compiled_arch": (_c_int, []),
+    "aether_tq_encode": (_c_int, [_p, _c_int, _c_ll, _c_int, _c_int, _p, _p, _p, _p, _p]),
+    "aether_tq_encode_into_pages": (
+        _c_int,
+        [_p, _c_int, _c_int, _c_int, _c_int, _c_int, _p, _p, _c_int, _p, _c_int, _p, _p, _p, _p],
+    ),
+    "aether_tq_decode": (_c_int, [_p, _p, _c_ll, _c_int, _c_int, _p, _p, _c_int, _p]),
+    "aether_wht": (_c_int, [_p, _p, _c_ll, _c_int, _p]),
+    "aether_sparse_sink_attention": (
+        _c_int,
+        [_p, _p, _p, _c_int, _p, _c_int, _p, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_f, _p],
+    ),
+    "aether_tiled_prefill_attention": (
+        _c_int,
+        [_p, _p, _p, _c_int, _p, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_f, _c_int, _p],
+    ),
+    "aether_csa_indexer_topk_scratch_bytes": (ctypes.c_size_t, [_c_int, _c_int]),
+    "aether_csa_indexer_topk": (
+        _c_int,
+        [_p, _p, _p, _c_int, _c_int, _c_int, _c_int, _c_int, _p, _p, _p],
+    ),
+    "aether_hca_compress": (_c_int, [_p, _p, _p, _c_int, _c_int, _c_int, _c_int, _p]),
+    "aether_csa_decode_paged": (
+        _c_int,
+        [
+            _p, _p, _p, _p, _p, _p,            # q, index_q, index_w, sink, window, window_len
+            _p, _p, _p, _p,                    # idx_codes, idx_scale, kv_codes, kv_scale
+            _p, _c_int, _c_int, _p, _c_int,    # page_table, stride, num_pages, nblocks, max_nblocks
+            _p, _p,                            # diag_idx, diag_kv
+            _c_int, _c_int, _c_int, _c_int, _c_int, _c_f,  # B, H, W, bits, top_k, scale
+            _p, _p, _p, _c_int, _p,            # out, sel_out, err, cluster, stream
+        ],
+    ),
+    "aether_csa_decode_paged_scores": (
+        _c_int,
+        [
+            _p, _p, _p, _p, _p, _p,
+            _p, _p, _p, _p,
+            _p, _c_int, _c_int, _p, _c_int,
+            _p, _p,
+            _c_int, _c_int, _c_int, _c_int, _c_int, _c_f,
+            _p, _p, _p, _c_int, _p, _c_int, _p,  # out, sel_out, score_out, stride, err, cluster, stream
+        ],
+    ),
+    "aether_hca_decode_paged": (
+        _c_int,
+        [
+            _p, _p, _p, _p,                    # q, sink, window, window_len
+            _p, _p,                            # kv_codes, kv_scale
+            _p, _c_int, _c_int, _p, _c_int,    # page_table, stride, num_pages, nblocks, max_nblocks
+            _p,                                # diag_kv
+            _c_int, _c_int, _c_int, _c_int, _c_f,  # B, H, W, bits, scale
+            _p, _p, _c_int, _p,                # out, err, cluster, stream
+        ],
+    ),
+}
+
+_lock = threading.Lock()
+_lib: Optional[ctypes.CDLL] = None
+
+
+class AetherKernelError(RuntimeError):
+    pass
+
+
+def library_path() -> Path:
+    return LIB_PATH
+
+
+def load() -> ctypes.CDLL:
+    """Load (once) and return the C-ABI library; raise if it is not built."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not LIB_PATH.exists():
+                raise AetherKernelError(
+                    f"Aether CUDA kernels are unavailable: {LIB_PATH} is not built "
+                    "(run aether_kernels._build.build() or __graft_entry__.build())."
+                )
+            lib = ctypes.CDLL(str(LIB_PATH))
+            for name, (res, args) in SIGNATURES.items():
+                fn = getattr(lib, name)
+                fn.restype = res
+                fn.argtypes = args
+            _lib = lib
+    return _lib
+
+
+def last_error() -> str:
+    msg = load().aether_last_error()
+    return msg.decode() if msg else ""
+
+
+def call(name: str, *args) -> None:
+    """Invoke a C entry point; translate a non-zero status into RuntimeError."""
+    rc = getattr(load(), name)(*args)
+    if rc != 0:
+        raise AetherKernelError(f"{name} failed ({rc}): {last_error()}")

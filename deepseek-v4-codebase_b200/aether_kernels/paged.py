@@ -1,0 +1,191 @@
+"""Paged TurboQuant KV cache and the fused decode entry points.
+
+Cache layout in HBM (one ``TurboQuantPagedCache`` per attention layer):
+
+    idx_codes [P, 64, 64*bits/8]  uint8   CSA indexer keys (rotated codes)
+    idx_scale [P, 64]             fp32    per-entry scale
+    kv_codes  [P, 64, 128*bits/8] uint8   shared K=V compressed entries
+    kv_scale  [P, 64]             fp32
+
+Entry ``i`` of a sequence lives in physical page ``page_table[seq, i // 64]``
+at slot ``i % 64``; the indexer and main streams share page ids.  Codes are
+PolarQuant codes (aether_2b/turbo_quant.py:127-166): int8 for 8-bit, packed
+signed nibbles (even element in the low nibble) for 4-bit.
+
+This replaces the reference's LRU pool of de-quantized 128-token pages that
+are gathered with ``torch.cat`` (aether_kernels/paged_kv_allocator.py:46-252,
+aether_2b/serving.py:378-410, 486-493): pages stay quantized and the kernels
+read them in place through the page table.
+"""
+from __future__ import annotations
+
+from typing import List, Optional, Sequence, Tuple
+
+import torch
+
+from . import _lib
+from .ops import _check, _cuda, _stream, rademacher_diag, tq_encode_into_pages
+
+PAGE = 64
+HEAD_DIM = 128
+INDEX_DIM = 64
+INDEX_HEADS = 4
+
+
+class TurboQuantPagedCache:
+    """Device page pool for one CSA or HCA layer (free-list page allocator)."""
+
+    def __init__(self, num_pages: int, bits: int, device, with_index: bool = True, seed: int = 42):
+        if bits not in (4, 8):
+            raise ValueError(f"bits must be 4 or 8, got {bits}")
+        self.bits = bits
+        self.seed = seed
+        self.num_pages = int(num_pages)
+        self.device = torch.device(device)
+        dev = self.device
+        self.kv_codes = torch.zeros(num_pages, PAGE, HEAD_DIM * bits // 8, dtype=torch.uint8, device=dev)
+        self.kv_scale = torch.zeros(num_pages, PAGE, dtype=torch.float32, device=dev)
+        if with_index:
+            self.idx_codes = torch.zeros(num_pages, PAGE, INDEX_DIM * bits // 8, dtype=torch.uint8, device=dev)
+            self.idx_scale = torch.zeros(num_pages, PAGE, dtype=torch.float32, device=dev)
+        else:
+            self.idx_codes = None
+            self.idx_scale = None
+        self._free: List[int] = list(range(num_pages - 1, -1, -1))
+
+    # ---------------------------------------------------------- page mgmt
+    @property
+    def free_pages(self) -> int:
+        return len(self._free)
+
+    def alloc_pages(self, n: int, generator: Optional[torch.Generator] = None) -> List[int]:
+        if n > len(self._free):
+            raise MemoryError(f"TurboQuant page pool exhausted: need {n}, {len(self._free)} free")
+        if generator is not None:
+            perm = torch.randperm(len(self._free), generator=generator)[:n].tolist()
+            picked = [self._free[i] for i in perm]
+            chosen = set(picked)
+            self._free = [p for p in self._free if p not in chosen]
+            return picked
+        return [self._free.pop() for _ in range(n)]
+
+    def release_pages(self, pages: Sequence[int]) -> None:
+        self._free.extend(int(p) for p in pages)
+
+    # --------------------------------------------------------------- write
+    def write(self, page_table: torch.Tensor, start_pos: torch.Tensor, kv: torch.Tensor,
+              index: Optional[torch.Tensor] = None, err: Optional[torch.Tensor] = None) -> None:
+        """Quantize ``kv`` [B, n, 128] (and ``index`` [B, n, 64]) and store
+        them at logical positions start_pos[b] .. start_pos[b]+n-1."""
+        tq_encode_into_pages(kv, self.bits, page_table, start_pos, self.kv_codes, self.kv_scale, self.seed, err)
+        if index is not None:
+            _check(self.idx_codes is not None, "this cache has no indexer stream")
+            tq_encode_into_pages(index, self.bits, page_table, start_pos, self.idx_codes, self.idx_scale,
+                                 self.seed, err)
+
+
+def _opt_ptr(t: Optional[torch.Tensor]):
+    return None if t is None else t.data_ptr()
+
+
+def csa_decode_paged(
+    q: torch.Tensor,
+    index_q: torch.Tensor,
+    index_weight: torch.Tensor,
+    sink: torch.Tensor,
+    window: torch.Tensor,
+    window_len: torch.Tensor,
+    cache: TurboQuantPagedCache,
+    page_table: torch.Tensor,
+    nblocks: torch.Tensor,
+    softmax_scale: float,
+    top_k: int = 256,
+    out: Optional[torch.Tensor] = None,
+    indices: Optional[torch.Tensor] = None,
+    err: Optional[torch.Tensor] = None,
+    cluster: int = 0,
+    scores: Optional[torch.Tensor] = None,
+) -> Tuple[torch.Tensor, torch.Tensor]:
+    """One fused CSA decode step for a batch of sequences.
+
+    q [B, H, 128] bf16 (post-RoPE, post-norm), index_q [B, 4, 64] fp32,
+    index_weight [B, 4] fp32 raw head weights (softplus applied in-kernel),
+    sink [H] fp32, window [B, W, 128] bf16 (oldest first, ``window_len[b]``
+    valid rows), page_table [B, max_pages] int32, nblocks [B] int32 visible
+    compressed blocks.  Returns ``(out [B, H, 128] bf16, indices [B, top_k]
+    int32)``: the attention output before the inverse output RoPE (what
+    ``AttentionKernelBackend.sparse_attention`` returns) and the selected
+    block indices in ascending order, -1 padded.
+    """
+    B, H, D = q.shape
+    _check(D == HEAD_DIM, f"head_dim must be {HEAD_DIM}")
+    for t, nm in ((q, "q"), (index_q, "index_q"), (index_weight, "index_weight"), (sink, "sink"),
+                  (window, "window"), (window_len, "window_len"), (page_table, "page_table"),
+                  (nblocks, "nblocks")):
+        _cuda(t, nm)
+    _check(q.dtype == torch.bfloat16 and window.dtype == torch.bfloat16, "q and window must be bfloat16")
+    _check(index_q.dtype == torch.float32 and index_weight.dtype == torch.float32 and sink.dtype == torch.float32,
+           "index_q, index_weight and sink must be float32")
+    _check(tuple(index_q.shape) == (B, INDEX_HEADS, INDEX_DIM), "index_q must have shape [B, 4, 64]")
+    _check(page_table.dtype == torch.int32 and nblocks.dtype == torch.int32 and window_len.dtype == torch.int32,
+           "page_table, nblocks and window_len must be int32")
+    _check(cache.idx_codes is not None, "CSA decode needs a cache with an indexer stream")
+    dev = q.device
+    if out is None:
+        out = torch.empty(B, H, D, dtype=torch.bfloat16, device=dev)
+    if indices is None:
+        indices = torch.empty(B, top_k, dtype=torch.int32, device=dev)
+    common = (
+        q.data_ptr(), index_q.data_ptr(), index_weight.data_ptr(), sink.data_ptr(), window.data_ptr(),
+        window_len.data_ptr(), cache.idx_codes.data_ptr(), cache.idx_scale.data_ptr(), cache.kv_codes.data_ptr(),
+        cache.kv_scale.data_ptr(), page_table.data_ptr(), page_table.shape[1], cache.num_pages,
+        nblocks.data_ptr(), page_table.shape[1] * PAGE,
+        rademacher_diag(INDEX_DIM, cache.seed, dev).data_ptr(), rademacher_diag(HEAD_DIM, cache.seed, dev).data_ptr(),
+        B, H, window.shape[1], cache.bits, int(top_k), float(softmax_scale),
+        out.data_ptr(), indices.data_ptr(),
+    )
+    if scores is None:
+        _lib.call("aether_csa_decode_paged", *common, _opt_ptr(err), int(cluster), _stream(dev))
+    else:
+        _cuda(scores, "scores")
+        _check(scores.dtype == torch.float32 and scores.shape[0] == B and scores.shape[1] >= page_table.shape[1] * PAGE,
+               "scores must be float32 [B, >= max_pages * 64]")
+        _lib.call("aether_csa_decode_paged_scores", *common, scores.data_ptr(), scores.shape[1], _opt_ptr(err),
+                  int(cluster), _stream(dev))
+    return out, indices
+
+
+def hca_decode_paged(
+    q: torch.Tensor,
+    sink: torch.Tensor,
+    window: torch.Tensor,
+    window_len: torch.Tensor,
+    cache: TurboQuantPagedCache,
+    page_table: torch.Tensor,
+    nblocks: torch.Tensor,
+    softmax_scale: float,
+    out: Optional[torch.Tensor] = None,
+    err: Optional[torch.Tensor] = None,
+    cluster: int = 0,
+) -> torch.Tensor:
+    """One fused HCA decode step: attention over every visible compressed
+    block plus the sliding window (aether_2b/serving.py:507-522)."""
+    B, H, D = q.shape
+    _check(D == HEAD_DIM, f"head_dim must be {HEAD_DIM}")
+    for t, nm in ((q, "q"), (sink, "sink"), (window, "window"), (window_len, "window_len"),
+                  (page_table, "page_table"), (nblocks, "nblocks")):
+        _cuda(t, nm)
+    _check(q.dtype == torch.bfloat16 and window.dtype == torch.bfloat16, "q and window must be bfloat16")
+    _check(sink.dtype == torch.float32, "sink must be float32")
+    dev = q.device
+    if out is None:
+        out = torch.empty(B, H, D, dtype=torch.bfloat16, device=dev)
+    _lib.call(
+        "aether_hca_decode_paged",
+        q.data_ptr(), sink.data_ptr(), window.data_ptr(), window_len.data_ptr(), cache.kv_codes.data_ptr(),
+        cache.kv_scale.data_ptr(), page_table.data_ptr(), page_table.shape[1], cache.num_pages, nblocks.data_ptr(),
+        page_table.shape[1] * PAGE, rademacher_diag(HEAD_DIM, cache.seed, dev).data_ptr(),
+        B, H, window.shape[1], cache.bits, float(softmax_scale), out.data_ptr(), _opt_ptr(err), int(cluster),
+        _stream(dev),
+    )
+    return out

@@ -1,0 +1,37 @@
+// Library-level C-ABI entry points: version, last error message, build info.
+#include <string.h>
+
+#include "capi_util.cuh"
+
+namespace aether {
+
+static thread_local char g_last_error[1024] = "";
+
+void set_last_error(const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+}
+
+int check_launch(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_last_error("%s: launch failed: %s", what, cudaGetErrorString(e));
+    return 2;
+  }
+  return 0;
+}
+
+}  // namespace aether
+
+extern "C" {
+
+const char* aether_last_error(void) { return aether::g_last_error; }
+
+int aether_abi_version(void) { return 1; }
+
+// Compute capability the kernels were compiled for (major*10+minor).
+int aether_compiled_arch(void) { return 100; }
+
+}

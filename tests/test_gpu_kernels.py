@@ -1,0 +1,274 @@
+"""GPU parity of the sm_100a kernels against the CPU oracle (bit-exact codes,
+exact top-k indices, attention within the bf16 tolerance)."""
+import pytest
+import torch
+
+from oracle import attention as oatt
+from oracle import decode as odec
+from oracle import turboquant as otq
+
+pytestmark = pytest.mark.gpu
+
+# attention tolerance of the decode path: bf16 output vs the fp32 oracle
+MAX_ABS = 2e-2
+MEAN_ABS = 1e-3
+
+
+@pytest.fixture(scope="module")
+def ak(cuda_device):
+    import aether_kernels
+    from aether_kernels import _lib
+
+    _lib.load()
+    return aether_kernels
+
+
+# ------------------------------------------------------------- TurboQuant
+@pytest.mark.parametrize("bits", [8, 4])
+@pytest.mark.parametrize("d", [128, 64])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32, torch.float16])
+def test_tq_encode_bit_exact(ak, bits, d, dtype):
+    from aether_kernels.turbo_quant import PolarQuant
+
+    g = torch.Generator().manual_seed(bits * 1000 + d)
+    x = (torch.randn(7, 333, d, generator=g) * 3).to(dtype)
+    x[0, 0] = 0  # all-zero vector: absmax clamps to 1e-8
+    x[0, 1] = torch.linspace(-1, 1, d).to(dtype)
+    codes, scale = PolarQuant(bits).encode(x.cuda())
+    rc, rs = otq.encode(x, bits)
+    assert codes.dtype == rc.dtype and codes.shape == rc.shape
+    assert torch.equal(codes.cpu(), rc)
+    assert torch.equal(scale.cpu(), rs)
+
+
+@pytest.mark.parametrize("bits", [8, 4])
+@pytest.mark.parametrize("d", [128, 64])
+def test_tq_decode_matches(ak, bits, d):
+    from aether_kernels.turbo_quant import PolarQuant, _wht
+
+    g = torch.Generator().manual_seed(5 + bits + d)
+    x = torch.randn(4, 100, d, generator=g)
+    rc, rs = otq.encode(x, bits)
+    pq = PolarQuant(bits)
+    got = pq.decode(rc.cuda(), rs.cuda(), out_dtype=torch.float32).cpu()
+    ref = otq.decode(rc, rs, bits)
+    assert torch.equal(got, ref)
+    got_bf = pq.decode(rc.cuda(), rs.cuda()).cpu()
+    assert torch.equal(got_bf, ref.to(torch.bfloat16))
+    assert torch.equal(_wht(x.cuda()).cpu(), otq.wht(x))
+
+
+# ------------------------------------------------ reference extension ops
+@pytest.mark.parametrize("dtype,index_dtype", [(torch.float32, torch.int64), (torch.float16, torch.int32),
+                                               (torch.bfloat16, torch.int64)])
+def test_sparse_sink_attention_reference_case(ak, dtype, index_dtype):
+    """The reference's own kernel test (tests/test_cuda_runtime.py:19-47)."""
+    ext = ak.load_aether_cuda_kernels()
+    torch.manual_seed(0)
+    q = torch.randn(2, 5, 4, 16, device="cuda", dtype=dtype)
+    kv = torch.randn(2, 23, 2, 16, device="cuda", dtype=dtype)
+    topk = torch.randint(0, 23, (2, 5, 7), device="cuda", dtype=index_dtype)
+    sink = torch.randn(4, device="cuda", dtype=dtype)
+    got = ext.sparse_sink_attention(q, kv, topk, sink, 0.125)
+    exp = oatt.sparse_attention(q.cpu(), kv.cpu(), topk.cpu(), sink.cpu(), 0.125).to(dtype)
+    tol = 5e-3 if dtype != torch.float32 else 1e-4
+    torch.testing.assert_close(got.float().cpu(), exp.float(), atol=tol, rtol=tol)
+
+
+def test_sparse_sink_attention_serving_shape(ak):
+    """Serving decode call: T=1, K=S full indices, D=128, bf16, scalar sink."""
+    torch.manual_seed(1)
+    B, S, H, D = 3, 300, 12, 128
+    q = torch.randn(B, 1, H, D, device="cuda", dtype=torch.bfloat16)
+    vals = torch.randn(B, S, D, device="cuda", dtype=torch.bfloat16)
+    kv = torch.stack([vals, vals], dim=2)
+    idx = torch.arange(S, device="cuda").view(1, 1, S).expand(B, 1, S).contiguous()
+    idx[0, 0, :5] = -1  # skipped
+    sink = torch.randn(1, device="cuda", dtype=torch.bfloat16)
+    got = ak.sparse_sink_attention(q, kv, idx, sink, D ** -0.5)
+    exp = oatt.sparse_attention(q.cpu(), kv.cpu(), idx.cpu(), sink.cpu(), D ** -0.5)
+    assert (got.float().cpu() - exp).abs().max() < MAX_ABS
+
+
+def test_tiled_prefill_attention(ak):
+    from aether_kernels.sparse_attention import tiled_prefill_attention
+
+    torch.manual_seed(2)
+    q = torch.randn(2, 9, 4, 64, device="cuda")
+    kv = torch.randn(2, 40, 2, 64, device="cuda")
+    sink = torch.randn(4, device="cuda")
+    got = tiled_prefill_attention(q, kv, sink, 0.125, tile_size=16)
+    idx = torch.arange(40).view(1, 1, 40).expand(2, 9, 40)
+    exp = oatt.sparse_attention(q.cpu(), kv.cpu(), idx, sink.cpu(), 0.125)
+    torch.testing.assert_close(got.cpu(), exp, atol=1e-4, rtol=1e-4)
+
+
+@pytest.mark.parametrize("S,k", [(23, 7), (1000, 256), (5000, 256), (300, 300)])
+def test_csa_indexer_topk(ak, S, k):
+    from aether_kernels.sparse_attention import csa_indexer_topk
+
+    g = torch.Generator().manual_seed(S)
+    iq = torch.randn(3, 4, 64, generator=g)
+    ikv = torch.randn(3, S, 64, generator=g)
+    iw = torch.randn(3, 4, generator=g)
+    got = csa_indexer_topk(iq.cuda(), ikv.cuda(), iw.cuda(), k).cpu()
+    exp, scores = oatt.dense_index_topk(iq, ikv, iw, k)
+    assert got.dtype == torch.int64 and got.shape == (3, k)
+    for b in range(3):
+        s = scores[b]
+        # same set and the same (score desc, index asc) order, except where the
+        # fp32 scores of two candidates are within rounding of each other
+        if not torch.equal(got[b], exp[b]):
+            assert torch.allclose(s[got[b]], s[exp[b]], rtol=1e-5, atol=1e-6)
+
+
+def test_csa_indexer_topk_ties_lowest_index(ak):
+    from aether_kernels.sparse_attention import csa_indexer_topk
+
+    iq = torch.ones(1, 4, 64)
+    ikv = torch.zeros(1, 50, 64)
+    ikv[0, ::2] = 1.0  # 25 equal positive scores, 25 zeros
+    iw = torch.zeros(1, 4)
+    got = csa_indexer_topk(iq.cuda(), ikv.cuda(), iw.cuda(), 30).cpu()[0]
+    assert got[:25].tolist() == list(range(0, 50, 2))
+    assert got[25:].tolist() == [1, 3, 5, 7, 9]
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_hca_compress(ak, dtype):
+    from aether_kernels.sparse_attention import hca_compress
+
+    torch.manual_seed(3)
+    c = torch.randn(4, 128, 128, device="cuda", dtype=dtype)
+    z = torch.randn(4, 128, 128, device="cuda", dtype=dtype)
+    got = hca_compress(c, z).float().cpu()
+    exp = oatt.hca_compress(c.cpu(), z.cpu())
+    tol = 1e-5 if dtype == torch.float32 else 1e-2
+    torch.testing.assert_close(got, exp, atol=tol, rtol=tol)
+
+
+# ------------------------------------------------ fused paged decode path
+def _run_decode(ak, batch, check_rows=None, cluster=0):
+    from aether_kernels.paged import csa_decode_paged, hca_decode_paged
+
+    c = batch.cache
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    if batch.kind == "csa":
+        out, sel = csa_decode_paged(batch.q, batch.index_q, batch.index_weight, batch.sink, batch.window,
+                                    batch.window_len, c, batch.page_table, batch.nblocks, batch.softmax_scale,
+                                    top_k=batch.top_k, err=err, cluster=cluster)
+    else:
+        out = hca_decode_paged(batch.q, batch.sink, batch.window, batch.window_len, c, batch.page_table,
+                               batch.nblocks, batch.softmax_scale, err=err, cluster=cluster)
+        sel = None
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    return out, sel
+
+
+def _oracle(batch, rows=None, use_selection=None):
+    c = batch.cache
+    rows = list(range(batch.q.shape[0])) if rows is None else rows
+    r = torch.tensor(rows)
+    return odec.decode_step(
+        batch.kind, batch.q.cpu()[r], None if batch.index_q is None else batch.index_q.cpu()[r],
+        None if batch.index_weight is None else batch.index_weight.cpu()[r], batch.sink.cpu(),
+        batch.window.cpu()[r], batch.window_len.cpu()[r], None if c.idx_codes is None else c.idx_codes.cpu(),
+        None if c.idx_scale is None else c.idx_scale.cpu(), c.kv_codes.cpu(), c.kv_scale.cpu(),
+        batch.page_table.cpu()[r], batch.nblocks.cpu()[r], batch.bits, batch.top_k, batch.softmax_scale,
+        use_selection=use_selection)
+
+
+def _check_decode(batch, out, sel, rows=None):
+    rows = list(range(batch.q.shape[0])) if rows is None else rows
+    ref = _oracle(batch, rows)
+    ties = 0
+    kern_sel = []
+    for i, b in enumerate(rows):
+        if sel is not None:
+            k = min(batch.top_k, int(batch.nblocks[b]))
+            got = sel[b].cpu()
+            assert (got[k:] == -1).all()
+            got = got[:k].long()
+            assert torch.equal(got, torch.sort(got).values), "indices must be ascending"
+            kern_sel.append(got)
+            if not torch.equal(got, ref.selected[i]):
+                assert ref.near_tie[i], f"row {b}: top-k differs outside the near-tie band"
+                ties += 1
+    if ties:
+        ref = _oracle(batch, rows, use_selection=kern_sel)
+    diff = (out.float().cpu()[torch.tensor(rows)] - ref.out).abs()
+    assert diff.max() < MAX_ABS, f"max abs {diff.max():.3e}"
+    assert diff.mean() < MEAN_ABS, f"mean abs {diff.mean():.3e}"
+    return ties
+
+
+@pytest.mark.parametrize("bits", [8, 4])
+@pytest.mark.parametrize("cluster", [4, 8])
+def test_csa_decode_small_ragged(ak, bits, cluster):
+    from aether_kernels.synthetic import make_decode_batch
+
+    batch = make_decode_batch("csa", 6, 40, 6000, bits, 4, seed=11 + bits, device="cuda")
+    out, sel = _run_decode(ak, batch, cluster=cluster)
+    _check_decode(batch, out, sel)
+
+
+def test_csa_decode_config0(ak):
+    """batch 4, 8192 tokens -> 2048 blocks, 8-bit."""
+    from aether_kernels.synthetic import make_decode_batch
+
+    batch = make_decode_batch("csa", 4, 8192, 8192, 8, 4, seed=0, device="cuda")
+    out, sel = _run_decode(ak, batch)
+    _check_decode(batch, out, sel)
+
+
+def test_csa_decode_config1_rows(ak):
+    """BASELINE config 1 shapes (4-bit, 16K-32K tokens), full batch of 64;
+    every 8th row is checked against the oracle."""
+    from aether_kernels.synthetic import make_decode_batch
+
+    batch = make_decode_batch("csa", 64, 16384, 32768, 4, 4, seed=1, device="cuda")
+    out, sel = _run_decode(ak, batch)
+    _check_decode(batch, out, sel, rows=list(range(0, 64, 8)))
+
+
+def test_csa_decode_short_and_empty(ak):
+    """nb = 0, nb < top_k, nb == top_k, partial windows."""
+    from aether_kernels.synthetic import make_decode_batch
+
+    batch = make_decode_batch("csa", 5, 0, 1100, 4, 4, seed=3, device="cuda")
+    toks = [0, 3, 50, 1024, 1100]
+    # rebuild with explicit lengths
+    batches = [make_decode_batch("csa", 1, t, t, 4, 4, seed=20 + i, device="cuda") for i, t in enumerate(toks)]
+    for bt in batches:
+        out, sel = _run_decode(ak, bt)
+        _check_decode(bt, out, sel)
+    del batch
+
+
+def test_csa_decode_exact_ties(ak):
+    """Identical index entries give bit-identical scores in the kernel and the
+    oracle; the kernel must take the lowest block indices among them."""
+    from aether_kernels.synthetic import make_decode_batch
+
+    batch = make_decode_batch("csa", 2, 4000, 4000, 8, 4, seed=4, device="cuda")
+    c = batch.cache
+    # every block of row 0 gets the same index entry -> all scores equal
+    for p in batch.page_table[0, : (1000 + 63) // 64].tolist():
+        c.idx_codes[p] = c.idx_codes[batch.page_table[0, 0]][0]
+        c.idx_scale[p] = c.idx_scale[batch.page_table[0, 0]][0]
+    out, sel = _run_decode(ak, batch)
+    assert sel[0, :256].cpu().tolist() == list(range(256))
+    _check_decode(batch, out, sel)
+
+
+@pytest.mark.parametrize("bits", [4, 8])
+def test_hca_decode(ak, bits):
+    """BASELINE config 2 shapes (HCA, 131072 tokens -> 1024 blocks, YaRN 4) at batch 6."""
+    from aether_kernels.rope import RopeConfig
+    from aether_kernels.synthetic import make_decode_batch
+
+    batch = make_decode_batch("hca", 6, 60000, 131072, bits, 128, seed=5, device="cuda",
+                              rope=RopeConfig.yarn(4.0))
+    out, _ = _run_decode(ak, batch)
+    _check_decode(batch, out, None)
