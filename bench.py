@@ -1,0 +1,415 @@
+#!/usr/bin/env python
+"""Benchmark of the CSA 4-bit-KV decode hot path.
+
+One *step* = one fused decode pass (indexer -> exact top-256 -> sparse sink
+attention over the selected compressed blocks + 128-token window) for a batch
+of 64 sequences whose contexts are drawn uniformly from 16K-32K tokens
+(4096-8192 compressed blocks), 12 heads x 128, 4-bit TurboQuant paged cache.
+A *query* is one sequence x one step x one layer.
+
+  value      queries/s over all ranks, inputs resident in HBM; steps replayed
+             from a CUDA graph; every step reads a different cache set, and
+             the sets together are > 4x L2 so every step reads cold HBM
+  e2e        queries/s through the public Python API (``csa_decode_paged``)
+             with the step's inputs copied from pinned host memory and the
+             outputs copied back inside the timed region
+  roofline   algorithmic bytes per launch / CUDA-event launch time, against
+             the measured HBM copy bandwidth (MEASURED_PEAKS.json)
+  cpu_baseline  the CPU restatement of the reference's fp32 torch path
+             (dequant, indexer, topk, gather, sparse attention) timed on the
+             host cores on a bounded sample of the same workload
+
+Multi-GPU: one process per GPU (torchrun); every rank runs its own batch of
+64 sequences (request partitioning, no collective on the data path);
+`value` = all ranks' queries / the slowest rank's time.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "deepseek-v4-codebase_b200"))
+
+METRIC = "CSA 4-bit-KV decode queries/s at 16K-32K ctx (batch 64/GPU)"
+UNIT = "queries/s"
+CFG = dict(batch=64, ctx_lo=16384, ctx_hi=32768, bits=4, compression=4, heads=12, window=128, top_k=256)
+FALLBACK_HBM_GBS = 6650.0
+NCU_SUMMARY = ROOT / "profiles" / "csa_decode_4bit_b64_ncu.md"
+
+
+def algorithmic_bytes(nblocks, window_len, bits, heads=12, top_k=256):
+    """Bytes one decode step must move: index pages (codes + scales), the
+    selected main entries, the bf16 window, q in / out, index query, head
+    weights, sink and the page-table entries."""
+    total = 0
+    for nb, wl in zip(nblocks, window_len):
+        k = min(top_k, nb)
+        total += nb * (64 * bits // 8 + 4)
+        total += k * (128 * bits // 8 + 4)
+        total += wl * 128 * 2
+        total += heads * 128 * 2 * 2
+        total += 4 * 64 * 4 + 4 * 4 + heads * 4
+        total += 4 * ((nb + 63) // 64)
+    return total
+
+
+def read_peak():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+        except Exception:
+            pass
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def read_traffic():
+    """Per-launch DRAM bytes of the decode kernel from the committed ncu
+    summary (line 'traffic_bytes_per_launch: N'), or None."""
+    if not NCU_SUMMARY.exists():
+        return None
+    for line in NCU_SUMMARY.read_text().splitlines():
+        if line.strip().startswith("traffic_bytes_per_launch:"):
+            try:
+                return int(line.split(":", 1)[1].strip())
+            except ValueError:
+                return None
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "50"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.thread.join(timeout=2)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) != 6:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx = float(parts[1])
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[2:]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        sm.sort()
+        return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def build_sets(nsets, device, rank):
+    from aether_kernels.paged import PAGE, TurboQuantPagedCache
+    from aether_kernels.synthetic import make_decode_batch
+
+    B, bits = CFG["batch"], CFG["bits"]
+    max_pages = CFG["ctx_hi"] // CFG["compression"] // PAGE
+    cache = TurboQuantPagedCache(nsets * B * max_pages, bits, device)
+    sets = []
+    for s in range(nsets):
+        sets.append(make_decode_batch("csa", B, CFG["ctx_lo"], CFG["ctx_hi"], bits, CFG["compression"],
+                                      heads=CFG["heads"], window=CFG["window"], top_k=CFG["top_k"],
+                                      seed=1000 * rank + s, device=device, cache=cache, gen_device=str(device)))
+    return cache, sets
+
+
+# ------------------------------------------------------------ CPU baseline
+def make_cpu_batch():
+    """The config-1 batch built with the CPU oracle encoder (no GPU needed)."""
+    from oracle import turboquant as otq
+    from aether_kernels.rope import RopeConfig, apply_rope, rope_attention_scale
+
+    g = torch.Generator().manual_seed(4242)
+    B, bits = CFG["batch"], CFG["bits"]
+    toks = (CFG["ctx_lo"] + torch.randint(0, CFG["ctx_hi"] - CFG["ctx_lo"] + 1, (B,), generator=g)).tolist()
+    nbs = [t // 4 for t in toks]
+    max_pages = max((n + 63) // 64 for n in nbs)
+    total_pages = sum((n + 63) // 64 for n in nbs)
+    perm = torch.randperm(total_pages, generator=g)
+    table = torch.zeros(B, max_pages, dtype=torch.int32)
+    pools = {
+        "idx_codes": torch.zeros(total_pages, 64, 64 * bits // 8, dtype=torch.uint8),
+        "idx_scale": torch.zeros(total_pages, 64),
+        "kv_codes": torch.zeros(total_pages, 64, 128 * bits // 8, dtype=torch.uint8),
+        "kv_scale": torch.zeros(total_pages, 64),
+    }
+    off = 0
+    rope = RopeConfig()
+    for b, n in enumerate(nbs):
+        npg = (n + 63) // 64
+        pages = perm[off: off + npg]
+        off += npg
+        table[b, :npg] = pages.to(torch.int32)
+        kv = torch.zeros(npg * 64, 128)
+        kv[:n] = apply_rope(torch.randn(n, 128, generator=g), torch.arange(n) * 4 + 3, rope)
+        ik = torch.zeros(npg * 64, 64)
+        ik[:n] = torch.randn(n, 64, generator=g)
+        c, s = otq.encode(kv.view(npg, 64, 128), bits)
+        pools["kv_codes"][pages], pools["kv_scale"][pages] = c, s.squeeze(-1)
+        c, s = otq.encode(ik.view(npg, 64, 64), bits)
+        pools["idx_codes"][pages], pools["idx_scale"][pages] = c, s.squeeze(-1)
+    return dict(pools=pools, q=torch.randn(B, CFG["heads"], 128, generator=g).to(torch.bfloat16),
+                index_q=torch.randn(B, 4, 64, generator=g), index_weight=torch.randn(B, 4, generator=g),
+                sink=torch.randn(CFG["heads"], generator=g),
+                window=torch.randn(B, CFG["window"], 128, generator=g).to(torch.bfloat16),
+                window_len=torch.full((B,), CFG["window"], dtype=torch.int32), page_table=table,
+                nblocks=torch.tensor(nbs, dtype=torch.int32),
+                softmax_scale=128 ** -0.5 * rope_attention_scale(rope))
+
+
+def cpu_decode(bt, rows):
+    from oracle import decode as odec
+
+    r = torch.tensor(rows)
+    p = bt["pools"]
+    return odec.decode_step("csa", bt["q"][r], bt["index_q"][r], bt["index_weight"][r], bt["sink"], bt["window"][r],
+                            bt["window_len"][r], p["idx_codes"], p["idx_scale"], p["kv_codes"], p["kv_scale"],
+                            bt["page_table"][r], bt["nblocks"][r], CFG["bits"], CFG["top_k"], bt["softmax_scale"],
+                            classify_ties=False)
+
+
+def cpu_baseline(steps: int, warmup: int, budget_s: float, full_line: bool = False):
+    sys.path.insert(0, str(ROOT))
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    bt = make_cpu_batch()
+    B, per_step = CFG["batch"], 4
+    for i in range(max(warmup, 0)):
+        cpu_decode(bt, [(i * per_step + j) % B for j in range(per_step)])
+    t0 = time.perf_counter()
+    n = 0
+    while n < max(steps, 1):
+        cpu_decode(bt, [(n * per_step + j) % B for j in range(per_step)])
+        n += 1
+        if time.perf_counter() - t0 > budget_s:
+            break
+    dt = time.perf_counter() - t0
+    done = n * per_step
+    qps = done / dt
+    base = {"value": round(qps, 2), "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"{done} queries ({n} steps x {per_step} sequences of the 64-sequence, 16K-32K-token, "
+                      "4-bit batch); fp32 torch CPU restatement of the reference path incl. per-step dequant"}
+    if not full_line:
+        return base
+    return {"metric": METRIC, "value": round(qps, 2), "unit": UNIT, "n_gpus": 0, "steps": n, "warmup": warmup,
+            "ms_per_step": round(dt / n * 1e3, 3), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic", "impl": "reference",
+            "config": {"workload": "csa_decode_4bit_b64_ctx16k-32k", **CFG},
+            "cpu_baseline": base,
+            "e2e": {"value": round(qps, 2), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+# ------------------------------------------------------------------- main
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=102400)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--sets", type=int, default=16)
+    ap.add_argument("--e2e-steps", type=int, default=200)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-pdl", dest="pdl", action="store_false",
+                    help="launch without programmatic dependent launch (no prefetch overlap across steps)")
+    ap.add_argument("--profile-launches", type=int, default=0,
+                    help="profiling mode: build the sets, run this many plain launches, print timings, exit")
+    args = ap.parse_args()
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        if rank == 0:
+            print(json.dumps(cpu_baseline(args.steps, args.warmup, budget_s=60.0, full_line=True)), flush=True)
+        return
+    assert args.warmup >= 3, "at least 3 warm-up steps"
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", device_id=dev)
+    from aether_kernels.paged import csa_decode_paged
+
+    cache, sets = build_sets(args.sets, dev, rank)
+    B = CFG["batch"]
+    outs = [torch.empty(B, CFG["heads"], 128, dtype=torch.bfloat16, device=dev) for _ in sets]
+    sels = [torch.empty(B, CFG["top_k"], dtype=torch.int32, device=dev) for _ in sets]
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+
+    def step(i, pdl=args.pdl):
+        s = sets[i % len(sets)]
+        csa_decode_paged(s.q, s.index_q, s.index_weight, s.sink, s.window, s.window_len, cache, s.page_table,
+                         s.nblocks, s.softmax_scale, top_k=s.top_k, out=outs[i % len(sets)],
+                         indices=sels[i % len(sets)], err=err, overlap_prefetch=pdl)
+
+    if args.profile_launches:
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(args.profile_launches + 1)]
+        for i in range(args.warmup):
+            step(i, False)
+        torch.cuda.synchronize()
+        for i in range(args.profile_launches):
+            evs[i].record()
+            step(i, False)
+        evs[-1].record()
+        torch.cuda.synchronize()
+        print("per-launch ms (plain launches):",
+              [round(evs[i].elapsed_time(evs[i + 1]), 4) for i in range(args.profile_launches)], flush=True)
+        assert int(err.item()) == 0
+        return
+
+    stream = torch.cuda.Stream(dev)
+    per_graph = 16 * len(sets)
+    with torch.cuda.stream(stream):
+        for i in range(args.warmup):
+            step(i)
+        stream.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for i in range(per_graph):
+                step(i)
+        g.replay()
+        stream.synchronize()
+    assert int(err.item()) == 0, f"kernel error flag {int(err.item())}"
+    replays = max(1, (args.steps + per_graph - 1) // per_graph)
+    steps = replays * per_graph
+
+    sampler = ClockSampler(local)
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize(dev)
+    sampler.start()
+    time.sleep(0.2)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        ev0.record(stream)
+        for _ in range(replays):
+            g.replay()
+        ev1.record(stream)
+    ev1.synchronize()
+    clocks = sampler.stop()
+    torch.cuda.synchronize(dev)
+    ms = ev0.elapsed_time(ev1)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
+        torch.distributed.barrier()
+    ms_step = ms / steps
+    value = world * B * steps / (ms / 1e3)
+
+    per_set = [algorithmic_bytes(s.nblocks.tolist(), s.window_len.tolist(), CFG["bits"]) for s in sets]
+    bytes_launch = sum(per_set) / len(per_set)
+    achieved = bytes_launch / (ms_step / 1e3) / 1e9
+    peak, peak_src = read_peak()
+
+    # ---- e2e through the public API with host buffers
+    s0 = sets[0]
+    host_in = {k: getattr(s0, k).cpu().pin_memory() for k in ("q", "index_q", "index_weight", "window_len",
+                                                               "nblocks")}
+    dev_in = {k: torch.empty_like(v, device=dev) for k, v in host_in.items()}
+    host_out = torch.empty(B, CFG["heads"], 128, dtype=torch.bfloat16).pin_memory()
+    host_sel = torch.empty(B, CFG["top_k"], dtype=torch.int32).pin_memory()
+    h2d = sum(v.numel() * v.element_size() for v in host_in.values())
+    d2h = host_out.numel() * 2 + host_sel.numel() * 4
+
+    def e2e_step():
+        for k, v in host_in.items():
+            dev_in[k].copy_(v, non_blocking=True)
+        o, sl = csa_decode_paged(dev_in["q"], dev_in["index_q"], dev_in["index_weight"], s0.sink, s0.window,
+                                 dev_in["window_len"], cache, s0.page_table, dev_in["nblocks"], s0.softmax_scale,
+                                 top_k=s0.top_k)
+        host_out.copy_(o, non_blocking=True)
+        host_sel.copy_(sl, non_blocking=True)
+
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            e2e_step()
+        stream.synchronize()
+        if world > 1:
+            torch.distributed.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.e2e_steps):
+            e2e_step()
+        e1.record(stream)
+    e1.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e_value = world * B * args.e2e_steps / (e2e_ms / 1e3)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(steps=1000, warmup=1, budget_s=15.0)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world, "steps": steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_step, 6), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "u8", "data": "synthetic",
+            "config": {"workload": "csa_decode_4bit_b64_ctx16k-32k", **CFG, "cache_sets": len(sets),
+                       "cache_bytes_cycled": int(sum(t.numel() * t.element_size() for t in cache.tensors())),
+                       "l2_policy": "inputs larger than L2: each step reads a different cache set, sets > 4x L2",
+                       "parallelism": f"request-sharded x{world}", "pdl": bool(args.pdl),
+                       "timing": "CUDA graph replay, CUDA events"},
+            "gpu_launches": steps,
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "peak_source": peak_src, "traffic": read_traffic(),
+                         "algorithmic_bytes_per_launch": int(bytes_launch)},
+            "e2e": {"value": round(e2e_value, 1), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "clocks": clocks,
+        }
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

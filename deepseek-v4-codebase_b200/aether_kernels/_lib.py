@@ -27,7 +27,7 @@ SIGNATURES = {
     "aether_tq_encode": (_c_int, [_p, _c_int, _c_ll, _c_int, _c_int, _p, _p, _p, _p, _p]),
     "aether_tq_encode_into_pages": (
         _c_int,
-        [_p, _c_int, _c_int, _c_int, _c_int, _c_int, _p, _p, _c_int, _p, _c_int, _p, _p, _p, _p],
+        [_p, _c_int, _c_int, _c_int, _c_int, _c_int, _p, _p, _c_int, _p, _c_int, _p, _p, _p],
     ),
     "aether_tq_decode": (_c_int, [_p, _p, _c_ll, _c_int, _c_int, _p, _p, _c_int, _p]),
     "aether_wht": (_c_int, [_p, _p, _c_ll, _c_int, _p]),
@@ -49,29 +49,30 @@ SIGNATURES = {
         _c_int,
         [
             _p, _p, _p, _p, _p, _p,            # q, index_q, index_w, sink, window, window_len
-            _p, _p, _p, _p,                    # idx_codes, idx_scale, kv_codes, kv_scale
+            _p, _p,                            # idx_pages, kv_pages
             _p, _c_int, _c_int, _p, _c_int,    # page_table, stride, num_pages, nblocks, max_nblocks
             _p, _p,                            # diag_idx, diag_kv
             _c_int, _c_int, _c_int, _c_int, _c_int, _c_f,  # B, H, W, bits, top_k, scale
-            _p, _p, _p, _c_int, _p,            # out, sel_out, err, cluster, stream
+            _p, _p, _p, _c_int, _c_int, _p,    # out, sel_out, err, cluster, pdl, stream
         ],
     ),
     "aether_csa_decode_paged_scores": (
         _c_int,
         [
             _p, _p, _p, _p, _p, _p,
-            _p, _p, _p, _p,
+            _p, _p,
             _p, _c_int, _c_int, _p, _c_int,
             _p, _p,
             _c_int, _c_int, _c_int, _c_int, _c_int, _c_f,
-            _p, _p, _p, _c_int, _p, _c_int, _p,  # out, sel_out, score_out, stride, err, cluster, stream
+            _p, _p, _p, _c_int, _p, _c_int, _c_int, _p,  # out, sel, score_out, stride, err, cluster, pdl, stream
         ],
     ),
+    "aether_csa_decode_smem_bytes": (_c_int, [_c_int]),
     "aether_hca_decode_paged": (
         _c_int,
         [
             _p, _p, _p, _p,                    # q, sink, window, window_len
-            _p, _p,                            # kv_codes, kv_scale
+            _p,                                # kv_pages
             _p, _c_int, _c_int, _p, _c_int,    # page_table, stride, num_pages, nblocks, max_nblocks
             _p,                                # diag_kv
             _c_int, _c_int, _c_int, _c_int, _c_f,  # B, H, W, bits, scale

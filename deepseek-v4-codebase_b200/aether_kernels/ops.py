@@ -70,23 +70,24 @@ def tq_encode(x: torch.Tensor, bits: int, seed: int = 42) -> Tuple[torch.Tensor,
 
 
 def tq_encode_into_pages(x: torch.Tensor, bits: int, page_table: torch.Tensor, start_pos: torch.Tensor,
-                         code_pool: torch.Tensor, scale_pool: torch.Tensor, seed: int = 42,
-                         err: Optional[torch.Tensor] = None) -> None:
+                         page_pool: torch.Tensor, seed: int = 42, err: Optional[torch.Tensor] = None) -> None:
     """Encode x [B, n, d] and write entry i of sequence b to logical position
-    start_pos[b] + i of that sequence's pages (page_table[b, pos // 64],
-    slot pos % 64) in the pools."""
+    start_pos[b] + i of that sequence's pages: page page_table[b, pos // 64],
+    slot pos % 64 of ``page_pool`` [P, 64 * row_bytes + 256] (64 code rows
+    followed by 64 fp32 scales per page)."""
     _cuda(x, "x")
     _check(x.dim() == 3, "x must have shape [B, n, D]")
     B, n, d = x.shape
-    for t, nm in ((page_table, "page_table"), (start_pos, "start_pos"), (code_pool, "code_pool"),
-                  (scale_pool, "scale_pool")):
+    for t, nm in ((page_table, "page_table"), (start_pos, "start_pos"), (page_pool, "page_pool")):
         _cuda(t, nm)
     _check(page_table.dtype == torch.int32 and start_pos.dtype == torch.int32, "page tables must be int32")
+    rb = d * bits // 8
+    _check(page_pool.dtype == torch.uint8 and page_pool.dim() == 2 and page_pool.shape[1] == 64 * rb + 256,
+           "page_pool must be uint8 [P, 64 * row_bytes + 256]")
     diag = rademacher_diag(d, seed, x.device)
     _lib.call("aether_tq_encode_into_pages", x.data_ptr(), _dt(x, "x"), B, n, d, bits, diag.data_ptr(),
-              page_table.data_ptr(), page_table.shape[1], start_pos.data_ptr(), code_pool.shape[0],
-              code_pool.data_ptr(), scale_pool.data_ptr(), None if err is None else err.data_ptr(),
-              _stream(x.device))
+              page_table.data_ptr(), page_table.shape[1], start_pos.data_ptr(), page_pool.shape[0],
+              page_pool.data_ptr(), None if err is None else err.data_ptr(), _stream(x.device))
 
 
 def tq_decode(codes: torch.Tensor, scale: torch.Tensor, bits: int, seed: int = 42,

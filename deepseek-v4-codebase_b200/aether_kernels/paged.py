@@ -2,10 +2,14 @@
 
 Cache layout in HBM (one ``TurboQuantPagedCache`` per attention layer):
 
-    idx_codes [P, 64, 64*bits/8]  uint8   CSA indexer keys (rotated codes)
-    idx_scale [P, 64]             fp32    per-entry scale
-    kv_codes  [P, 64, 128*bits/8] uint8   shared K=V compressed entries
-    kv_scale  [P, 64]             fp32
+    idx_pages [P, 64*R_i + 256] uint8   CSA indexer keys: 64 code rows of
+                                        R_i = 64*bits/8 bytes, then 64 fp32 scales
+    kv_pages  [P, 64*R_m + 256] uint8   shared K=V entries: 64 rows of
+                                        R_m = 128*bits/8 bytes, then 64 scales
+
+A page (codes and scales) is one contiguous block so one bulk (TMA) copy
+moves it; ``idx_codes`` / ``idx_scale`` / ``kv_codes`` / ``kv_scale`` are
+views into the pages.
 
 Entry ``i`` of a sequence lives in physical page ``page_table[seq, i // 64]``
 at slot ``i % 64``; the indexer and main streams share page ids.  Codes are
@@ -42,16 +46,40 @@ class TurboQuantPagedCache:
         self.seed = seed
         self.num_pages = int(num_pages)
         self.device = torch.device(device)
-        dev = self.device
-        self.kv_codes = torch.zeros(num_pages, PAGE, HEAD_DIM * bits // 8, dtype=torch.uint8, device=dev)
-        self.kv_scale = torch.zeros(num_pages, PAGE, dtype=torch.float32, device=dev)
-        if with_index:
-            self.idx_codes = torch.zeros(num_pages, PAGE, INDEX_DIM * bits // 8, dtype=torch.uint8, device=dev)
-            self.idx_scale = torch.zeros(num_pages, PAGE, dtype=torch.float32, device=dev)
-        else:
-            self.idx_codes = None
-            self.idx_scale = None
+        self.kv_row = HEAD_DIM * bits // 8
+        self.idx_row = INDEX_DIM * bits // 8
+        self.kv_pages = torch.zeros(num_pages, PAGE * self.kv_row + PAGE * 4, dtype=torch.uint8, device=self.device)
+        self.idx_pages = (torch.zeros(num_pages, PAGE * self.idx_row + PAGE * 4, dtype=torch.uint8,
+                                      device=self.device) if with_index else None)
         self._free: List[int] = list(range(num_pages - 1, -1, -1))
+
+    # ------------------------------------------------------------- views
+    @staticmethod
+    def _codes(pages, row):
+        return None if pages is None else pages[:, : PAGE * row].view(pages.shape[0], PAGE, row)
+
+    @staticmethod
+    def _scales(pages, row):
+        return None if pages is None else pages[:, PAGE * row:].view(torch.float32)
+
+    @property
+    def kv_codes(self):
+        return self._codes(self.kv_pages, self.kv_row)
+
+    @property
+    def kv_scale(self):
+        return self._scales(self.kv_pages, self.kv_row)
+
+    @property
+    def idx_codes(self):
+        return self._codes(self.idx_pages, self.idx_row)
+
+    @property
+    def idx_scale(self):
+        return self._scales(self.idx_pages, self.idx_row)
+
+    def tensors(self):
+        return [t for t in (self.idx_pages, self.kv_pages) if t is not None]
 
     # ---------------------------------------------------------- page mgmt
     @property
@@ -77,11 +105,10 @@ class TurboQuantPagedCache:
               index: Optional[torch.Tensor] = None, err: Optional[torch.Tensor] = None) -> None:
         """Quantize ``kv`` [B, n, 128] (and ``index`` [B, n, 64]) and store
         them at logical positions start_pos[b] .. start_pos[b]+n-1."""
-        tq_encode_into_pages(kv, self.bits, page_table, start_pos, self.kv_codes, self.kv_scale, self.seed, err)
+        tq_encode_into_pages(kv, self.bits, page_table, start_pos, self.kv_pages, self.seed, err)
         if index is not None:
-            _check(self.idx_codes is not None, "this cache has no indexer stream")
-            tq_encode_into_pages(index, self.bits, page_table, start_pos, self.idx_codes, self.idx_scale,
-                                 self.seed, err)
+            _check(self.idx_pages is not None, "this cache has no indexer stream")
+            tq_encode_into_pages(index, self.bits, page_table, start_pos, self.idx_pages, self.seed, err)
 
 
 def _opt_ptr(t: Optional[torch.Tensor]):
@@ -105,6 +132,7 @@ def csa_decode_paged(
     err: Optional[torch.Tensor] = None,
     cluster: int = 0,
     scores: Optional[torch.Tensor] = None,
+    overlap_prefetch: bool = False,
 ) -> Tuple[torch.Tensor, torch.Tensor]:
     """One fused CSA decode step for a batch of sequences.
 
@@ -116,6 +144,15 @@ def csa_decode_paged(
     int32)``: the attention output before the inverse output RoPE (what
     ``AttentionKernelBackend.sparse_attention`` returns) and the selected
     block indices in ascending order, -1 padded.
+
+    ``cluster`` 0 (default) runs one CTA per sequence; 4 or 8 spread each
+    sequence over a thread-block cluster.  ``overlap_prefetch=True`` launches
+    with programmatic dependent launch: the kernel may start while the
+    previous kernel on the stream is still running and, before waiting for
+    it, reads ``page_table``, ``nblocks``, ``window_len``, the cache pages and
+    every window row except the newest.  Use it only when the immediately
+    preceding kernel writes none of those.  ``scores`` (optional fp32
+    [B, >= max_pages * 64]) receives every visible block's index score.
     """
     B, H, D = q.shape
     _check(D == HEAD_DIM, f"head_dim must be {HEAD_DIM}")
@@ -129,7 +166,7 @@ def csa_decode_paged(
     _check(tuple(index_q.shape) == (B, INDEX_HEADS, INDEX_DIM), "index_q must have shape [B, 4, 64]")
     _check(page_table.dtype == torch.int32 and nblocks.dtype == torch.int32 and window_len.dtype == torch.int32,
            "page_table, nblocks and window_len must be int32")
-    _check(cache.idx_codes is not None, "CSA decode needs a cache with an indexer stream")
+    _check(cache.idx_pages is not None, "CSA decode needs a cache with an indexer stream")
     dev = q.device
     if out is None:
         out = torch.empty(B, H, D, dtype=torch.bfloat16, device=dev)
@@ -137,21 +174,21 @@ def csa_decode_paged(
         indices = torch.empty(B, top_k, dtype=torch.int32, device=dev)
     common = (
         q.data_ptr(), index_q.data_ptr(), index_weight.data_ptr(), sink.data_ptr(), window.data_ptr(),
-        window_len.data_ptr(), cache.idx_codes.data_ptr(), cache.idx_scale.data_ptr(), cache.kv_codes.data_ptr(),
-        cache.kv_scale.data_ptr(), page_table.data_ptr(), page_table.shape[1], cache.num_pages,
+        window_len.data_ptr(), cache.idx_pages.data_ptr(), cache.kv_pages.data_ptr(), page_table.data_ptr(), page_table.shape[1], cache.num_pages,
         nblocks.data_ptr(), page_table.shape[1] * PAGE,
         rademacher_diag(INDEX_DIM, cache.seed, dev).data_ptr(), rademacher_diag(HEAD_DIM, cache.seed, dev).data_ptr(),
         B, H, window.shape[1], cache.bits, int(top_k), float(softmax_scale),
         out.data_ptr(), indices.data_ptr(),
     )
     if scores is None:
-        _lib.call("aether_csa_decode_paged", *common, _opt_ptr(err), int(cluster), _stream(dev))
+        _lib.call("aether_csa_decode_paged", *common, _opt_ptr(err), int(cluster), int(overlap_prefetch),
+                  _stream(dev))
     else:
         _cuda(scores, "scores")
         _check(scores.dtype == torch.float32 and scores.shape[0] == B and scores.shape[1] >= page_table.shape[1] * PAGE,
                "scores must be float32 [B, >= max_pages * 64]")
         _lib.call("aether_csa_decode_paged_scores", *common, scores.data_ptr(), scores.shape[1], _opt_ptr(err),
-                  int(cluster), _stream(dev))
+                  int(cluster), int(overlap_prefetch), _stream(dev))
     return out, indices
 
 
@@ -182,8 +219,8 @@ def hca_decode_paged(
         out = torch.empty(B, H, D, dtype=torch.bfloat16, device=dev)
     _lib.call(
         "aether_hca_decode_paged",
-        q.data_ptr(), sink.data_ptr(), window.data_ptr(), window_len.data_ptr(), cache.kv_codes.data_ptr(),
-        cache.kv_scale.data_ptr(), page_table.data_ptr(), page_table.shape[1], cache.num_pages, nblocks.data_ptr(),
+        q.data_ptr(), sink.data_ptr(), window.data_ptr(), window_len.data_ptr(), cache.kv_pages.data_ptr(),
+        page_table.data_ptr(), page_table.shape[1], cache.num_pages, nblocks.data_ptr(),
         page_table.shape[1] * PAGE, rademacher_diag(HEAD_DIM, cache.seed, dev).data_ptr(),
         B, H, window.shape[1], cache.bits, float(softmax_scale), out.data_ptr(), _opt_ptr(err), int(cluster),
         _stream(dev),

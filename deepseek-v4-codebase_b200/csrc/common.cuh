@@ -17,6 +17,10 @@ constexpr int kIdxHeads = 4;    // indexer heads on the decode path
 constexpr int kPage = 64;       // compressed entries per cache page
 constexpr int kMaxHeads = 16;   // query heads are padded to one 16-row MMA tile
 
+// Cache page layout: one page holds 64 entries as [64 x code row][64 x fp32
+// scale], so a page (codes and scales) moves with a single bulk copy.
+__host__ __device__ constexpr int page_bytes(int row_bytes) { return kPage * row_bytes + kPage * 4; }
+
 // Error bits written by kernels into the caller's status word.
 enum : int {
   kErrWaitTimeout = 1,   // an mbarrier / copy wait ran past its bound

@@ -70,8 +70,9 @@ struct CsaCfg {
   static constexpr int PST = COLS + 8;                     // P row stride (halves)
 
   // ---- shared memory layout (bytes) ----
-  static constexpr int STAGE_CODES = CH * kPage * RB_IDX;
-  static constexpr int STAGE_BYTES = STAGE_CODES + CH * kPage * 4;
+  static constexpr int PB_IDX = page_bytes(RB_IDX);   // one index page: codes + scales
+  static constexpr int PB_KV = page_bytes(RB_KV);
+  static constexpr int STAGE_BYTES = CH * PB_IDX;
   static constexpr int RING = HCA ? 0 : STAGES * STAGE_BYTES;
   // attention-phase buffers alias the ring (it is dead once scoring ends)
   static constexpr int A_KC = 0;                                   // fp16 [SELM][kRowH]
@@ -105,10 +106,8 @@ struct CsaParams {
   const float* sink;            // [H]
   const __nv_bfloat16* window;  // [B, W, 128]
   const int32_t* window_len;    // [B]
-  const uint8_t* idx_codes;     // [P, 64, 64*bits/8]
-  const float* idx_scale;       // [P, 64]
-  const uint8_t* kv_codes;      // [P, 64, 128*bits/8]
-  const float* kv_scale;        // [P, 64]
+  const uint8_t* idx_pages;     // [P][64 x 64*bits/8 codes | 64 x fp32 scales]
+  const uint8_t* kv_pages;      // [P][64 x 128*bits/8 codes | 64 x fp32 scales]
   const int32_t* page_table;    // [B, table_stride]
   const int32_t* nblocks;       // [B] visible compressed blocks
   const float* diag_idx;        // [64]  +-1
@@ -205,22 +204,14 @@ __global__ void __launch_bounds__(kThreads) csa_decode_kernel(CsaParams p) {
     const int stage = c % C::STAGES;
     uint8_t* dst = smem + stage * C::STAGE_BYTES;
     const int np = min(C::CH, pg1 - pg0 - c * C::CH);
-    uint32_t bytes = 0;
-    for (int i = 0; i < np; ++i) {
-      int phys = ptab[pg0 + c * C::CH + i];
-      if (phys >= 0 && phys < p.num_pages) bytes += kPage * C::RB_IDX + kPage * 4;
-    }
-    mbar_expect_tx(&bars[stage], bytes);
+    mbar_expect_tx(&bars[stage], np * C::PB_IDX);
     for (int i = 0; i < np; ++i) {
       int phys = ptab[pg0 + c * C::CH + i];
       if (phys < 0 || phys >= p.num_pages) {
         report_error(p.err, kErrBadPage);
-        continue;
+        phys = 0;
       }
-      bulk_g2s(dst + i * kPage * C::RB_IDX, p.idx_codes + static_cast<long long>(phys) * kPage * C::RB_IDX,
-               kPage * C::RB_IDX, &bars[stage]);
-      bulk_g2s(dst + C::STAGE_CODES + i * kPage * 4, p.idx_scale + static_cast<long long>(phys) * kPage, kPage * 4,
-               &bars[stage]);
+      bulk_g2s(dst + i * C::PB_IDX, p.idx_pages + static_cast<long long>(phys) * C::PB_IDX, C::PB_IDX, &bars[stage]);
     }
   };
 
@@ -308,16 +299,18 @@ __global__ void __launch_bounds__(kThreads) csa_decode_kernel(CsaParams p) {
     for (int c = 0; c < nchunks; ++c) {
       const int stage = c % C::STAGES;
       mbar_wait(&bars[stage], (c / C::STAGES) & 1, p.err);
-      const uint8_t* codes = smem + stage * C::STAGE_BYTES;
-      const float* ksc = reinterpret_cast<const float*>(codes + C::STAGE_CODES);
+      const uint8_t* stg = smem + stage * C::STAGE_BYTES;
       const int np = min(C::CH, pg1 - pg0 - c * C::CH);
       const int tiles = np * (kPage / 16);
       for (int tile = warp; tile < tiles; tile += kWarps) {
         const int rowA = tile * 16 + g, rowB = rowA + 8;  // rows within the stage
+        const uint8_t* codes = stg + (tile >> 2) * C::PB_IDX;  // the tile's page
+        const float* ksc = reinterpret_cast<const float*>(codes + kPage * C::RB_IDX);
+        const int ra = rowA & 63, rbb = rowB & 63;
         uint32_t a[2][4];
         if (BITS == 4) {
-          const uint2 va = *reinterpret_cast<const uint2*>(codes + rowA * C::RB_IDX + t * 8);
-          const uint2 vb = *reinterpret_cast<const uint2*>(codes + rowB * C::RB_IDX + t * 8);
+          const uint2 va = *reinterpret_cast<const uint2*>(codes + ra * C::RB_IDX + t * 8);
+          const uint2 vb = *reinterpret_cast<const uint2*>(codes + rbb * C::RB_IDX + t * 8);
           uint32_t la0, ha0, la1, ha1, lb0, hb0, lb1, hb1;
           nib_to_s8(va.x, la0, ha0);
           nib_to_s8(va.y, la1, ha1);
@@ -326,8 +319,8 @@ __global__ void __launch_bounds__(kThreads) csa_decode_kernel(CsaParams p) {
           a[0][0] = la0; a[0][1] = lb0; a[0][2] = ha0; a[0][3] = hb0;
           a[1][0] = la1; a[1][1] = lb1; a[1][2] = ha1; a[1][3] = hb1;
         } else {
-          const uint4 va = *reinterpret_cast<const uint4*>(codes + rowA * C::RB_IDX + t * 16);
-          const uint4 vb = *reinterpret_cast<const uint4*>(codes + rowB * C::RB_IDX + t * 16);
+          const uint4 va = *reinterpret_cast<const uint4*>(codes + ra * C::RB_IDX + t * 16);
+          const uint4 vb = *reinterpret_cast<const uint4*>(codes + rbb * C::RB_IDX + t * 16);
           a[0][0] = va.x; a[0][1] = vb.x; a[0][2] = va.y; a[0][3] = vb.y;
           a[1][0] = va.z; a[1][1] = vb.z; a[1][2] = va.w; a[1][3] = vb.w;
         }
@@ -355,7 +348,7 @@ __global__ void __launch_bounds__(kThreads) csa_decode_kernel(CsaParams p) {
         if (t < 2) {
           const int key = c * C::CH * kPage + lrow;  // CTA-local key index
           if (key < nkeys) {
-            float s = __fadd_rn(__fmul_rn(t == 0 ? sA : sB, ksc[lrow]), 0.0f);
+            float s = __fadd_rn(__fmul_rn(t == 0 ? sA : sB, ksc[lrow & 63]), 0.0f);
             scores[key] = __float_as_uint(s) + 1u;
           }
         }
@@ -572,9 +565,9 @@ __global__ void __launch_bounds__(kThreads) csa_decode_kernel(CsaParams p) {
         report_error(p.err, kErrBadPage);
         phys = 0;
       }
-      const long long e = static_cast<long long>(phys) * kPage + (blk & 63);
-      cp_async16(raw + row * C::RB_KV + ch * 16, p.kv_codes + e * C::RB_KV + ch * 16);
-      if (ch == 0) cp_async4(ks + row, p.kv_scale + e);
+      const uint8_t* pg = p.kv_pages + static_cast<long long>(phys) * C::PB_KV;
+      cp_async16(raw + row * C::RB_KV + ch * 16, pg + (blk & 63) * C::RB_KV + ch * 16);
+      if (ch == 0) cp_async4(ks + row, pg + kPage * C::RB_KV + (blk & 63) * 4);
     }
   }
   // queries: plain (for the window) and rotated WHT(diag * q) (for the codes)
@@ -871,8 +864,7 @@ static int choose_cluster(int B, bool hca, int bits, int max_nblocks) {
 }
 
 static int csa_common(bool hca, const void* q, const float* index_q, const float* index_w, const float* sink,
-                      const void* window, const int32_t* window_len, const uint8_t* idx_codes,
-                      const float* idx_scale, const uint8_t* kv_codes, const float* kv_scale,
+                      const void* window, const int32_t* window_len, const uint8_t* idx_pages, const uint8_t* kv_pages,
                       const int32_t* page_table, int table_stride, int num_pages, const int32_t* nblocks,
                       int max_nblocks, const float* diag_idx, const float* diag_kv, int B, int H, int W, int bits,
                       int top_k, float softmax_scale, void* out, int32_t* sel_out, int* err, int cluster,
@@ -896,10 +888,8 @@ static int csa_common(bool hca, const void* q, const float* index_q, const float
   p.sink = sink;
   p.window = static_cast<const __nv_bfloat16*>(window);
   p.window_len = window_len;
-  p.idx_codes = idx_codes;
-  p.idx_scale = idx_scale;
-  p.kv_codes = kv_codes;
-  p.kv_scale = kv_scale;
+  p.idx_pages = idx_pages;
+  p.kv_pages = kv_pages;
   p.page_table = page_table;
   p.nblocks = nblocks;
   p.diag_idx = diag_idx;
@@ -921,6 +911,13 @@ static int csa_common(bool hca, const void* q, const float* index_q, const float
   return check_launch(hca ? "hca_decode_paged" : "csa_decode_paged");
 }
 
+int csa_decode_cta(const void* q, const float* index_q, const float* index_w, const float* sink, const void* window,
+                   const int32_t* window_len, const uint8_t* idx_pages, const uint8_t* kv_pages,
+                   const int32_t* page_table, int table_stride, int num_pages, const int32_t* nblocks,
+                   int max_nblocks, const float* diag_idx, const float* diag_kv, int B, int H, int W, int bits,
+                   int top_k, float softmax_scale, void* out, int32_t* sel_out, float* score_out, int score_stride,
+                   int* err, int pdl, void* stream);
+
 }  // namespace aether
 
 using namespace aether;
@@ -928,24 +925,27 @@ using namespace aether;
 extern "C" {
 
 int aether_csa_decode_paged(const void* q, const float* index_q, const float* index_w, const float* sink,
-                            const void* window, const int32_t* window_len, const uint8_t* idx_codes,
-                            const float* idx_scale, const uint8_t* kv_codes, const float* kv_scale,
+                            const void* window, const int32_t* window_len, const uint8_t* idx_pages, const uint8_t* kv_pages,
                             const int32_t* page_table, int table_stride, int num_pages, const int32_t* nblocks,
                             int max_nblocks, const float* diag_idx, const float* diag_kv, int B, int H, int W,
                             int bits, int top_k, float softmax_scale, void* out, int32_t* sel_out, int* err,
-                            int cluster, void* stream) {
-  AETHER_REQUIRE(index_q && index_w && idx_codes && idx_scale && diag_idx, "csa_decode_paged: null index input");
-  return csa_common(false, q, index_q, index_w, sink, window, window_len, idx_codes, idx_scale, kv_codes, kv_scale,
+                            int cluster, int pdl, void* stream) {
+  AETHER_REQUIRE(index_q && index_w && idx_pages && diag_idx, "csa_decode_paged: null index input");
+  if (cluster <= 1)
+    return csa_decode_cta(q, index_q, index_w, sink, window, window_len, idx_pages, kv_pages, page_table,
+                          table_stride, num_pages, nblocks, max_nblocks, diag_idx, diag_kv, B, H, W, bits, top_k,
+                          softmax_scale, out, sel_out, nullptr, 0, err, pdl, stream);
+  return csa_common(false, q, index_q, index_w, sink, window, window_len, idx_pages, kv_pages,
                     page_table, table_stride, num_pages, nblocks, max_nblocks, diag_idx, diag_kv, B, H, W, bits,
                     top_k, softmax_scale, out, sel_out, err, cluster, stream);
 }
 
 int aether_hca_decode_paged(const void* q, const float* sink, const void* window, const int32_t* window_len,
-                            const uint8_t* kv_codes, const float* kv_scale, const int32_t* page_table,
+                            const uint8_t* kv_pages, const int32_t* page_table,
                             int table_stride, int num_pages, const int32_t* nblocks, int max_nblocks,
                             const float* diag_kv, int B, int H, int W, int bits, float softmax_scale, void* out,
                             int* err, int cluster, void* stream) {
-  return csa_common(true, q, nullptr, nullptr, sink, window, window_len, nullptr, nullptr, kv_codes, kv_scale,
+  return csa_common(true, q, nullptr, nullptr, sink, window, window_len, nullptr, kv_pages,
                     page_table, table_stride, num_pages, nblocks, max_nblocks, nullptr, diag_kv, B, H, W, bits, 0,
                     softmax_scale, out, nullptr, err, cluster, stream);
 }
@@ -953,16 +953,19 @@ int aether_hca_decode_paged(const void* q, const float* sink, const void* window
 // Same as aether_csa_decode_paged, and additionally writes every visible
 // block's index score to score_out[b * score_stride + block] (fp32).
 int aether_csa_decode_paged_scores(const void* q, const float* index_q, const float* index_w, const float* sink,
-                                   const void* window, const int32_t* window_len, const uint8_t* idx_codes,
-                                   const float* idx_scale, const uint8_t* kv_codes, const float* kv_scale,
+                                   const void* window, const int32_t* window_len, const uint8_t* idx_pages, const uint8_t* kv_pages,
                                    const int32_t* page_table, int table_stride, int num_pages,
                                    const int32_t* nblocks, int max_nblocks, const float* diag_idx,
                                    const float* diag_kv, int B, int H, int W, int bits, int top_k,
                                    float softmax_scale, void* out, int32_t* sel_out, float* score_out,
-                                   int score_stride, int* err, int cluster, void* stream) {
-  AETHER_REQUIRE(index_q && index_w && idx_codes && idx_scale && diag_idx, "csa_decode_paged: null index input");
+                                   int score_stride, int* err, int cluster, int pdl, void* stream) {
+  AETHER_REQUIRE(index_q && index_w && idx_pages && diag_idx, "csa_decode_paged: null index input");
   AETHER_REQUIRE(score_out && score_stride >= max_nblocks, "score_out must hold max_nblocks per row");
-  return csa_common(false, q, index_q, index_w, sink, window, window_len, idx_codes, idx_scale, kv_codes, kv_scale,
+  if (cluster <= 1)
+    return csa_decode_cta(q, index_q, index_w, sink, window, window_len, idx_pages, kv_pages, page_table,
+                          table_stride, num_pages, nblocks, max_nblocks, diag_idx, diag_kv, B, H, W, bits, top_k,
+                          softmax_scale, out, sel_out, score_out, score_stride, err, pdl, stream);
+  return csa_common(false, q, index_q, index_w, sink, window, window_len, idx_pages, kv_pages,
                     page_table, table_stride, num_pages, nblocks, max_nblocks, diag_idx, diag_kv, B, H, W, bits,
                     top_k, softmax_scale, out, sel_out, err, cluster, stream, score_out, score_stride);
 }

@@ -89,23 +89,34 @@ __device__ __forceinline__ void warp_wht(float (&v)[D / 32], int lane) {
 // Destination address resolution: either dense rows, or paged slots
 // (page_table[seq * stride + pos / 64], slot pos % 64) for cache appends.
 struct RowDst {
-  const int32_t* page_table;  // null => dense
+  const int32_t* page_table;  // null => dense rows
   const int32_t* start_pos;   // [B] first block position written per sequence
   int table_stride;
   int rows_per_seq;
   int num_pages;
 };
 
-__device__ __forceinline__ long long resolve_row(const RowDst& r, long long row, int* err) {
-  if (!r.page_table) return row;
+// Byte offsets of a row's codes and scale.  Dense: codes[row], scales[row].
+// Paged: page = page_table[seq, pos / 64], slot = pos % 64 inside the
+// [codes | scales] page layout (page_bytes).
+__device__ __forceinline__ bool resolve_row(const RowDst& r, long long row, int rb, int* err, long long& code_off,
+                                            long long& scale_off) {
+  if (!r.page_table) {
+    code_off = row * rb;
+    scale_off = row * 4;
+    return true;
+  }
   const int seq = static_cast<int>(row / r.rows_per_seq);
   const int pos = r.start_pos[seq] + static_cast<int>(row % r.rows_per_seq);
   const int page = r.page_table[static_cast<long long>(seq) * r.table_stride + (pos >> 6)];
   if (page < 0 || page >= r.num_pages) {
     report_error(err, kErrBadPage);
-    return -1;
+    return false;
   }
-  return static_cast<long long>(page) * kPage + (pos & (kPage - 1));
+  const long long base = static_cast<long long>(page) * page_bytes(rb);
+  code_off = base + (pos & (kPage - 1)) * rb;
+  scale_off = base + kPage * rb + (pos & (kPage - 1)) * 4;
+  return true;
 }
 
 template <int D, int BITS, typename T>
@@ -129,9 +140,11 @@ __global__ void __launch_bounds__(256) tq_encode_kernel(const T* __restrict__ x,
   for (int k = 0; k < EPL; ++k) m = fmaxf(m, fabsf(v[k]));
   m = warp_max(m);
   m = fmaxf(m, 9.99999993922529e-09f);  // float32(1e-8), torch clamp_(min=1e-8)
-  const long long out_row = resolve_row(dst, row, err);
-  if (out_row < 0) return;
-  if (lane == 0) scales[out_row] = __fdiv_rn(m, L);
+  constexpr int RB = BITS == 8 ? D : D / 2;
+  long long coff, soff;
+  if (!resolve_row(dst, row, RB, err, coff, soff)) return;
+  uint8_t* scale_base = dst.page_table ? codes : reinterpret_cast<uint8_t*>(scales);
+  if (lane == 0) *reinterpret_cast<float*>(scale_base + soff) = __fdiv_rn(m, L);
   int q[EPL];
 #pragma unroll
   for (int k = 0; k < EPL; ++k) {
@@ -143,7 +156,7 @@ __global__ void __launch_bounds__(256) tq_encode_kernel(const T* __restrict__ x,
     uint32_t w = 0;
 #pragma unroll
     for (int k = 0; k < EPL; ++k) w |= (static_cast<uint32_t>(q[k]) & 0xFFu) << (8 * k);
-    uint8_t* base = codes + out_row * D + lane * EPL;
+    uint8_t* base = codes + coff + lane * EPL;
     if (EPL == 4)
       *reinterpret_cast<uint32_t*>(base) = w;
     else
@@ -152,7 +165,7 @@ __global__ void __launch_bounds__(256) tq_encode_kernel(const T* __restrict__ x,
     uint32_t w = 0;
 #pragma unroll
     for (int k = 0; k < EPL; ++k) w |= (static_cast<uint32_t>(q[k]) & 0xFu) << (4 * k);
-    uint8_t* base = codes + out_row * (D / 2) + lane * (EPL / 2);
+    uint8_t* base = codes + coff + lane * (EPL / 2);
     if (EPL == 4)
       *reinterpret_cast<uint16_t*>(base) = static_cast<uint16_t>(w);
     else
@@ -262,13 +275,13 @@ int aether_tq_encode(const void* x, int dtype, long long rows, int d, int bits, 
 
 int aether_tq_encode_into_pages(const void* x, int dtype, int batch, int rows_per_seq, int d, int bits,
                                 const float* diag, const int32_t* page_table, int table_stride,
-                                const int32_t* start_pos, int num_pages, uint8_t* code_pool, float* scale_pool,
-                                int* err, void* stream) {
+                                const int32_t* start_pos, int num_pages, uint8_t* page_pool, int* err,
+                                void* stream) {
   AETHER_REQUIRE(page_table && start_pos, "encode_into_pages: page_table and start_pos are required");
   AETHER_REQUIRE(batch >= 0 && rows_per_seq >= 0, "encode_into_pages: negative size");
   RowDst dst{page_table, start_pos, table_stride, rows_per_seq > 0 ? rows_per_seq : 1, num_pages};
-  return launch_encode(dtype, x, diag, code_pool, scale_pool, static_cast<long long>(batch) * rows_per_seq, d,
-                       bits, dst, err, static_cast<cudaStream_t>(stream));
+  return launch_encode(dtype, x, diag, page_pool, nullptr, static_cast<long long>(batch) * rows_per_seq, d, bits,
+                       dst, err, static_cast<cudaStream_t>(stream));
 }
 
 int aether_tq_decode(const uint8_t* codes, const float* scales, long long rows, int d, int bits,

@@ -74,9 +74,11 @@ class DecodeResult:
 
 def decode_step(kind: str, q, index_q, index_weight, sink, window, window_len, idx_codes, idx_scale, kv_codes,
                 kv_scale, page_table, nblocks, bits: int, top_k: int, softmax_scale: float, seed: int = 42,
-                tie_tol: float = 1e-5, use_selection: Optional[List[torch.Tensor]] = None) -> DecodeResult:
+                tie_tol: float = 1e-5, use_selection: Optional[List[torch.Tensor]] = None,
+                classify_ties: bool = True) -> DecodeResult:
     """All tensors on the CPU.  ``use_selection`` replaces the oracle's top-k
-    by a given per-row selection (to check attention on a near-tie row)."""
+    by a given per-row selection (to check attention on a near-tie row);
+    ``classify_ties=False`` skips the fp64 near-tie bookkeeping (timing)."""
     B, H, D = q.shape
     outs, sels, ties = [], [], []
     for b in range(B):
@@ -95,7 +97,7 @@ def decode_step(kind: str, q, index_q, index_weight, sink, window, window_len, i
             elif nb > 0:
                 s32 = index_scores(index_q[b].float(), index_weight[b].float(), keys)
                 sel = torch.sort(topk_stable(s32, k)).values
-                if nb > k:
+                if nb > k and classify_ties:
                     s64 = index_scores(index_q[b].double(), index_weight[b].double(), keys.double())
                     srt = torch.sort(s64, descending=True).values
                     mag = (index_q[b].double().abs() @ keys.double().abs().T)

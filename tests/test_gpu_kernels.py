@@ -204,7 +204,7 @@ def _check_decode(batch, out, sel, rows=None):
 
 
 @pytest.mark.parametrize("bits", [8, 4])
-@pytest.mark.parametrize("cluster", [4, 8])
+@pytest.mark.parametrize("cluster", [0, 4, 8])
 def test_csa_decode_small_ragged(ak, bits, cluster):
     from aether_kernels.synthetic import make_decode_batch
 
@@ -272,3 +272,21 @@ def test_hca_decode(ak, bits):
                               rope=RopeConfig.yarn(4.0))
     out, _ = _run_decode(ak, batch)
     _check_decode(batch, out, None)
+
+
+def test_csa_decode_overlap_prefetch(ak):
+    """Back-to-back launches with programmatic dependent launch give the
+    same results as plain launches."""
+    from aether_kernels.paged import csa_decode_paged
+    from aether_kernels.synthetic import make_decode_batch
+
+    bs = [make_decode_batch("csa", 8, 9000, 30000, 4, 4, seed=40 + i, device="cuda") for i in range(3)]
+    plain = [_run_decode(ak, b) for b in bs]
+    outs = []
+    for b in bs:
+        outs.append(csa_decode_paged(b.q, b.index_q, b.index_weight, b.sink, b.window, b.window_len, b.cache,
+                                     b.page_table, b.nblocks, b.softmax_scale, top_k=b.top_k, overlap_prefetch=True))
+    torch.cuda.synchronize()
+    for (o, s), (po, ps) in zip(outs, plain):
+        assert torch.equal(s, ps)
+        assert torch.equal(o, po)
