@@ -1,0 +1,130 @@
+/*
+ * C ABI of libaether_b200.so: sm_100a (B200) kernels for Aether-2B's CSA/HCA
+ * decode path over a paged TurboQuant KV cache.
+ *
+ * Conventions
+ *   - All pointers are device pointers unless stated; sizes are element counts.
+ *   - `stream` is a cudaStream_t passed as void*; work is enqueued, not waited.
+ *   - Return 0 on success, 1 for an invalid argument, 2 for a CUDA error; the
+ *     message is in aether_last_error() (thread-local).
+ *   - `err` (optional, may be NULL) is a device int that kernels OR error bits
+ *     into: 1 = a bounded wait expired, 2 = page id outside the pool,
+ *     4 = a size exceeded a compiled limit.
+ *   - dtype codes: 0 = float32, 1 = float16, 2 = bfloat16.
+ *   - Cache pages: 64 entries per page stored as [64 code rows][64 fp32
+ *     scales]; row bytes = dim * bits / 8 (4-bit codes: two's complement
+ *     nibbles, even element in the low nibble).
+ *
+ * Reference citations are file:line inside itz-sayak/deepseek-v4-codebase.
+ */
+#ifndef AETHER_B200_H_
+#define AETHER_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+const char* aether_last_error(void);
+int aether_abi_version(void);
+int aether_compiled_arch(void);
+
+/* ---------------------------------------------------------------- TurboQuant
+ * Replaces PolarQuant.encode (aether_2b/turbo_quant.py:127-166): codes are
+ * bit-identical to the reference's fp32 path.  x [rows, d] (d = 64 or 128),
+ * diag [d] the +-1 Rademacher diagonal (turbo_quant.py:111-121).
+ * codes: int8 [rows, d] (bits 8) or uint8 [rows, d/2] (bits 4); scales [rows]. */
+int aether_tq_encode(const void* x, int dtype, long long rows, int d, int bits, const float* diag,
+                     uint8_t* codes, float* scales, int* err, void* stream);
+
+/* Cache append (replaces aether_2b/serving.py:327-344 _quant_append): encodes
+ * x [batch, rows_per_seq, d] and writes row i of sequence b at logical
+ * position start_pos[b] + i of that sequence's pages in page_pool. */
+int aether_tq_encode_into_pages(const void* x, int dtype, int batch, int rows_per_seq, int d, int bits,
+                                const float* diag, const int32_t* page_table, int table_stride,
+                                const int32_t* start_pos, int num_pages, uint8_t* page_pool, int* err,
+                                void* stream);
+
+/* Replaces PolarQuant.decode (aether_2b/turbo_quant.py:168-211). */
+int aether_tq_decode(const uint8_t* codes, const float* scales, long long rows, int d, int bits,
+                     const float* diag, void* out, int out_dtype, void* stream);
+
+/* Normalised Walsh-Hadamard transform, fp32 (aether_2b/turbo_quant.py:49-76). */
+int aether_wht(const float* x, float* out, long long rows, int d, void* stream);
+
+/* ------------------------------------------------ reference extension ops
+ * Replaces sparse_sink_attention (aether_kernels/csrc/bindings.cpp:21-46,
+ * sparse_sink_attention_cuda.cu:118-177).  q [B,T,H,D], kv [B,S,2,D],
+ * topk_indices [B,T,K] int32 or int64 (entries outside [0,S) skipped),
+ * sink scalar or [H], all in `dtype`; out [B,T,H,D]. */
+int aether_sparse_sink_attention(const void* q, const void* kv, const void* topk_indices, int idx_is_int64,
+                                 const void* sink, int sink_numel, void* out, int dtype, int B, int T, int H, int D,
+                                 int S, int K, float softmax_scale, void* stream);
+
+/* Replaces tiled_prefill_attention (bindings.cpp:58-77): every target token
+ * attends to all S sources; the sink enters the denominator once. */
+int aether_tiled_prefill_attention(const void* q, const void* kv, const void* sink, int sink_numel, void* out,
+                                   int dtype, int B, int T, int H, int D, int S, float softmax_scale, int tile_size,
+                                   void* stream);
+
+/* Replaces csa_indexer_topk (bindings.cpp:88-101) with the canonical score
+ * sum_h softplus(w_h) * relu(q_h . k_s) (aether_2b/modeling.py:609-611);
+ * out [B,k] int64 ordered by (score desc, index asc).  `scratch` holds
+ * aether_csa_indexer_topk_scratch_bytes(B, S) bytes. */
+size_t aether_csa_indexer_topk_scratch_bytes(int B, int S);
+int aether_csa_indexer_topk(const float* index_q, const float* index_kv, const float* index_weight, int B, int IH,
+                            int IC, int S, int k, float* scratch, int64_t* out, void* stream);
+
+/* Replaces hca_compress (bindings.cpp:110-119): softmax over the window of
+ * buffer_z per channel, weighted sum of buffer_c; out [B,D]. */
+int aether_hca_compress(const void* buffer_c, const void* buffer_z, void* out, int dtype, int B, int M, int D,
+                        void* stream);
+
+/* ------------------------------------------------- fused paged decode
+ * One CSA decode step for B sequences (replaces the data flow of
+ * aether_2b/serving.py:597-625 + the backend call at :450-467):
+ *   q [B,H,128] bf16, index_q [B,4,64] fp32, index_w [B,4] fp32 raw head
+ *   weights, sink [H] fp32, window [B,W,128] bf16 (window_len[b] valid rows,
+ *   oldest first), idx_pages / kv_pages page pools, page_table [B,table_stride]
+ *   int32, nblocks [B] visible compressed blocks (<= max_nblocks <= 8192),
+ *   diag_idx [64] / diag_kv [128] Rademacher diagonals.
+ * out [B,H,128] bf16 (attention output before the inverse output RoPE),
+ * sel_out [B,top_k] int32 selected block ids ascending, -1 padded (may be NULL).
+ * cluster: 0 = one CTA per sequence, 4 or 8 = thread-block cluster per sequence.
+ * pdl: 1 = programmatic dependent launch; the kernel then reads page_table,
+ * nblocks, window_len, cache pages and all window rows but the newest before
+ * the previous kernel in the stream has completed. */
+int aether_csa_decode_paged(const void* q, const float* index_q, const float* index_w, const float* sink,
+                            const void* window, const int32_t* window_len, const uint8_t* idx_pages,
+                            const uint8_t* kv_pages, const int32_t* page_table, int table_stride, int num_pages,
+                            const int32_t* nblocks, int max_nblocks, const float* diag_idx, const float* diag_kv,
+                            int B, int H, int W, int bits, int top_k, float softmax_scale, void* out,
+                            int32_t* sel_out, int* err, int cluster, int pdl, void* stream);
+
+/* As aether_csa_decode_paged, also writing each visible block's index score
+ * to score_out[b * score_stride + block]. */
+int aether_csa_decode_paged_scores(const void* q, const float* index_q, const float* index_w, const float* sink,
+                                   const void* window, const int32_t* window_len, const uint8_t* idx_pages,
+                                   const uint8_t* kv_pages, const int32_t* page_table, int table_stride,
+                                   int num_pages, const int32_t* nblocks, int max_nblocks, const float* diag_idx,
+                                   const float* diag_kv, int B, int H, int W, int bits, int top_k,
+                                   float softmax_scale, void* out, int32_t* sel_out, float* score_out,
+                                   int score_stride, int* err, int cluster, int pdl, void* stream);
+
+/* One HCA decode step (replaces aether_2b/serving.py:507-522): attention over
+ * every visible compressed block plus the window; nblocks <= 1024. */
+int aether_hca_decode_paged(const void* q, const float* sink, const void* window, const int32_t* window_len,
+                            const uint8_t* kv_pages, const int32_t* page_table, int table_stride, int num_pages,
+                            const int32_t* nblocks, int max_nblocks, const float* diag_kv, int B, int H, int W,
+                            int bits, float softmax_scale, void* out, int* err, int cluster, void* stream);
+
+/* Shared-memory bytes of the one-CTA-per-sequence CSA decode kernel. */
+int aether_csa_decode_smem_bytes(int bits);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* AETHER_B200_H_ */
