@@ -44,6 +44,11 @@ SIGNATURES = {
         _c_int,
         [_p, _p, _p, _c_int, _c_int, _c_int, _c_int, _c_int, _p, _p, _p],
     ),
+    "aether_csa_indexer_topk_noalloc_max_scores": (_c_ll, []),
+    "aether_csa_indexer_topk_noalloc": (
+        _c_int,
+        [_p, _p, _p, _c_int, _c_int, _c_int, _c_int, _c_int, _p, _p],
+    ),
     "aether_hca_compress": (_c_int, [_p, _p, _p, _c_int, _c_int, _c_int, _c_int, _p]),
     "aether_csa_decode_paged": (
         _c_int,

@@ -383,3 +383,73 @@ int aether_hca_compress(const void* buffer_c, const void* buffer_z, void* out, i
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// csa_indexer_topk without any allocation.
+//
+// Some callers cannot allocate device memory at the point where they need the
+// indexer: code running inside a host callback or a custom allocator's hook,
+// engines that must not call cudaMalloc while another stream is being
+// captured, or plugins that only ever receive the caller's input and output
+// buffers.  For them this variant keeps its score buffer in a fixed array of
+// the library itself, so nothing is allocated per call.
+//
+// Limit: batch * sources <= kNoAllocScores (1 Mi fp32 scores, 4 MiB).  Every
+// GPU that loads the library holds that array until the process exits.
+// The first call on a device, with that device current, looks up the array's
+// device address (cudaGetSymbolAddress) and caches it; make that first call
+// before any stream capture.  All calls share the one array: every call
+// overwrites the scores it reads, so nothing has to be cleared, but two calls
+// whose kernels overlap on the GPU (different streams, no ordering) race on it.
+#include <mutex>
+
+namespace aether {
+
+constexpr long long kNoAllocScores = 1ll << 20;
+static __device__ __align__(256) float g_noalloc_scores[kNoAllocScores];
+
+static std::mutex g_noalloc_mu;
+static float* g_noalloc_ptr[64] = {};
+
+static int noalloc_scratch(float** out) {
+  int dev = 0;
+  AETHER_CUDA_TRY(cudaGetDevice(&dev), "csa_indexer_topk_noalloc: cudaGetDevice");
+  AETHER_REQUIRE(dev >= 0 && dev < 64, "csa_indexer_topk_noalloc: device ordinal %d not supported", dev);
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    AETHER_CUDA_TRY(cudaGetSymbolAddress(&p, g_noalloc_scores), "csa_indexer_topk_noalloc: cudaGetSymbolAddress");
+    g_noalloc_ptr[dev] = static_cast<float*>(p);
+  }
+  *out = g_noalloc_ptr[dev];
+  return 0;
+}
+
+}  // namespace aether
+
+extern "C" {
+
+long long aether_csa_indexer_topk_noalloc_max_scores(void) { return aether::kNoAllocScores; }
+
+int aether_csa_indexer_topk_noalloc(const float* index_q, const float* index_kv, const float* index_weight, int B,
+                                    int IH, int IC, int S, int k, int64_t* out, void* stream) {
+  AETHER_REQUIRE(k > 0, "k must be positive");
+  AETHER_REQUIRE(k <= S, "k (%d) must not exceed the number of sources (%d)", k, S);
+  AETHER_REQUIRE(k <= kTopkMax, "k must be <= %d, got %d", kTopkMax, k);
+  AETHER_REQUIRE(S < 65536, "csa_indexer_topk_noalloc: at most 65535 sources per row, got %d", S);
+  AETHER_REQUIRE(B >= 0 && static_cast<long long>(B) * S <= aether::kNoAllocScores,
+                 "csa_indexer_topk_noalloc: batch * sources = %lld exceeds the built-in scratch of %lld scores",
+                 static_cast<long long>(B) * S, aether::kNoAllocScores);
+  if (B == 0) return 0;
+  float* scratch = nullptr;
+  const int rc = aether::noalloc_scratch(&scratch);
+  if (rc) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const long long warps = static_cast<long long>(B) * S;
+  dense_index_score_kernel<<<(warps * 32 + 255) / 256, 256, 0, st>>>(index_q, index_kv, index_weight, scratch, B, IH,
+                                                                     IC, S);
+  row_topk_kernel<<<B, kTopkThreads, 0, st>>>(scratch, S, k, out);
+  return check_launch("csa_indexer_topk_noalloc");
+}
+
+}  // extern "C"

@@ -77,6 +77,20 @@ size_t aether_csa_indexer_topk_scratch_bytes(int B, int S);
 int aether_csa_indexer_topk(const float* index_q, const float* index_kv, const float* index_weight, int B, int IH,
                             int IC, int S, int k, float* scratch, int64_t* out, void* stream);
 
+/* Variant of aether_csa_indexer_topk that allocates nothing; it has no
+ * counterpart in the reference.  For callers that cannot allocate device
+ * memory where they call the indexer (host callbacks, allocator hooks, code
+ * running while another stream is being captured, plugins handed only their
+ * input and output buffers): the score buffer is a fixed array inside the
+ * library, B * S <= aether_csa_indexer_topk_noalloc_max_scores() (1 Mi scores,
+ * 4 MiB held on every GPU that loads the library until exit).  Larger sizes
+ * return 1 with a message.  The first call on a device (that device current)
+ * looks up the array's address; make it before any stream capture.  Calls
+ * share the array: calls whose kernels overlap on the GPU race. */
+long long aether_csa_indexer_topk_noalloc_max_scores(void);
+int aether_csa_indexer_topk_noalloc(const float* index_q, const float* index_kv, const float* index_weight, int B,
+                                    int IH, int IC, int S, int k, int64_t* out, void* stream);
+
 /* Replaces hca_compress (bindings.cpp:110-119): softmax over the window of
  * buffer_z per channel, weighted sum of buffer_c; out [B,D]. */
 int aether_hca_compress(const void* buffer_c, const void* buffer_z, void* out, int dtype, int B, int M, int D,
