@@ -140,6 +140,12 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
+def max_ws_bytes(batch):
+    from aether_kernels.paged import csa_workspace_bytes
+
+    return csa_workspace_bytes(batch, CFG["ctx_hi"] // CFG["compression"])
+
+
 def build_sets(nsets, device, rank):
     from aether_kernels.paged import PAGE, TurboQuantPagedCache
     from aether_kernels.synthetic import make_decode_batch
@@ -253,6 +259,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-pdl", dest="pdl", action="store_false",
                     help="launch without programmatic dependent launch (no prefetch overlap across steps)")
+    ap.add_argument("--cluster", type=int, default=0, help="0: score + attend kernels; 4 or 8: cluster kernel")
+    ap.add_argument("--microbatches", type=int, default=1,
+                    help="split each step's batch into this many independent micro-batches on separate streams")
     ap.add_argument("--profile-launches", type=int, default=0,
                     help="profiling mode: build the sets, run this many plain launches, print timings, exit")
     args = ap.parse_args()
@@ -279,11 +288,31 @@ def main():
     sels = [torch.empty(B, CFG["top_k"], dtype=torch.int32, device=dev) for _ in sets]
     err = torch.zeros(1, dtype=torch.int32, device=dev)
 
-    def step(i, pdl=args.pdl):
+    mb = args.microbatches
+    assert B % mb == 0
+    mbs = B // mb
+    side = [torch.cuda.Stream(dev) for _ in range(mb)]
+    ws = [torch.empty(max_ws_bytes(mbs), dtype=torch.uint8, device=dev) for _ in range(mb)]
+
+    def launch(i, lo, hi, pdl, w):
         s = sets[i % len(sets)]
-        csa_decode_paged(s.q, s.index_q, s.index_weight, s.sink, s.window, s.window_len, cache, s.page_table,
-                         s.nblocks, s.softmax_scale, top_k=s.top_k, out=outs[i % len(sets)],
-                         indices=sels[i % len(sets)], err=err, overlap_prefetch=pdl)
+        csa_decode_paged(s.q[lo:hi], s.index_q[lo:hi], s.index_weight[lo:hi], s.sink, s.window[lo:hi],
+                         s.window_len[lo:hi], cache, s.page_table[lo:hi], s.nblocks[lo:hi], s.softmax_scale,
+                         top_k=s.top_k, out=outs[i % len(sets)][lo:hi], indices=sels[i % len(sets)][lo:hi],
+                         err=err, overlap_prefetch=pdl, workspace=w, cluster=args.cluster)
+
+    def step(i, pdl=args.pdl):
+        if mb == 1:
+            launch(i, 0, B, pdl, ws[0])
+            return
+        # independent micro-batches on their own streams (fork / join)
+        cur = torch.cuda.current_stream(dev)
+        for k in range(mb):
+            side[k].wait_stream(cur)
+            with torch.cuda.stream(side[k]):
+                launch(i, k * mbs, (k + 1) * mbs, pdl, ws[k])
+        for k in range(mb):
+            cur.wait_stream(side[k])
 
     if args.profile_launches:
         evs = [torch.cuda.Event(enable_timing=True) for _ in range(args.profile_launches + 1)]
@@ -396,6 +425,7 @@ def main():
                        "cache_bytes_cycled": int(sum(t.numel() * t.element_size() for t in cache.tensors())),
                        "l2_policy": "inputs larger than L2: each step reads a different cache set, sets > 4x L2",
                        "parallelism": f"request-sharded x{world}", "pdl": bool(args.pdl),
+                       "microbatches": args.microbatches,
                        "timing": "CUDA graph replay, CUDA events"},
             "gpu_launches": steps,
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",

@@ -58,7 +58,7 @@ SIGNATURES = {
             _p, _c_int, _c_int, _p, _c_int,    # page_table, stride, num_pages, nblocks, max_nblocks
             _p, _p,                            # diag_idx, diag_kv
             _c_int, _c_int, _c_int, _c_int, _c_int, _c_f,  # B, H, W, bits, top_k, scale
-            _p, _p, _p, _c_int, _c_int, _p,    # out, sel_out, err, cluster, pdl, stream
+            _p, _p, _p, _p, _c_int, _c_int, _p,  # out, sel_out, workspace, err, cluster, pdl, stream
         ],
     ),
     "aether_csa_decode_paged_scores": (
@@ -69,10 +69,12 @@ SIGNATURES = {
             _p, _c_int, _c_int, _p, _c_int,
             _p, _p,
             _c_int, _c_int, _c_int, _c_int, _c_int, _c_f,
-            _p, _p, _p, _c_int, _p, _c_int, _c_int, _p,  # out, sel, score_out, stride, err, cluster, pdl, stream
+            _p, _p, _p, _c_int, _p, _p, _c_int, _c_int, _p,  # out, sel, score_out, stride, ws, err, cluster, pdl, stream
         ],
     ),
     "aether_csa_decode_smem_bytes": (_c_int, [_c_int]),
+    "aether_csa_decode_workspace_bytes": (ctypes.c_size_t, [_c_int, _c_int]),
+    "aether_csa_decode_set_debug_timer": (None, [_p]),
     "aether_hca_decode_paged": (
         _c_int,
         [

@@ -111,6 +111,11 @@ class TurboQuantPagedCache:
             tq_encode_into_pages(index, self.bits, page_table, start_pos, self.idx_pages, self.seed, err)
 
 
+def csa_workspace_bytes(batch: int, max_nblocks: int) -> int:
+    """Workspace bytes of ``csa_decode_paged`` (u32 score key per visible block)."""
+    return int(_lib.load().aether_csa_decode_workspace_bytes(int(batch), int(max_nblocks)))
+
+
 def _opt_ptr(t: Optional[torch.Tensor]):
     return None if t is None else t.data_ptr()
 
@@ -133,6 +138,7 @@ def csa_decode_paged(
     cluster: int = 0,
     scores: Optional[torch.Tensor] = None,
     overlap_prefetch: bool = False,
+    workspace: Optional[torch.Tensor] = None,
 ) -> Tuple[torch.Tensor, torch.Tensor]:
     """One fused CSA decode step for a batch of sequences.
 
@@ -153,6 +159,9 @@ def csa_decode_paged(
     every window row except the newest.  Use it only when the immediately
     preceding kernel writes none of those.  ``scores`` (optional fp32
     [B, >= max_pages * 64]) receives every visible block's index score.
+    ``workspace`` (optional uint8 tensor of ``csa_workspace_bytes(B, max_pages
+    * 64)`` bytes) holds the per-block score keys between the two kernels;
+    it is allocated per call when not given.
     """
     B, H, D = q.shape
     _check(D == HEAD_DIM, f"head_dim must be {HEAD_DIM}")
@@ -180,15 +189,20 @@ def csa_decode_paged(
         B, H, window.shape[1], cache.bits, int(top_k), float(softmax_scale),
         out.data_ptr(), indices.data_ptr(),
     )
+    need = csa_workspace_bytes(B, page_table.shape[1] * PAGE)
+    if workspace is None:
+        workspace = torch.empty(max(need, 16), dtype=torch.uint8, device=dev)
+    _check(workspace.is_cuda and workspace.numel() * workspace.element_size() >= need,
+           f"workspace must hold {need} bytes")
     if scores is None:
-        _lib.call("aether_csa_decode_paged", *common, _opt_ptr(err), int(cluster), int(overlap_prefetch),
-                  _stream(dev))
+        _lib.call("aether_csa_decode_paged", *common, workspace.data_ptr(), _opt_ptr(err), int(cluster),
+                  int(overlap_prefetch), _stream(dev))
     else:
         _cuda(scores, "scores")
         _check(scores.dtype == torch.float32 and scores.shape[0] == B and scores.shape[1] >= page_table.shape[1] * PAGE,
                "scores must be float32 [B, >= max_pages * 64]")
-        _lib.call("aether_csa_decode_paged_scores", *common, scores.data_ptr(), scores.shape[1], _opt_ptr(err),
-                  int(cluster), int(overlap_prefetch), _stream(dev))
+        _lib.call("aether_csa_decode_paged_scores", *common, scores.data_ptr(), scores.shape[1],
+                  workspace.data_ptr(), _opt_ptr(err), int(cluster), int(overlap_prefetch), _stream(dev))
     return out, indices
 
 

@@ -193,8 +193,7 @@ __global__ void __launch_bounds__(kTopkThreads) row_topk_kernel(const float* __r
         m = nbits == 0 || (key >> (32 - nbits)) == prefix;
         if (m) dig = (key >> shift) & 255u;
       }
-      const uint32_t peers = __match_any_sync(0xffffffffu, dig);
-      if (m && (__ffs(peers) - 1) == lane) atomicAdd(&hist[dig], __popc(peers));
+      if (m) atomicAdd(&hist[dig], 1u);
     }
     __syncthreads();
     if (warp == 0) {

@@ -390,8 +390,7 @@ __global__ void __launch_bounds__(kThreads) csa_decode_kernel(CsaParams p) {
             m = nbits == 0 || (key >> (32 - nbits)) == prefix;
             if (m) dig = (key >> shift) & 255u;
           }
-          const uint32_t peers = __match_any_sync(0xffffffffu, dig);
-          if (m && (__ffs(peers) - 1) == lane) atomicAdd(&h[dig], __popc(peers));
+          if (m) atomicAdd(&h[dig], 1u);
         }
         cl.sync();
         uint32_t cnt[CS];
@@ -916,7 +915,7 @@ int csa_decode_cta(const void* q, const float* index_q, const float* index_w, co
                    const int32_t* page_table, int table_stride, int num_pages, const int32_t* nblocks,
                    int max_nblocks, const float* diag_idx, const float* diag_kv, int B, int H, int W, int bits,
                    int top_k, float softmax_scale, void* out, int32_t* sel_out, float* score_out, int score_stride,
-                   int* err, int pdl, void* stream);
+                   uint32_t* workspace, int* err, int pdl, void* stream);
 
 }  // namespace aether
 
@@ -928,13 +927,13 @@ int aether_csa_decode_paged(const void* q, const float* index_q, const float* in
                             const void* window, const int32_t* window_len, const uint8_t* idx_pages, const uint8_t* kv_pages,
                             const int32_t* page_table, int table_stride, int num_pages, const int32_t* nblocks,
                             int max_nblocks, const float* diag_idx, const float* diag_kv, int B, int H, int W,
-                            int bits, int top_k, float softmax_scale, void* out, int32_t* sel_out, int* err,
-                            int cluster, int pdl, void* stream) {
+                            int bits, int top_k, float softmax_scale, void* out, int32_t* sel_out,
+                            uint32_t* workspace, int* err, int cluster, int pdl, void* stream) {
   AETHER_REQUIRE(index_q && index_w && idx_pages && diag_idx, "csa_decode_paged: null index input");
   if (cluster <= 1)
     return csa_decode_cta(q, index_q, index_w, sink, window, window_len, idx_pages, kv_pages, page_table,
                           table_stride, num_pages, nblocks, max_nblocks, diag_idx, diag_kv, B, H, W, bits, top_k,
-                          softmax_scale, out, sel_out, nullptr, 0, err, pdl, stream);
+                          softmax_scale, out, sel_out, nullptr, 0, workspace, err, pdl, stream);
   return csa_common(false, q, index_q, index_w, sink, window, window_len, idx_pages, kv_pages,
                     page_table, table_stride, num_pages, nblocks, max_nblocks, diag_idx, diag_kv, B, H, W, bits,
                     top_k, softmax_scale, out, sel_out, err, cluster, stream);
@@ -958,13 +957,14 @@ int aether_csa_decode_paged_scores(const void* q, const float* index_q, const fl
                                    const int32_t* nblocks, int max_nblocks, const float* diag_idx,
                                    const float* diag_kv, int B, int H, int W, int bits, int top_k,
                                    float softmax_scale, void* out, int32_t* sel_out, float* score_out,
-                                   int score_stride, int* err, int cluster, int pdl, void* stream) {
+                                   int score_stride, uint32_t* workspace, int* err, int cluster, int pdl,
+                                   void* stream) {
   AETHER_REQUIRE(index_q && index_w && idx_pages && diag_idx, "csa_decode_paged: null index input");
   AETHER_REQUIRE(score_out && score_stride >= max_nblocks, "score_out must hold max_nblocks per row");
   if (cluster <= 1)
     return csa_decode_cta(q, index_q, index_w, sink, window, window_len, idx_pages, kv_pages, page_table,
                           table_stride, num_pages, nblocks, max_nblocks, diag_idx, diag_kv, B, H, W, bits, top_k,
-                          softmax_scale, out, sel_out, score_out, score_stride, err, pdl, stream);
+                          softmax_scale, out, sel_out, score_out, score_stride, workspace, err, pdl, stream);
   return csa_common(false, q, index_q, index_w, sink, window, window_len, idx_pages, kv_pages,
                     page_table, table_stride, num_pages, nblocks, max_nblocks, diag_idx, diag_kv, B, H, W, bits,
                     top_k, softmax_scale, out, sel_out, err, cluster, stream, score_out, score_stride);

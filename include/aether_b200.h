@@ -106,7 +106,10 @@ int aether_hca_compress(const void* buffer_c, const void* buffer_z, void* out, i
  *   diag_idx [64] / diag_kv [128] Rademacher diagonals.
  * out [B,H,128] bf16 (attention output before the inverse output RoPE),
  * sel_out [B,top_k] int32 selected block ids ascending, -1 padded (may be NULL).
- * cluster: 0 = one CTA per sequence, 4 or 8 = thread-block cluster per sequence.
+ * workspace: aether_csa_decode_workspace_bytes(B, max_nblocks) bytes of device
+ * memory for per-block score keys (cluster 0 only; contents need no clearing).
+ * cluster: 0 = score kernel + select/attend kernel (default); 4 or 8 = one
+ * thread-block cluster per sequence.
  * pdl: 1 = programmatic dependent launch; the kernel then reads page_table,
  * nblocks, window_len, cache pages and all window rows but the newest before
  * the previous kernel in the stream has completed. */
@@ -115,7 +118,7 @@ int aether_csa_decode_paged(const void* q, const float* index_q, const float* in
                             const uint8_t* kv_pages, const int32_t* page_table, int table_stride, int num_pages,
                             const int32_t* nblocks, int max_nblocks, const float* diag_idx, const float* diag_kv,
                             int B, int H, int W, int bits, int top_k, float softmax_scale, void* out,
-                            int32_t* sel_out, int* err, int cluster, int pdl, void* stream);
+                            int32_t* sel_out, uint32_t* workspace, int* err, int cluster, int pdl, void* stream);
 
 /* As aether_csa_decode_paged, also writing each visible block's index score
  * to score_out[b * score_stride + block]. */
@@ -125,7 +128,8 @@ int aether_csa_decode_paged_scores(const void* q, const float* index_q, const fl
                                    int num_pages, const int32_t* nblocks, int max_nblocks, const float* diag_idx,
                                    const float* diag_kv, int B, int H, int W, int bits, int top_k,
                                    float softmax_scale, void* out, int32_t* sel_out, float* score_out,
-                                   int score_stride, int* err, int cluster, int pdl, void* stream);
+                                   int score_stride, uint32_t* workspace, int* err, int cluster, int pdl,
+                                   void* stream);
 
 /* One HCA decode step (replaces aether_2b/serving.py:507-522): attention over
  * every visible compressed block plus the window; nblocks <= 1024. */
@@ -134,7 +138,10 @@ int aether_hca_decode_paged(const void* q, const float* sink, const void* window
                             const int32_t* nblocks, int max_nblocks, const float* diag_kv, int B, int H, int W,
                             int bits, float softmax_scale, void* out, int* err, int cluster, void* stream);
 
-/* Shared-memory bytes of the one-CTA-per-sequence CSA decode kernel. */
+/* Workspace bytes of aether_csa_decode_paged (cluster 0). */
+size_t aether_csa_decode_workspace_bytes(int B, int max_nblocks);
+
+/* Shared-memory bytes of the select/attend CSA decode kernel. */
 int aether_csa_decode_smem_bytes(int bits);
 
 #ifdef __cplusplus
