@@ -75,6 +75,16 @@ SIGNATURES = {
     "aether_csa_decode_smem_bytes": (_c_int, [_c_int]),
     "aether_csa_decode_workspace_bytes": (ctypes.c_size_t, [_c_int, _c_int]),
     "aether_csa_decode_set_debug_timer": (None, [_p]),
+    "aether_csa_local_candidates": (
+        _c_int,
+        [_p, _p, _p, _p, _c_int, _c_int, _p, _c_int, _p, _c_int, _c_int, _c_int, _c_int, _p, _p, _p, _p, _p],
+    ),
+    "aether_csa_attend_candidates": (
+        _c_int,
+        [_p, _p, _p, _p, _p, _p, _c_int, _c_int, _p, _c_int, _p, _p, _p, _c_int, _c_int, _c_int,
+         _c_int, _c_int, _c_int, _c_int, _c_int, _c_f, _p, _p, _p, _p, _p, _p],
+    ),
+    "aether_lse_merge": (_c_int, [_p, _p, _p, _c_int, _c_int, _c_int, _p, _p]),
     "aether_hca_decode_paged": (
         _c_int,
         [

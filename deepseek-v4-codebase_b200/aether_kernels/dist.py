@@ -1,0 +1,139 @@
+"""Multi-device CSA decode.
+
+Two layouts (new design: the reference serves one sequence per process and
+only shards layers, aether_2b/serving.py:1053-1076):
+
+* request partitioning -- each rank decodes its own sequences with
+  ``csa_decode_paged``; no collective on the data path.
+* context partitioning (``csa_decode_context_parallel``) -- one long
+  sequence's compressed blocks are split into contiguous ranges, one per
+  rank.  Each rank keeps the exact top-k of every 8192-block chunk of its
+  range; the candidate lists are all-gathered (NCCL over NVLink) and every
+  rank takes the exact global top-k of the union (a global winner is always
+  in its own chunk's top-k; ties go to the lower block id on every rank);
+  each rank attends to the winners it holds (the last rank also to the
+  window) and the partial results (O, max, sum) are all-gathered and merged
+  by log-sum-exp with the sink counted once.
+
+The collective orchestration (``context_parallel_step``) takes the three
+compute steps as callables, so the same code runs with the CUDA kernels over
+NCCL and, in the CPU tests, with reference-math callables over gloo.
+"""
+from __future__ import annotations
+
+from typing import Callable, Optional, Tuple
+
+import torch
+import torch.distributed as dist
+
+from . import _lib
+from .ops import _check, _cuda, _stream, rademacher_diag
+from .paged import HEAD_DIM, INDEX_DIM, PAGE, TurboQuantPagedCache, csa_workspace_bytes
+
+CHUNK = 8192
+
+
+def chunks_for(max_nblocks: int) -> int:
+    return max(1, (max_nblocks + CHUNK - 1) // CHUNK)
+
+
+# ------------------------------------------------------------ device steps
+def local_candidates(index_q, index_weight, cache: TurboQuantPagedCache, page_table, nblocks, id_base: int,
+                     top_k: int = 256, err: Optional[torch.Tensor] = None) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Exact top_k of every 8192-block chunk of this device's blocks.
+
+    Returns (keys, ids), each int32 [B, chunks * top_k]; keys are the
+    order-preserving u32 score keys (bit patterns, 0 = padding), ids the
+    global block ids (ascending, -1 = padding)."""
+    B = index_q.shape[0]
+    max_nb = page_table.shape[1] * PAGE
+    ch = chunks_for(max_nb)
+    dev = index_q.device
+    keys = torch.empty(B, ch * top_k, dtype=torch.int32, device=dev)
+    ids = torch.empty(B, ch * top_k, dtype=torch.int32, device=dev)
+    ws = torch.empty(max(csa_workspace_bytes(B, max_nb), 16), dtype=torch.uint8, device=dev)
+    _lib.call("aether_csa_local_candidates", index_q.data_ptr(), index_weight.data_ptr(), cache.idx_pages.data_ptr(),
+              page_table.data_ptr(), page_table.shape[1], cache.num_pages, nblocks.data_ptr(), max_nb,
+              rademacher_diag(INDEX_DIM, cache.seed, dev).data_ptr(), B, cache.bits, int(top_k), int(id_base),
+              keys.data_ptr(), ids.data_ptr(), ws.data_ptr(), None if err is None else err.data_ptr(), _stream(dev))
+    return keys, ids
+
+
+def attend_candidates(q, sink, window, window_len, cache: TurboQuantPagedCache, page_table, nblocks, cand_keys,
+                      cand_ids, id_base: int, softmax_scale: float, top_k: int = 256, partial: bool = True,
+                      err: Optional[torch.Tensor] = None):
+    """Exact top_k of the merged candidates, attention over the winners held
+    here.  partial=True returns (part_o fp32 [B,H,128], part_ml fp32
+    [B,H,2], selected int32 [B,top_k]); otherwise (out bf16 [B,H,128], selected)."""
+    B, H, D = q.shape
+    _check(D == HEAD_DIM, f"head_dim must be {HEAD_DIM}")
+    dev = q.device
+    for t, nm in ((cand_keys, "cand_keys"), (cand_ids, "cand_ids")):
+        _cuda(t, nm)
+    n = cand_keys.shape[1]
+    sel = torch.empty(B, top_k, dtype=torch.int32, device=dev)
+    if partial:
+        po = torch.empty(B, H, D, dtype=torch.float32, device=dev)
+        pml = torch.empty(B, H, 2, dtype=torch.float32, device=dev)
+        out_ptr, po_ptr, pml_ptr = None, po.data_ptr(), pml.data_ptr()
+    else:
+        out = torch.empty(B, H, D, dtype=torch.bfloat16, device=dev)
+        out_ptr, po_ptr, pml_ptr = out.data_ptr(), None, None
+    _lib.call("aether_csa_attend_candidates", q.data_ptr(), sink.data_ptr(), window.data_ptr(), window_len.data_ptr(),
+              cache.kv_pages.data_ptr(), page_table.data_ptr(), page_table.shape[1], cache.num_pages,
+              nblocks.data_ptr(), page_table.shape[1] * PAGE, rademacher_diag(HEAD_DIM, cache.seed, dev).data_ptr(),
+              cand_keys.data_ptr(), cand_ids.data_ptr(), n, n, int(id_base), B, H, window.shape[1], cache.bits,
+              int(top_k), float(softmax_scale), out_ptr, sel.data_ptr(), po_ptr, pml_ptr,
+              None if err is None else err.data_ptr(), _stream(dev))
+    return (po, pml, sel) if partial else (out, sel)
+
+
+def lse_merge(part_o: torch.Tensor, part_ml: torch.Tensor, sink: torch.Tensor) -> torch.Tensor:
+    """part_o [G,B,H,128] fp32, part_ml [G,B,H,2] fp32, sink [H] fp32 -> bf16 [B,H,128]."""
+    G, B, H, D = part_o.shape
+    out = torch.empty(B, H, D, dtype=torch.bfloat16, device=part_o.device)
+    _lib.call("aether_lse_merge", part_o.contiguous().data_ptr(), part_ml.contiguous().data_ptr(), sink.data_ptr(),
+              G, B, H, out.data_ptr(), _stream(part_o.device))
+    return out
+
+
+# ---------------------------------------------------------- orchestration
+def context_parallel_step(candidates_fn: Callable[[], Tuple[torch.Tensor, torch.Tensor]],
+                          attend_fn: Callable[[torch.Tensor, torch.Tensor], Tuple[torch.Tensor, torch.Tensor,
+                                                                                  torch.Tensor]],
+                          merge_fn: Callable[[torch.Tensor, torch.Tensor], torch.Tensor],
+                          group=None):
+    """One context-parallel decode step.  candidates_fn() -> (keys, ids) of
+    this rank; attend_fn(all_keys, all_ids) -> (part_o, part_ml, selected);
+    merge_fn(stacked part_o, stacked part_ml) -> output.  Candidate lists are
+    concatenated in rank order, so ids stay ascending when rank r holds the
+    r-th contiguous block range."""
+    world = dist.get_world_size(group)
+    keys, ids = candidates_fn()
+    kl = [torch.empty_like(keys) for _ in range(world)]
+    il = [torch.empty_like(ids) for _ in range(world)]
+    dist.all_gather(kl, keys.contiguous(), group=group)
+    dist.all_gather(il, ids.contiguous(), group=group)
+    all_keys = torch.cat(kl, dim=1).contiguous()
+    all_ids = torch.cat(il, dim=1).contiguous()
+    po, pml, sel = attend_fn(all_keys, all_ids)
+    pol = [torch.empty_like(po) for _ in range(world)]
+    pmll = [torch.empty_like(pml) for _ in range(world)]
+    dist.all_gather(pol, po.contiguous(), group=group)
+    dist.all_gather(pmll, pml.contiguous(), group=group)
+    return merge_fn(torch.stack(pol), torch.stack(pmll)), sel
+
+
+def csa_decode_context_parallel(q, index_q, index_weight, sink, window, window_len, cache: TurboQuantPagedCache,
+                                page_table, nblocks, id_base: int, softmax_scale: float, top_k: int = 256,
+                                group=None, err: Optional[torch.Tensor] = None):
+    """CSA decode for sequences whose blocks are split across the ranks of
+    ``group``: this rank holds global blocks [id_base, id_base + nblocks[b]).
+    ``window_len`` is 0 on every rank but the one holding the window.
+    Returns (out bf16 [B,H,128], selected global block ids [B,top_k])."""
+    return context_parallel_step(
+        lambda: local_candidates(index_q, index_weight, cache, page_table, nblocks, id_base, top_k, err),
+        lambda k, i: attend_candidates(q, sink, window, window_len, cache, page_table, nblocks, k, i, id_base,
+                                       softmax_scale, top_k, partial=True, err=err),
+        lambda po, pml: lse_merge(po, pml, sink),
+        group=group)

@@ -45,7 +45,8 @@ constexpr int kMaxTopK = 256;
 constexpr int kWinMax = 128;
 constexpr int kWRow = kHeadDim * 2 + 16;  // padded bf16 window row (bytes)
 constexpr int kL1Bins = 4096;             // histogram of key >> 19
-constexpr int kRankMax = 512;             // boundary-bin size ranked exactly
+constexpr int kMaxPagesLocal = 4096;      // page-table entries per sequence on one device (262144 blocks)
+constexpr int kMaxBlocks = kMaxPagesLocal * kPage;
 
 template <int BITS>
 struct QCfg {
@@ -75,9 +76,10 @@ struct QCfg {
   static constexpr int REGION = A_END > S_END ? A_END : S_END;
 
   static constexpr int OFF_WIN = REGION;                     // bf16 [128][kWRow]
-  static constexpr int OFF_PT = OFF_WIN + kWinMax * kWRow;   // i32 [128]
-  static constexpr int OFF_SEL = OFF_PT + (kMaxKeys / kPage) * 4;  // i32 [256]
-  static constexpr int OFF_SCAN = OFF_SEL + kMaxTopK * 4;     // u32 [64]
+  static constexpr int OFF_PT = OFF_WIN + kWinMax * kWRow;   // i32 [kMaxPagesLocal]
+  static constexpr int OFF_SEL = OFF_PT + kMaxPagesLocal * 4;  // i32 [256] positions
+  static constexpr int OFF_OWN = OFF_SEL + kMaxTopK * 4;     // i32 [256] local block ids attended here
+  static constexpr int OFF_SCAN = OFF_OWN + kMaxTopK * 4;     // u32 [64]
   static constexpr int OFF_MISC = OFF_SCAN + 64 * 4;
   static constexpr int MISC_BYTES = 512;
   static constexpr int SMEM = OFF_MISC + MISC_BYTES;
@@ -117,6 +119,23 @@ struct QParams {
   int score_stride;
   uint32_t* ws;    // [B][ws_stride] per-block score keys (kernel A -> kernel B)
   int ws_stride;
+  // selection source of the attend kernel: the workspace row (implicit ids,
+  // `chunks` CTAs per sequence each taking 8192 blocks) or an explicit
+  // candidate list [B][cand_stride] of keys and ascending global ids
+  int chunks;
+  const uint32_t* cand_keys;
+  const int32_t* cand_ids;
+  int cand_n, cand_stride;
+  // select-only output: top_k (key, id) per CTA, [B * chunks][top_k]
+  uint32_t* sel_keys_out;
+  int32_t* sel_ids_out;
+  int sel_stride;  // row stride of the select-only output (multiple of 4)
+  // this device holds blocks [id_base, id_base + nblocks[b]) of sequence b
+  int id_base;
+  // partial output for a cross-device merge: un-normalised O [B][H][128]
+  // and (max logit, sum) [B][H][2]; the sink is left to the merge
+  float* part_o;
+  float* part_ml;
   long long* dbg;  // per-CTA phase timestamps [grid][16] (profiling aid), or null
   int* err;
   int table_stride, num_pages, H, W, top_k;
@@ -136,6 +155,8 @@ struct QMisc {
   uint32_t ncand;
   uint32_t thr;
   uint32_t take_eq;
+  uint32_t nvalid;
+  uint32_t nown;
   float m_h[kMaxHeads];
   float l_h[kMaxHeads];
 };
@@ -324,7 +345,7 @@ __global__ void __launch_bounds__(kSThreads) csa_score_kernel(QParams p, int spl
   const int g = lane >> 2, t = lane & 3;
   pdl_launch_dependents();
   int nb = p.nblocks[b];
-  nb = max(0, min(nb, min(kMaxKeys, p.table_stride * kPage)));
+  nb = max(0, min(nb, min(kMaxBlocks, p.table_stride * kPage)));
   const int npages = (nb + kPage - 1) / kPage;
   const int pg0 = sp * C::PPC;
   if (pg0 >= npages) return;
@@ -464,9 +485,10 @@ template <int BITS>
 __global__ void __launch_bounds__(kQThreads, 1) csa_attend_kernel(QParams p) {
   using C = QCfg<BITS>;
   extern __shared__ __align__(128) uint8_t smem[];
-  const int b = blockIdx.x;
+  const int b = blockIdx.x / p.chunks, chunk = blockIdx.x % p.chunks;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, t = lane & 3;
+  const bool select_only = p.sel_keys_out != nullptr;
   auto stamp = [&](int slot, bool who) {
     if (p.dbg && who) {
       long long ts;
@@ -482,31 +504,36 @@ __global__ void __launch_bounds__(kQThreads, 1) csa_attend_kernel(QParams p) {
   uint32_t* hist = reinterpret_cast<uint32_t*>(smem + C::S_HIST);
   int32_t* pt = reinterpret_cast<int32_t*>(smem + C::OFF_PT);
   int32_t* sel = reinterpret_cast<int32_t*>(smem + C::OFF_SEL);
+  int32_t* own = reinterpret_cast<int32_t*>(smem + C::OFF_OWN);
   uint32_t* wtot = reinterpret_cast<uint32_t*>(smem + C::OFF_SCAN);
   QMisc* misc = reinterpret_cast<QMisc*>(smem + C::OFF_MISC);
 
   // ------------------------------------------------------------ prologue
-  int nb = p.nblocks[b];
-  if (nb > kMaxKeys || nb > p.table_stride * kPage) {
+  int nb = p.nblocks[b];  // blocks of sequence b held on this device
+  if (nb > kMaxBlocks || nb > p.table_stride * kPage) {
     if (tid == 0) report_error(p.err, kErrBadShape);
-    nb = min(kMaxKeys, p.table_stride * kPage);
+    nb = min(kMaxBlocks, p.table_stride * kPage);
   }
   nb = max(nb, 0);
-  const int K = min(p.top_k, nb);
+  const bool explicit_list = p.cand_keys != nullptr;
+  // keys this CTA selects from: positions 0..n-1, in ascending block-id order
+  const int n = explicit_list ? min(p.cand_n, kMaxKeys) : max(0, min(nb - chunk * kMaxKeys, kMaxKeys));
   const int npages = (nb + kPage - 1) / kPage;
   const int W = p.W;
-  const int wl = max(0, min(p.window_len[b], W));
-  const int32_t* ptab = p.page_table + static_cast<long long>(b) * p.table_stride;
-  for (int i = tid; i < npages; i += kQThreads) {
-    int v = ptab[i];
-    if (v < 0 || v >= p.num_pages) {
-      report_error(p.err, kErrBadPage);
-      v = 0;
+  const int wl = select_only ? 0 : max(0, min(p.window_len[b], W));
+  if (!select_only) {
+    const int32_t* ptab = p.page_table + static_cast<long long>(b) * p.table_stride;
+    for (int i = tid; i < npages; i += kQThreads) {
+      int v = ptab[i];
+      if (v < 0 || v >= p.num_pages) {
+        report_error(p.err, kErrBadPage);
+        v = 0;
+      }
+      pt[i] = v;
     }
-    pt[i] = v;
   }
   for (int i = tid; i < kL1Bins; i += kQThreads) hist[i] = 0;
-  if (tid < kMaxTopK) sel[tid] = 0;  // every slot holds a valid block id
+  if (tid < kMaxTopK) sel[tid] = 0;  // every slot holds a valid position
   if (tid == 0) {
     misc->thr = 0;
     misc->take_eq = 0xFFFFFFFFu;
@@ -514,6 +541,8 @@ __global__ void __launch_bounds__(kQThreads, 1) csa_attend_kernel(QParams p) {
     misc->bin = 0;
     misc->above = 0;
     misc->cnt = 0;
+    misc->nvalid = 0;
+    misc->nown = 0;
   }
   // window rows other than the newest are cache state: prefetch them now
   {
@@ -524,39 +553,50 @@ __global__ void __launch_bounds__(kQThreads, 1) csa_attend_kernel(QParams p) {
     asm volatile("cp.async.commit_group;" ::: "memory");
   }
   stamp(1, tid == 0);
-  // the block keys come from the score kernel
+  // the block keys come from the score kernel (or a previous select)
   pdl_wait();
   stamp(2, tid == 0);
-  constexpr int PER = kMaxKeys / kQThreads;  // 16 keys per thread, in index order
+  constexpr int PER = kMaxKeys / kQThreads;  // 16 keys per thread, in source order
   const int i0 = tid * PER;
   uint32_t kr[PER];
   {
-    const uint32_t* src = p.ws + static_cast<long long>(b) * p.ws_stride + i0;
+    const uint32_t* src = explicit_list ? p.cand_keys + static_cast<long long>(b) * p.cand_stride + i0
+                                        : p.ws + static_cast<long long>(b) * p.ws_stride + chunk * kMaxKeys + i0;
 #pragma unroll
     for (int v = 0; v < PER / 4; ++v) {
       uint4 x = make_uint4(0, 0, 0, 0);
-      if (i0 + 4 * v < nb) x = __ldcg(reinterpret_cast<const uint4*>(src) + v);
+      if (i0 + 4 * v < n) x = __ldcg(reinterpret_cast<const uint4*>(src) + v);
       kr[4 * v] = x.x; kr[4 * v + 1] = x.y; kr[4 * v + 2] = x.z; kr[4 * v + 3] = x.w;
     }
+    uint32_t cnt = 0;
 #pragma unroll
     for (int j = 0; j < PER; ++j) {
-      kr[j] = i0 + j < nb ? kr[j] : 0u;
-      if (i0 + j < nb) atomicAdd(&hist[kr[j] >> 19], 1u);
+      kr[j] = i0 + j < n ? kr[j] : 0u;  // key 0 = no block
+      if (kr[j]) {
+        atomicAdd(&hist[kr[j] >> 19], 1u);
+        ++cnt;
+      }
     }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) cnt += __shfl_xor_sync(0xffffffffu, cnt, o);
+    if (lane == 0 && cnt) atomicAdd(&misc->nvalid, cnt);
 #pragma unroll
     for (int v = 0; v < PER / 4; ++v)
       *reinterpret_cast<uint4*>(scores + i0 + 4 * v) = make_uint4(kr[4 * v], kr[4 * v + 1], kr[4 * v + 2], kr[4 * v + 3]);
   }
   __syncthreads();
   stamp(3, tid == 0);
-  if (p.score_out) {
-    float* so = p.score_out + static_cast<long long>(b) * p.score_stride;
-    for (int i = tid; i < nb; i += kQThreads) so[i] = __uint_as_float(scores[i] - 1u);
+  const int nvalid = static_cast<int>(misc->nvalid);
+  const int K = min(p.top_k, nvalid);
+  if (p.score_out && !explicit_list) {
+    float* so = p.score_out + static_cast<long long>(b) * p.score_stride + chunk * kMaxKeys;
+    for (int i = tid; i < n; i += kQThreads) so[i] = __uint_as_float(scores[i] - 1u);
   }
 
   // ------------------------------------------------------------- select
-  // Result: every key > thr is taken, and the take_eq lowest-index keys == thr.
-  if (nb > K) {
+  // Result: every key > thr is taken, and the take_eq lowest-position keys
+  // == thr.  Keys are >= 1 for real blocks, so thr = 0 takes all of them.
+  if (nvalid > K) {
     uint32_t R = static_cast<uint32_t>(K);
     find_bin(hist, kL1Bins, R, wtot, misc, tid, lane, warp);
     const uint32_t b1 = misc->bin;
@@ -565,15 +605,15 @@ __global__ void __launch_bounds__(kQThreads, 1) csa_attend_kernel(QParams p) {
       if (tid == 0) misc->thr = b1 << 19;  // lowest key of bin b1: the whole bin is taken
     } else {
       // refine inside bin b1 over its keys only: bits 18..8, then 7..0
-      uint32_t* cand = reinterpret_cast<uint32_t*>(smem + C::S_CAND);  // keys of bin b1
+      uint32_t* cand = reinterpret_cast<uint32_t*>(smem + C::S_CAND);
       uint32_t mine = 0;
 #pragma unroll
-      for (int j = 0; j < PER; ++j) mine += (kr[j] >> 19) == b1 && i0 + j < nb;
+      for (int j = 0; j < PER; ++j) mine += kr[j] != 0u && (kr[j] >> 19) == b1;
       uint32_t off = 0;
       if (mine) off = atomicAdd(&misc->ncand, mine);
 #pragma unroll
       for (int j = 0; j < PER; ++j) {
-        const bool m = (kr[j] >> 19) == b1 && i0 + j < nb;
+        const bool m = kr[j] != 0u && (kr[j] >> 19) == b1;
         if (m) cand[off] = kr[j];
         off += m;
       }
@@ -597,22 +637,21 @@ __global__ void __launch_bounds__(kQThreads, 1) csa_attend_kernel(QParams p) {
         R -= misc->above;
         if (tid == 0) {
           misc->thr = (b1 << 19) | (b2 << 8) | static_cast<uint32_t>(misc->bin);
-          misc->take_eq = R;  // keys equal to thr: the lowest-index R of them
+          misc->take_eq = R;  // keys equal to thr: the lowest-position R of them
         }
       }
     }
   }
   __syncthreads();
   stamp(4, tid == 0);
-  // ordered compaction from registers: thread order is block-index order
+  // ordered compaction from registers: thread order is source order
   {
     const uint32_t thr = misc->thr, take_eq = misc->take_eq;
     uint32_t cs = 0, ce = 0;
 #pragma unroll
     for (int j = 0; j < PER; ++j) {
-      const bool valid = i0 + j < nb;
-      cs += valid && kr[j] > thr;
-      ce += valid && kr[j] == thr;
+      cs += kr[j] != 0u && kr[j] > thr;
+      ce += kr[j] != 0u && kr[j] == thr;
     }
     const uint32_t packed = cs | (ce << 16);
     const uint32_t exc = block_scan_incl(packed, wtot, lane, warp) - packed;
@@ -620,8 +659,7 @@ __global__ void __launch_bounds__(kQThreads, 1) csa_attend_kernel(QParams p) {
     if (cs | ce) {
 #pragma unroll
       for (int j = 0; j < PER; ++j) {
-        const bool valid = i0 + j < nb;
-        const bool st = valid && kr[j] > thr, eq = valid && kr[j] == thr;
+        const bool st = kr[j] != 0u && kr[j] > thr, eq = kr[j] != 0u && kr[j] == thr;
         const uint32_t pos = st ? sb + min(eb, take_eq) : sb + eb;
         if ((st || (eq && eb < take_eq)) && pos < static_cast<uint32_t>(K)) sel[pos] = i0 + j;
         sb += st;
@@ -631,10 +669,41 @@ __global__ void __launch_bounds__(kQThreads, 1) csa_attend_kernel(QParams p) {
   }
   __syncthreads();
   stamp(5, tid == 0);
+  // global block id of a source position
+  const int32_t* cids = explicit_list ? p.cand_ids + static_cast<long long>(b) * p.cand_stride : nullptr;
+  auto gid_of = [&](int pos) -> int {
+    return explicit_list ? cids[pos] : p.id_base + chunk * kMaxKeys + pos;
+  };
+  if (select_only) {
+    const long long o = static_cast<long long>(blockIdx.x) * p.sel_stride;
+    for (int i = tid; i < p.sel_stride; i += kQThreads) {
+      p.sel_keys_out[o + i] = i < K ? scores[sel[i]] : 0u;
+      p.sel_ids_out[o + i] = i < K ? gid_of(sel[i]) : -1;
+    }
+    return;
+  }
   if (p.sel_out) {
     int32_t* so = p.sel_out + static_cast<long long>(b) * p.top_k;
-    for (int i = tid; i < p.top_k; i += kQThreads) so[i] = i < K ? sel[i] : -1;
+    for (int i = tid; i < p.top_k; i += kQThreads) so[i] = i < K ? gid_of(sel[i]) : -1;
   }
+  // the selected blocks held on this device, as local ids (order kept)
+  if (warp == 0) {
+    uint32_t base = 0;
+    for (int r0 = 0; r0 < K; r0 += 32) {
+      const int i = r0 + lane;
+      int loc = -1;
+      if (i < K) {
+        const int gidv = gid_of(sel[i]);
+        if (gidv >= p.id_base && gidv < p.id_base + nb) loc = gidv - p.id_base;
+      }
+      const uint32_t bal = __ballot_sync(0xffffffffu, loc >= 0);
+      if (loc >= 0) own[base + __popc(bal & ((1u << lane) - 1))] = loc;
+      base += __popc(bal);
+    }
+    if (lane == 0) misc->nown = base;
+  }
+  __syncthreads();
+  const int KO = static_cast<int>(misc->nown);
 
   // --------------------------------------------------------- attention
   // (the select-phase buffers are dead from here on)
@@ -646,12 +715,12 @@ __global__ void __launch_bounds__(kQThreads, 1) csa_attend_kernel(QParams p) {
   float* logit = reinterpret_cast<float*>(smem + C::A_LOG);
   __half* P = reinterpret_cast<__half*>(smem + C::A_P);
   float* Obuf = reinterpret_cast<float*>(smem + C::A_O);
-  const int ntc = (K + 15) / 16, ntw = (wl + 15) / 16;
+  const int ntc = (KO + 15) / 16, ntw = (wl + 15) / 16;
   {
     constexpr int CPR = C::RB_KV / 16;
-    for (int i = tid; i < K * CPR; i += kQThreads) {
+    for (int i = tid; i < KO * CPR; i += kQThreads) {
       const int row = i / CPR, ch = i % CPR;
-      const int blk = min(max(sel[row], 0), max(nb - 1, 0));
+      const int blk = min(max(own[row], 0), max(nb - 1, 0));
       const uint8_t* pg = p.kv_pages + static_cast<long long>(pt[blk >> 6]) * C::PB_KV;
       cp_async16(raw + row * C::RAWS + ch * 16, pg + (blk & 63) * C::RB_KV + ch * 16);
       if (ch == 0) cp_async4(ks + row, pg + kPage * C::RB_KV + (blk & 63) * 4);
@@ -692,7 +761,7 @@ __global__ void __launch_bounds__(kQThreads, 1) csa_attend_kernel(QParams p) {
   for (int i = tid; i < ntc * 16 * 16; i += kQThreads) {
     const int row = i >> 4, c8 = (i & 15) * 8;
     uint4 o = make_uint4(0, 0, 0, 0);
-    if (row < K) {
+    if (row < KO) {
       if (BITS == 4) {
         const uint32_t w = *reinterpret_cast<const uint32_t*>(raw + row * C::RAWS + c8 / 2);
         o = make_uint4(nib_byte_to_h2(w & 0xFFu), nib_byte_to_h2((w >> 8) & 0xFFu), nib_byte_to_h2((w >> 16) & 0xFFu),
@@ -744,8 +813,8 @@ __global__ void __launch_bounds__(kQThreads, 1) csa_attend_kernel(QParams p) {
           const int src = tile * 16 + nt * 8 + 2 * t;
           float z0 = acc[nt][e] + acc2[nt][e], z1 = acc[nt][e + 1] + acc2[nt][e + 1];
           if (comp) {
-            z0 = src < K ? z0 * ks[src] * p.softmax_scale : -INFINITY;
-            z1 = src + 1 < K ? z1 * ks[src + 1] * p.softmax_scale : -INFINITY;
+            z0 = src < KO ? z0 * ks[src] * p.softmax_scale : -INFINITY;
+            z1 = src + 1 < KO ? z1 * ks[src + 1] * p.softmax_scale : -INFINITY;
           } else {
             z0 = (src - ntc * 16) < wl ? z0 * p.softmax_scale : -INFINITY;
             z1 = (src + 1 - ntc * 16) < wl ? z1 * p.softmax_scale : -INFINITY;
@@ -822,14 +891,11 @@ __global__ void __launch_bounds__(kQThreads, 1) csa_attend_kernel(QParams p) {
   }
   __syncthreads();
   stamp(9, tid == 0);
-  // ---- per head: inverse rotation, sink, normalise, store
+  // ---- per head: inverse rotation, then either the final sink-normalised
+  // bf16 output or the partial (O, max, sum) for a cross-device merge
   if (warp < p.H) {
     const int h = warp;
     const float m = misc->m_h[h], l = misc->l_h[h];
-    const float sk = p.sink[h];
-    const float M = fmaxf(m, sk);
-    const float a = m == -INFINITY ? 0.f : __expf(m - M);
-    const float inv = a / (l * a + __expf(sk - M));
     const float4 o1 = *reinterpret_cast<const float4*>(Obuf + h * kHeadDim + lane * 4);
     const float4 o2 = *reinterpret_cast<const float4*>(Obuf + 16 * kHeadDim + h * kHeadDim + lane * 4);
     float vr[4] = {o1.x, o1.y, o1.z, o1.w};
@@ -837,73 +903,105 @@ __global__ void __launch_bounds__(kQThreads, 1) csa_attend_kernel(QParams p) {
     warp_wht128(vr, lane);
     float o[4];
 #pragma unroll
-    for (int k = 0; k < 4; ++k) o[k] = (vr[k] * 0.0883883461356163f * p.diag_kv[lane * 4 + k] + vw[k]) * inv;
-    __nv_bfloat162 o01 = __floats2bfloat162_rn(o[0], o[1]), o23 = __floats2bfloat162_rn(o[2], o[3]);
-    *reinterpret_cast<uint2*>(p.out + (static_cast<long long>(b) * p.H + h) * kHeadDim + lane * 4) =
-        make_uint2(*reinterpret_cast<uint32_t*>(&o01), *reinterpret_cast<uint32_t*>(&o23));
+    for (int k = 0; k < 4; ++k) o[k] = vr[k] * 0.0883883461356163f * p.diag_kv[lane * 4 + k] + vw[k];
+    if (p.part_o) {
+      *reinterpret_cast<float4*>(p.part_o + (static_cast<long long>(b) * p.H + h) * kHeadDim + lane * 4) =
+          make_float4(o[0], o[1], o[2], o[3]);
+      if (lane == 0)
+        *reinterpret_cast<float2*>(p.part_ml + (static_cast<long long>(b) * p.H + h) * 2) = make_float2(m, l);
+    } else {
+      const float sk = p.sink[h];
+      const float M = fmaxf(m, sk);
+      const float a = m == -INFINITY ? 0.f : __expf(m - M);
+      const float inv = a / (l * a + __expf(sk - M));
+      __nv_bfloat162 o01 = __floats2bfloat162_rn(o[0] * inv, o[1] * inv), o23 = __floats2bfloat162_rn(o[2] * inv, o[3] * inv);
+      *reinterpret_cast<uint2*>(p.out + (static_cast<long long>(b) * p.H + h) * kHeadDim + lane * 4) =
+          make_uint2(*reinterpret_cast<uint32_t*>(&o01), *reinterpret_cast<uint32_t*>(&o23));
+    }
   }
   stamp(10, tid == 0);
 }
 
 
 template <int BITS>
-static int launch_split(const QParams& p, int B, int max_nblocks, bool pdl, cudaStream_t st) {
-  using CA = SCfg<BITS>;
-  using CB = QCfg<BITS>;
-  auto ka = csa_score_kernel<BITS>;
-  auto kb = csa_attend_kernel<BITS>;
-  static bool attr = false;
-  if (!attr) {
-    AETHER_CUDA_TRY(cudaFuncSetAttribute(ka, cudaFuncAttributeMaxDynamicSharedMemorySize, CA::SMEM),
+static int set_smem_attrs() {
+  static bool done = false;
+  if (!done) {
+    AETHER_CUDA_TRY(cudaFuncSetAttribute(csa_score_kernel<BITS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         SCfg<BITS>::SMEM),
                     "csa_decode: set shared memory size (score)");
-    AETHER_CUDA_TRY(cudaFuncSetAttribute(kb, cudaFuncAttributeMaxDynamicSharedMemorySize, CB::SMEM),
+    AETHER_CUDA_TRY(cudaFuncSetAttribute(csa_attend_kernel<BITS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         QCfg<BITS>::SMEM),
                     "csa_decode: set shared memory size (attend)");
-    attr = true;
+    done = true;
   }
+  return 0;
+}
+
+static cudaLaunchAttribute g_pdl_attr = [] {
+  cudaLaunchAttribute a;
+  a.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  a.val.programmaticStreamSerializationAllowed = 1;
+  return a;
+}();
+
+template <int BITS>
+static int launch_score(const QParams& p, int B, int max_nblocks, bool pdl, cudaStream_t st) {
+  using CA = SCfg<BITS>;
   const int max_pages = (max_nblocks + kPage - 1) / kPage;
   const int splits = max(1, (max_pages + CA::PPC - 1) / CA::PPC);
-  cudaLaunchAttribute at[1];
-  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  at[0].val.programmaticStreamSerializationAllowed = 1;
-  cudaLaunchConfig_t ca = {};
-  ca.gridDim = dim3(B * splits);
-  ca.blockDim = dim3(kSThreads);
-  ca.dynamicSmemBytes = CA::SMEM;
-  ca.stream = st;
-  ca.attrs = at;
-  ca.numAttrs = pdl ? 1 : 0;
-  AETHER_CUDA_TRY(cudaLaunchKernelEx(&ca, ka, p, splits), "csa_decode: launch (score)");
-  // the attend kernel always overlaps its prologue with the score kernel,
-  // which writes nothing that prologue reads
-  cudaLaunchConfig_t cb = {};
-  cb.gridDim = dim3(B);
-  cb.blockDim = dim3(kQThreads);
-  cb.dynamicSmemBytes = CB::SMEM;
-  cb.stream = st;
-  cb.attrs = at;
-  cb.numAttrs = 1;
-  AETHER_CUDA_TRY(cudaLaunchKernelEx(&cb, kb, p), "csa_decode: launch (attend)");
-  return check_launch("csa_decode");
+  cudaLaunchConfig_t c = {};
+  c.gridDim = dim3(B * splits);
+  c.blockDim = dim3(kSThreads);
+  c.dynamicSmemBytes = CA::SMEM;
+  c.stream = st;
+  c.attrs = &g_pdl_attr;
+  c.numAttrs = pdl ? 1 : 0;
+  AETHER_CUDA_TRY(cudaLaunchKernelEx(&c, csa_score_kernel<BITS>, p, splits), "csa_decode: launch (score)");
+  return 0;
+}
+
+template <int BITS>
+static int launch_attend(const QParams& p, int B, bool pdl, cudaStream_t st) {
+  cudaLaunchConfig_t c = {};
+  c.gridDim = dim3(B * p.chunks);
+  c.blockDim = dim3(kQThreads);
+  c.dynamicSmemBytes = QCfg<BITS>::SMEM;
+  c.stream = st;
+  c.attrs = &g_pdl_attr;
+  c.numAttrs = pdl ? 1 : 0;
+  AETHER_CUDA_TRY(cudaLaunchKernelEx(&c, csa_attend_kernel<BITS>, p), "csa_decode: launch (attend)");
+  return 0;
 }
 
 static long long* g_cta_debug = nullptr;
 
-int csa_decode_cta(const void* q, const float* index_q, const float* index_w, const float* sink, const void* window,
-                   const int32_t* window_len, const uint8_t* idx_pages, const uint8_t* kv_pages,
-                   const int32_t* page_table, int table_stride, int num_pages, const int32_t* nblocks,
-                   int max_nblocks, const float* diag_idx, const float* diag_kv, int B, int H, int W, int bits,
-                   int top_k, float softmax_scale, void* out, int32_t* sel_out, float* score_out, int score_stride,
-                   uint32_t* workspace, int* err, int pdl, void* stream) {
+// workspace layout: u32 keys [B][ws_stride], then candidate keys / ids
+// [B][chunks * kMaxTopK] each (only for sequences longer than 8192 blocks)
+static size_t workspace_bytes(int B, int max_nblocks) {
+  const size_t keys = static_cast<size_t>(B) * csa_workspace_stride(max_nblocks) * 4;
+  const int chunks = (max_nblocks + kMaxKeys - 1) / kMaxKeys;
+  const size_t cand = chunks > 1 ? static_cast<size_t>(B) * chunks * kMaxTopK * 8 : 0;  // sel_stride <= 256
+  return keys + cand;
+}
+
+static int check_common(int bits, int H, int W, int top_k, int max_nblocks, int table_stride, int num_pages) {
   AETHER_REQUIRE(bits == 4 || bits == 8, "bits must be 4 or 8, got %d", bits);
   AETHER_REQUIRE(H >= 1 && H <= kMaxHeads, "num_heads must be in [1, %d], got %d", kMaxHeads, H);
   AETHER_REQUIRE(W >= 0 && W <= kWinMax, "window capacity must be in [0, %d], got %d", kWinMax, W);
   AETHER_REQUIRE(top_k >= 1 && top_k <= kMaxTopK, "top_k must be in [1, %d], got %d", kMaxTopK, top_k);
-  AETHER_REQUIRE(max_nblocks >= 0 && max_nblocks <= kMaxKeys,
-                 "csa decode: %d visible blocks exceed the per-query limit %d", max_nblocks, kMaxKeys);
+  AETHER_REQUIRE(max_nblocks >= 0 && max_nblocks <= kMaxBlocks,
+                 "csa decode: %d visible blocks exceed the per-device limit %d", max_nblocks, kMaxBlocks);
   AETHER_REQUIRE(table_stride >= 1 && num_pages >= 1, "page table / pool must be non-empty");
-  AETHER_REQUIRE(workspace != nullptr, "csa decode: workspace is required");
-  if (B == 0) return 0;
-  QParams p;
+  return 0;
+}
+
+static QParams base_params(const void* q, const float* index_q, const float* index_w, const float* sink,
+                           const void* window, const int32_t* window_len, const uint8_t* idx_pages,
+                           const uint8_t* kv_pages, const int32_t* page_table, int table_stride, int num_pages,
+                           const int32_t* nblocks, int max_nblocks, const float* diag_idx, const float* diag_kv,
+                           int H, int W, int top_k, float softmax_scale, int* err) {
+  QParams p{};
   p.q = static_cast<const __nv_bfloat16*>(q);
   p.index_q = index_q;
   p.index_w = index_w;
@@ -916,12 +1014,8 @@ int csa_decode_cta(const void* q, const float* index_q, const float* index_w, co
   p.nblocks = nblocks;
   p.diag_idx = diag_idx;
   p.diag_kv = diag_kv;
-  p.out = static_cast<__nv_bfloat16*>(out);
-  p.sel_out = sel_out;
-  p.score_out = score_out;
-  p.score_stride = score_stride;
-  p.ws = workspace;
   p.ws_stride = csa_workspace_stride(max_nblocks);
+  p.chunks = 1;
   p.dbg = g_cta_debug;
   p.err = err;
   p.table_stride = table_stride;
@@ -930,11 +1024,101 @@ int csa_decode_cta(const void* q, const float* index_q, const float* index_w, co
   p.W = W;
   p.top_k = top_k;
   p.softmax_scale = softmax_scale;
+  return p;
+}
+
+template <int BITS>
+static int run_decode(QParams p, int B, int max_nblocks, bool pdl, cudaStream_t st, uint8_t* workspace) {
+  int rc = set_smem_attrs<BITS>();
+  if (rc) return rc;
+  p.ws = reinterpret_cast<uint32_t*>(workspace);
+  rc = launch_score<BITS>(p, B, max_nblocks, pdl, st);
+  if (rc) return rc;
+  const int chunks = (max_nblocks + kMaxKeys - 1) / kMaxKeys;
+  if (chunks <= 1) return launch_attend<BITS>(p, B, true, st);
+  // long sequences: top-k per 8192-block chunk, then top-k of the chunk winners
+  uint32_t* ckeys = p.ws + static_cast<size_t>(B) * p.ws_stride;
+  int32_t* cids = reinterpret_cast<int32_t*>(ckeys + static_cast<size_t>(B) * chunks * kMaxTopK);
+  QParams ps = p;
+  ps.chunks = chunks;
+  ps.sel_keys_out = ckeys;
+  ps.sel_ids_out = cids;
+  ps.out = nullptr;
+  ps.sel_out = nullptr;
+  ps.score_out = nullptr;
+  ps.sel_stride = (p.top_k + 3) & ~3;
+  // candidate rows are laid out [B * chunks][sel_stride]; reread as [B][chunks * sel_stride]
+  rc = launch_attend<BITS>(ps, B, true, st);
+  if (rc) return rc;
+  QParams pa = p;
+  pa.cand_keys = ckeys;
+  pa.cand_ids = cids;
+  pa.cand_n = chunks * ps.sel_stride;
+  pa.cand_stride = chunks * ps.sel_stride;
+  pa.score_out = nullptr;
+  return launch_attend<BITS>(pa, B, true, st);
+}
+
+int csa_decode_cta(const void* q, const float* index_q, const float* index_w, const float* sink, const void* window,
+                   const int32_t* window_len, const uint8_t* idx_pages, const uint8_t* kv_pages,
+                   const int32_t* page_table, int table_stride, int num_pages, const int32_t* nblocks,
+                   int max_nblocks, const float* diag_idx, const float* diag_kv, int B, int H, int W, int bits,
+                   int top_k, float softmax_scale, void* out, int32_t* sel_out, float* score_out, int score_stride,
+                   uint32_t* workspace, int* err, int pdl, void* stream) {
+  int rc = check_common(bits, H, W, top_k, max_nblocks, table_stride, num_pages);
+  if (rc) return rc;
+  AETHER_REQUIRE(workspace != nullptr, "csa decode: workspace is required");
+  AETHER_REQUIRE(!score_out || max_nblocks <= kMaxKeys, "csa decode: score output is limited to %d blocks", kMaxKeys);
+  if (B == 0) return 0;
+  QParams p = base_params(q, index_q, index_w, sink, window, window_len, idx_pages, kv_pages, page_table, table_stride,
+                          num_pages, nblocks, max_nblocks, diag_idx, diag_kv, H, W, top_k, softmax_scale, err);
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.sel_out = sel_out;
+  p.score_out = score_out;
+  p.score_stride = score_stride;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  return bits == 4 ? launch_split<4>(p, B, max_nblocks, pdl != 0, st) : launch_split<8>(p, B, max_nblocks, pdl != 0, st);
+  rc = bits == 4 ? run_decode<4>(p, B, max_nblocks, pdl != 0, st, reinterpret_cast<uint8_t*>(workspace))
+                 : run_decode<8>(p, B, max_nblocks, pdl != 0, st, reinterpret_cast<uint8_t*>(workspace));
+  if (rc) return rc;
+  return check_launch("csa_decode");
+}
+
+// ----------------------------------------------------------- LSE merge
+// out[b,h,:] = sum_r e^{m_r - M} O_r / (sum_r e^{m_r - M} l_r + e^{sink_h - M}),
+// M = max(max_r m_r, sink_h): partial attention over disjoint source sets
+// combined exactly (the sink counted once).  One warp per (b, h).
+__global__ void lse_merge_kernel(const float* __restrict__ part_o, const float* __restrict__ part_ml,
+                                 const float* __restrict__ sink, int G, int B, int H,
+                                 __nv_bfloat16* __restrict__ out) {
+  const int lane = threadIdx.x & 31;
+  const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  if (w >= B * H) return;
+  const int h = w % H;
+  const long long stride_r = static_cast<long long>(B) * H;
+  float M = sink[h];
+  for (int r = 0; r < G; ++r) M = fmaxf(M, part_ml[(r * stride_r + w) * 2]);
+  float L = __expf(sink[h] - M);
+  float acc[4] = {0, 0, 0, 0};
+  for (int r = 0; r < G; ++r) {
+    const float m = part_ml[(r * stride_r + w) * 2], l = part_ml[(r * stride_r + w) * 2 + 1];
+    const float a = m == -INFINITY ? 0.f : __expf(m - M);
+    L += a * l;
+    const float4 o = *reinterpret_cast<const float4*>(part_o + (r * stride_r + w) * kHeadDim + lane * 4);
+    acc[0] += a * o.x;
+    acc[1] += a * o.y;
+    acc[2] += a * o.z;
+    acc[3] += a * o.w;
+  }
+  const float inv = 1.f / L;
+  __nv_bfloat162 o01 = __floats2bfloat162_rn(acc[0] * inv, acc[1] * inv);
+  __nv_bfloat162 o23 = __floats2bfloat162_rn(acc[2] * inv, acc[3] * inv);
+  *reinterpret_cast<uint2*>(out + static_cast<long long>(w) * kHeadDim + lane * 4) =
+      make_uint2(*reinterpret_cast<uint32_t*>(&o01), *reinterpret_cast<uint32_t*>(&o23));
 }
 
 }  // namespace aether
+
+using namespace aether;
 
 // Profiling aid: when buf is non-null, later CSA decode launches record
 // per-CTA phase timestamps (%globaltimer, ns) of the attend kernel into
@@ -942,9 +1126,100 @@ int csa_decode_cta(const void* q, const float* index_q, const float* index_w, co
 extern "C" void aether_csa_decode_set_debug_timer(long long* buf) { aether::g_cta_debug = buf; }
 
 extern "C" size_t aether_csa_decode_workspace_bytes(int B, int max_nblocks) {
-  return static_cast<size_t>(B > 0 ? B : 0) * aether::csa_workspace_stride(max_nblocks) * sizeof(uint32_t);
+  return aether::workspace_bytes(B > 0 ? B : 0, max_nblocks);
 }
 
 extern "C" int aether_csa_decode_smem_bytes(int bits) {
   return bits == 4 ? aether::QCfg<4>::SMEM : aether::QCfg<8>::SMEM;
+}
+
+// Context-parallel step 1: score this device's blocks [id_base, id_base +
+// nblocks[b]) of every sequence and keep the top_k of each 8192-block chunk.
+// cand_keys / cand_ids: [B][chunks * top_k], chunks = ceil(max_nblocks / 8192);
+// padding entries have key 0 and id -1.
+extern "C" int aether_csa_local_candidates(const float* index_q, const float* index_w, const uint8_t* idx_pages,
+                                           const int32_t* page_table, int table_stride, int num_pages,
+                                           const int32_t* nblocks, int max_nblocks, const float* diag_idx, int B,
+                                           int bits, int top_k, int id_base, uint32_t* cand_keys, int32_t* cand_ids,
+                                           void* workspace, int* err, void* stream) {
+  int rc = check_common(bits, 1, 0, top_k, max_nblocks, table_stride, num_pages);
+  if (rc) return rc;
+  AETHER_REQUIRE(workspace && cand_keys && cand_ids, "csa_local_candidates: null buffer");
+  AETHER_REQUIRE((top_k & 3) == 0, "csa_local_candidates: top_k must be a multiple of 4, got %d", top_k);
+  if (B == 0) return 0;
+  QParams p = base_params(nullptr, index_q, index_w, nullptr, nullptr, nullptr, idx_pages, nullptr, page_table,
+                          table_stride, num_pages, nblocks, max_nblocks, diag_idx, nullptr, 1, 0, top_k, 0.f, err);
+  p.ws = static_cast<uint32_t*>(workspace);
+  p.id_base = id_base;
+  p.chunks = max(1, (max_nblocks + kMaxKeys - 1) / kMaxKeys);
+  p.sel_keys_out = cand_keys;
+  p.sel_ids_out = cand_ids;
+  p.sel_stride = top_k;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (bits == 4) {
+    rc = set_smem_attrs<4>();
+    if (!rc) rc = launch_score<4>(p, B, max_nblocks, false, st);
+    if (!rc) rc = launch_attend<4>(p, B, true, st);
+  } else {
+    rc = set_smem_attrs<8>();
+    if (!rc) rc = launch_score<8>(p, B, max_nblocks, false, st);
+    if (!rc) rc = launch_attend<8>(p, B, true, st);
+  }
+  if (rc) return rc;
+  return check_launch("csa_local_candidates");
+}
+
+// Context-parallel step 2: exact top_k over a merged candidate list (keys and
+// ascending global ids, [B][cand_stride], cand_n used per row), attention over
+// the winners this device holds (ids in [id_base, id_base + nblocks[b])) plus
+// its window rows (window_len may be 0).  With part_o / part_ml given the
+// un-normalised partial (O [B][H][128], (max, sum) [B][H][2]) is written for
+// aether_lse_merge; otherwise the final bf16 output.  sel_out (optional)
+// receives the global winners [B][top_k] in ascending order.
+extern "C" int aether_csa_attend_candidates(const void* q, const float* sink, const void* window,
+                                            const int32_t* window_len, const uint8_t* kv_pages,
+                                            const int32_t* page_table, int table_stride, int num_pages,
+                                            const int32_t* nblocks, int max_nblocks, const float* diag_kv,
+                                            const uint32_t* cand_keys, const int32_t* cand_ids, int cand_n,
+                                            int cand_stride, int id_base, int B, int H, int W, int bits, int top_k,
+                                            float softmax_scale, void* out, int32_t* sel_out, float* part_o,
+                                            float* part_ml, int* err, void* stream) {
+  int rc = check_common(bits, H, W, top_k, max_nblocks, table_stride, num_pages);
+  if (rc) return rc;
+  AETHER_REQUIRE(cand_keys && cand_ids, "csa_attend_candidates: null candidate list");
+  AETHER_REQUIRE(cand_n >= 0 && cand_n <= kMaxKeys && cand_stride >= cand_n,
+                 "csa_attend_candidates: candidate count %d must be in [0, %d]", cand_n, kMaxKeys);
+  AETHER_REQUIRE((cand_stride & 3) == 0, "csa_attend_candidates: cand_stride must be a multiple of 4");
+  AETHER_REQUIRE((part_o == nullptr) == (part_ml == nullptr), "part_o and part_ml go together");
+  AETHER_REQUIRE(part_o || out, "csa_attend_candidates: no output");
+  if (B == 0) return 0;
+  QParams p = base_params(q, nullptr, nullptr, sink, window, window_len, nullptr, kv_pages, page_table, table_stride,
+                          num_pages, nblocks, max_nblocks, nullptr, diag_kv, H, W, top_k, softmax_scale, err);
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.sel_out = sel_out;
+  p.cand_keys = cand_keys;
+  p.cand_ids = cand_ids;
+  p.cand_n = cand_n;
+  p.cand_stride = cand_stride;
+  p.id_base = id_base;
+  p.part_o = part_o;
+  p.part_ml = part_ml;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  rc = bits == 4 ? set_smem_attrs<4>() : set_smem_attrs<8>();
+  if (!rc) rc = bits == 4 ? launch_attend<4>(p, B, false, st) : launch_attend<8>(p, B, false, st);
+  if (rc) return rc;
+  return check_launch("csa_attend_candidates");
+}
+
+// Combine G partial attention results (from aether_csa_attend_candidates on
+// G devices, gathered as part_o [G][B][H][128], part_ml [G][B][H][2]) with the
+// per-head sink into the bf16 output [B][H][128].
+extern "C" int aether_lse_merge(const float* part_o, const float* part_ml, const float* sink, int G, int B, int H,
+                                void* out, void* stream) {
+  AETHER_REQUIRE(G >= 1 && B >= 0 && H >= 1, "lse_merge: bad sizes");
+  if (B == 0) return 0;
+  const int warps = B * H;
+  lse_merge_kernel<<<(warps * 32 + 255) / 256, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      part_o, part_ml, sink, G, B, H, static_cast<__nv_bfloat16*>(out));
+  return check_launch("lse_merge");
 }

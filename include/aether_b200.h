@@ -102,7 +102,8 @@ int aether_hca_compress(const void* buffer_c, const void* buffer_z, void* out, i
  *   q [B,H,128] bf16, index_q [B,4,64] fp32, index_w [B,4] fp32 raw head
  *   weights, sink [H] fp32, window [B,W,128] bf16 (window_len[b] valid rows,
  *   oldest first), idx_pages / kv_pages page pools, page_table [B,table_stride]
- *   int32, nblocks [B] visible compressed blocks (<= max_nblocks <= 8192),
+ *   int32, nblocks [B] visible compressed blocks (<= max_nblocks <= 262144;
+ *   sequences over 8192 blocks are selected in two levels),
  *   diag_idx [64] / diag_kv [128] Rademacher diagonals.
  * out [B,H,128] bf16 (attention output before the inverse output RoPE),
  * sel_out [B,top_k] int32 selected block ids ascending, -1 padded (may be NULL).
@@ -137,6 +138,40 @@ int aether_hca_decode_paged(const void* q, const float* sink, const void* window
                             const uint8_t* kv_pages, const int32_t* page_table, int table_stride, int num_pages,
                             const int32_t* nblocks, int max_nblocks, const float* diag_kv, int B, int H, int W,
                             int bits, float softmax_scale, void* out, int* err, int cluster, void* stream);
+
+/* ------------------------------------------ context-parallel decode
+ * New design (the reference has no multi-GPU attention): a
+ * sequence's compressed blocks are split into contiguous ranges, one per
+ * device; this device holds blocks [id_base, id_base + nblocks[b]).
+ *
+ * Step 1: exact top_k of each 8192-block chunk of this device's range.
+ * cand_keys / cand_ids [B][chunks * top_k] (chunks = ceil(max_nblocks/8192),
+ * top_k a multiple of 4): order-preserving u32 score keys and global block
+ * ids, ascending; padding has key 0 and id -1.  workspace: as for
+ * aether_csa_decode_paged. */
+int aether_csa_local_candidates(const float* index_q, const float* index_w, const uint8_t* idx_pages,
+                                const int32_t* page_table, int table_stride, int num_pages, const int32_t* nblocks,
+                                int max_nblocks, const float* diag_idx, int B, int bits, int top_k, int id_base,
+                                uint32_t* cand_keys, int32_t* cand_ids, void* workspace, int* err, void* stream);
+
+/* Step 2: exact top_k over the all-gathered candidate lists (cand_n entries
+ * per row, ids ascending), attention over the winners held here plus this
+ * device's window rows (window_len 0 where the window lives elsewhere).
+ * part_o [B][H][128] and part_ml [B][H][2] (max logit, sum of exponentials)
+ * receive the un-normalised partial result; with them NULL, out [B][H][128]
+ * bf16 receives the final one.  sel_out [B][top_k] (optional): global winners. */
+int aether_csa_attend_candidates(const void* q, const float* sink, const void* window, const int32_t* window_len,
+                                 const uint8_t* kv_pages, const int32_t* page_table, int table_stride, int num_pages,
+                                 const int32_t* nblocks, int max_nblocks, const float* diag_kv,
+                                 const uint32_t* cand_keys, const int32_t* cand_ids, int cand_n, int cand_stride,
+                                 int id_base, int B, int H, int W, int bits, int top_k, float softmax_scale, void* out,
+                                 int32_t* sel_out, float* part_o, float* part_ml, int* err, void* stream);
+
+/* Step 3: log-sum-exp merge of G partials [G][B][H][128] / [G][B][H][2] with
+ * the sink counted once (aether_pipeline/serving.py:99-130 softmax over the
+ * union of the source sets); out [B][H][128] bf16. */
+int aether_lse_merge(const float* part_o, const float* part_ml, const float* sink, int G, int B, int H, void* out,
+                     void* stream);
 
 /* Workspace bytes of aether_csa_decode_paged (cluster 0). */
 size_t aether_csa_decode_workspace_bytes(int B, int max_nblocks);
