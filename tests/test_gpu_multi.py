@@ -1,0 +1,71 @@
+"""Context-parallel CSA decode over NCCL on 2 or more GPUs (config 3 shape):
+every rank holds one contiguous range of the sequence's compressed blocks;
+the result must equal the single-GPU decode of the whole sequence."""
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port, q_out):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    import sys
+    from pathlib import Path
+
+    sys.path.insert(0, str(Path(__file__).resolve().parents[1] / "deepseek-v4-codebase_b200"))
+    import torch.distributed as dist
+
+    from aether_kernels.dist import csa_decode_context_parallel
+    from aether_kernels.paged import csa_decode_paged
+    from aether_kernels.rope import RopeConfig
+    from aether_kernels.synthetic import make_decode_batch
+
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev)
+    b = make_decode_batch("csa", 1, 262144, 262144, 8, 4, seed=33, device=dev, rope=RopeConfig.yarn(8.0))
+    npg = b.page_table.shape[1]
+    per = npg // world
+    pt = b.page_table[:, rank * per:(rank + 1) * per].contiguous()
+    nb = torch.tensor([per * 64], dtype=torch.int32, device=dev)
+    wl = b.window_len if rank == world - 1 else torch.zeros_like(b.window_len)
+    out, sel = csa_decode_context_parallel(b.q, b.index_q, b.index_weight, b.sink, b.window, wl, b.cache, pt, nb,
+                                           rank * per * 64, b.softmax_scale, b.top_k)
+    torch.cuda.synchronize()
+    if rank == 0:
+        ref, ref_sel = csa_decode_paged(b.q, b.index_q, b.index_weight, b.sink, b.window, b.window_len, b.cache,
+                                        b.page_table, b.nblocks, b.softmax_scale, top_k=b.top_k)
+        torch.cuda.synchronize()
+        q_out.put((bool(torch.equal(sel, ref_sel)), float((out.float() - ref.float()).abs().max())))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_context_parallel_nccl():
+    world = torch.cuda.device_count()
+    if world < 2:
+        pytest.skip("needs 2 or more GPUs")
+    ctx = mp.get_context("spawn")
+    q_out = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q_out)) for r in range(world)]
+    for p in procs:
+        p.start()
+    same_sel, max_diff = q_out.get(timeout=600)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    assert same_sel
+    assert max_diff < 1e-2
