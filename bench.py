@@ -427,7 +427,7 @@ def main():
                        "parallelism": f"request-sharded x{world}", "pdl": bool(args.pdl),
                        "microbatches": args.microbatches,
                        "timing": "CUDA graph replay, CUDA events"},
-            "gpu_launches": steps,
+            "gpu_launches": steps * (1 if args.cluster else 2),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_source": peak_src, "traffic": read_traffic(),
                          "algorithmic_bytes_per_launch": int(bytes_launch)},
