@@ -33,8 +33,13 @@
 //   codes converted to fp16 in registers; the window uses bf16 ldmatrix
 //   operands.  One warp per head adds the inverse-rotated compressed part to
 //   the window part, normalises with the sink and stores bf16.
+#include <cooperative_groups.h>
+#include <stdlib.h>
+
 #include "capi_util.cuh"
 #include "common.cuh"
+
+namespace cg = cooperative_groups;
 
 namespace aether {
 
@@ -48,41 +53,45 @@ constexpr int kL1Bins = 4096;             // histogram of key >> 19
 constexpr int kMaxPagesLocal = 4096;      // page-table entries per sequence on one device (262144 blocks)
 constexpr int kMaxBlocks = kMaxPagesLocal * kPage;
 
-template <int BITS>
+template <int BITS, int CS>
 struct QCfg {
-  static constexpr int RB_IDX = kIdxDim * BITS / 8;
   static constexpr int RB_KV = kHeadDim * BITS / 8;
-  static constexpr int PB_IDX = page_bytes(RB_IDX);
   static constexpr int PB_KV = page_bytes(RB_KV);
   static constexpr int RAWS = RB_KV + 16;                    // padded stride of gathered code rows
   static constexpr int KROW = kHeadDim + 8;                  // fp16 operand row stride (halves)
-  static constexpr int LST = kMaxTopK + kWinMax;             // logit row stride (floats)
-  static constexpr int PST = kMaxTopK + kWinMax + 8;         // P row stride (halves)
+  static constexpr int SL = kMaxTopK / CS;                   // selected rows attended per CTA (max)
+  static constexpr int WSL = kWinMax / CS;                   // window rows per CTA (max)
+  static constexpr int LST = SL + WSL;                       // logit row stride (floats)
+  static constexpr int PST = SL + WSL + 8;                   // P row stride (halves)
+  static constexpr int HPC = (kMaxHeads + CS - 1) / CS;      // heads finalised per CTA (max)
+  static constexpr int SLOT = 4 + 2 * kHeadDim;              // merge slot: m, l, pad, pad, O_rot, O_win
   // select phase (aliases the attention buffers below)
-  static constexpr int S_SCORES = 0;                         // u32 [8192]
-  static constexpr int S_HIST = S_SCORES + kMaxKeys * 4;     // u32 [4096]
-  static constexpr int S_CAND = S_HIST + kL1Bins * 4;        // u32 [8192] keys of the threshold bin
-  static constexpr int S_END = S_CAND + kMaxKeys * 4;
+  static constexpr int S_HIST = 0;                           // u32 [4096]
+  static constexpr int S_END = S_HIST + kL1Bins * 4;
   // attention phase
-  static constexpr int A_KC = 0;                             // f16 [256][KROW] expanded codes
-  static constexpr int A_RAW = A_KC + kMaxTopK * KROW * 2;   // [256][RAWS] gathered codes
-  static constexpr int A_KS = A_RAW + kMaxTopK * RAWS;       // fp32 [256]
-  static constexpr int A_QR = A_KS + kMaxTopK * 4;           // f16 [16][KROW] rotated q
+  static constexpr int A_KC = 0;                             // f16 [SL][KROW] expanded codes
+  static constexpr int A_KS = A_KC + SL * KROW * 2;          // fp32 [SL]
+  static constexpr int A_QR = A_KS + SL * 4;                 // f16 [16][KROW] rotated q
   static constexpr int A_QW = A_QR + 16 * KROW * 2;          // bf16 [16][KROW] plain q
   static constexpr int A_LOG = A_QW + 16 * KROW * 2;         // fp32 [16][LST]
   static constexpr int A_P = A_LOG + 16 * LST * 4;           // f16 [16][PST]
-  static constexpr int A_O = A_P + 16 * PST * 2;             // fp32 [2][16][128]
+  static constexpr int A_O = (A_P + 16 * PST * 2 + 15) & ~15;  // fp32 [2][16][128]
   static constexpr int A_END = A_O + 2 * 16 * kHeadDim * 4;
-  static constexpr int REGION = A_END > S_END ? A_END : S_END;
+  // gathered code rows [SL][RAWS] share the logits / P / O area (dead by then)
+  static constexpr int A_RAW = A_LOG;
+  static_assert(A_RAW + SL * RAWS <= A_END, "raw rows fit the shared area");
+  static constexpr int REGION = ((A_END > S_END ? A_END : S_END) + 127) & ~127;
 
-  static constexpr int OFF_WIN = REGION;                     // bf16 [128][kWRow]
-  static constexpr int OFF_PT = OFF_WIN + kWinMax * kWRow;   // i32 [kMaxPagesLocal]
+  static constexpr int OFF_WIN = REGION;                     // bf16 [WSL][kWRow] this CTA's window rows
+  static constexpr int OFF_MERGE = OFF_WIN + WSL * kWRow;    // fp32 [CS][HPC][SLOT]
+  static constexpr int OFF_PT = OFF_MERGE + CS * HPC * SLOT * 4;  // i32 [kMaxPagesLocal]
   static constexpr int OFF_SEL = OFF_PT + kMaxPagesLocal * 4;  // i32 [256] positions
-  static constexpr int OFF_OWN = OFF_SEL + kMaxTopK * 4;     // i32 [256] local block ids attended here
-  static constexpr int OFF_SCAN = OFF_OWN + kMaxTopK * 4;     // u32 [64]
+  static constexpr int OFF_OWN = OFF_SEL + kMaxTopK * 4;     // i32 [256] local block ids attended
+  static constexpr int OFF_SCAN = OFF_OWN + kMaxTopK * 4;    // u32 [64]
   static constexpr int OFF_MISC = OFF_SCAN + 64 * 4;
   static constexpr int MISC_BYTES = 512;
-  static constexpr int SMEM = OFF_MISC + MISC_BYTES;
+  static constexpr int OFF_LUT = OFF_MISC + MISC_BYTES;      // u32 [256]: code byte -> half2
+  static constexpr int SMEM = OFF_LUT + 256 * 4;
   static_assert(SMEM <= 227 * 1024, "fits one CTA per SM");
 };
 
@@ -167,7 +176,7 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;"); }
 
-// Block-wide inclusive scan of one u32 per thread (512 threads); uses wtot[0..31].
+// Block-wide inclusive scan of one u32 per thread; uses wtot[0..63].
 __device__ __forceinline__ uint32_t block_scan_incl(uint32_t v, uint32_t* wtot, int lane, int warp) {
   uint32_t inc = v;
 #pragma unroll
@@ -184,10 +193,10 @@ __device__ __forceinline__ uint32_t block_scan_incl(uint32_t v, uint32_t* wtot, 
       const uint32_t u = __shfl_up_sync(0xffffffffu, w, o);
       if (lane >= o) w += u;
     }
-    if (lane < kQWarps) wtot[16 + lane] = w;
+    wtot[32 + lane] = w;
   }
   __syncthreads();
-  return (warp ? wtot[16 + warp - 1] : 0u) + inc;
+  return (warp ? wtot[32 + warp - 1] : 0u) + inc;
 }
 
 // Bin holding the R-th largest element of a histogram scanned from the top
@@ -343,6 +352,16 @@ __global__ void __launch_bounds__(kSThreads) csa_score_kernel(QParams p, int spl
   const int b = blockIdx.x / splits, sp = blockIdx.x % splits;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, t = lane & 3;
+  // profiling aid: phase timestamps after the attend kernel's area
+  long long* dbg = p.dbg ? p.dbg + 65536 + blockIdx.x * 8 : nullptr;
+  auto stamp = [&](int slot) {
+    if (dbg && tid == 0) {
+      long long ts;
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(ts));
+      dbg[slot] = ts;
+    }
+  };
+  stamp(0);
   pdl_launch_dependents();
   int nb = p.nblocks[b];
   nb = max(0, min(nb, min(kMaxBlocks, p.table_stride * kPage)));
@@ -372,6 +391,7 @@ __global__ void __launch_bounds__(kSThreads) csa_score_kernel(QParams p, int spl
       bulk_g2s(smem + lane * C::PB_IDX, p.idx_pages + static_cast<long long>(phys) * C::PB_IDX, C::PB_IDX, bar);
     }
   }
+  stamp(1);
   pdl_wait();
   if (warp < kIdxHeads) index_query_limbs(p, b, warp, lane, limb, alpha, lsum);
   __syncthreads();
@@ -401,7 +421,9 @@ __global__ void __launch_bounds__(kSThreads) csa_score_kernel(QParams p, int spl
   const int c0i = BITS == 4 ? -8 * lsum[t][0] : 0;
   const int c1i = BITS == 4 ? -8 * lsum[t][1] : 0;
   const int c2i = BITS == 4 ? -8 * lsum[t][2] : 0;
+  stamp(2);
   mbar_wait(bar, 0, p.err);
+  stamp(3);
   uint32_t* out = p.ws + static_cast<long long>(b) * p.ws_stride;
   const int tiles = np * (kPage / 16);
   for (int t0 = warp; t0 < tiles; t0 += 2 * kSWarps) {
@@ -479,13 +501,18 @@ __global__ void __launch_bounds__(kSThreads) csa_score_kernel(QParams p, int spl
       }
     }
   }
+  stamp(4);
 }
 
-template <int BITS>
-__global__ void __launch_bounds__(kQThreads, 1) csa_attend_kernel(QParams p) {
-  using C = QCfg<BITS>;
+template <int BITS, int CS>
+__global__ void __launch_bounds__(kQThreads, CS > 1 ? 2 : 1) csa_attend_kernel(QParams p) {
+  using C = QCfg<BITS, CS>;
   extern __shared__ __align__(128) uint8_t smem[];
-  const int b = blockIdx.x / p.chunks, chunk = blockIdx.x % p.chunks;
+  // grid: ((sequence * chunks) + chunk) * CS + rank; a cluster of CS CTAs
+  // serves one (sequence, chunk): every CTA selects, each attends a slice
+  const int r = blockIdx.x % CS;
+  const int bc = blockIdx.x / CS;
+  const int b = bc / p.chunks, chunk = bc % p.chunks;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, t = lane & 3;
   const bool select_only = p.sel_keys_out != nullptr;
@@ -498,15 +525,19 @@ __global__ void __launch_bounds__(kQThreads, 1) csa_attend_kernel(QParams p) {
   };
   stamp(0, tid == 0);
   pdl_launch_dependents();
+  // announce this CTA is running; the wait comes before the first remote access
+  if constexpr (CS > 1) asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
 
   uint8_t* winb = smem + C::OFF_WIN;
-  uint32_t* scores = reinterpret_cast<uint32_t*>(smem + C::S_SCORES);
   uint32_t* hist = reinterpret_cast<uint32_t*>(smem + C::S_HIST);
+  float* merge = reinterpret_cast<float*>(smem + C::OFF_MERGE);
   int32_t* pt = reinterpret_cast<int32_t*>(smem + C::OFF_PT);
   int32_t* sel = reinterpret_cast<int32_t*>(smem + C::OFF_SEL);
   int32_t* own = reinterpret_cast<int32_t*>(smem + C::OFF_OWN);
   uint32_t* wtot = reinterpret_cast<uint32_t*>(smem + C::OFF_SCAN);
   QMisc* misc = reinterpret_cast<QMisc*>(smem + C::OFF_MISC);
+  uint32_t* lut = reinterpret_cast<uint32_t*>(smem + C::OFF_LUT);
+  if (BITS == 4 && tid < 256) lut[tid] = nib_byte_to_h2(static_cast<uint32_t>(tid));
 
   // ------------------------------------------------------------ prologue
   int nb = p.nblocks[b];  // blocks of sequence b held on this device
@@ -521,6 +552,9 @@ __global__ void __launch_bounds__(kQThreads, 1) csa_attend_kernel(QParams p) {
   const int npages = (nb + kPage - 1) / kPage;
   const int W = p.W;
   const int wl = select_only ? 0 : max(0, min(p.window_len[b], W));
+  const int wsl = (W + CS - 1) / CS;               // window rows per CTA
+  const int w0 = r * wsl;                           // this CTA's first window row
+  const int wn = max(0, min(wl - w0, wsl));         // its valid window rows
   if (!select_only) {
     const int32_t* ptab = p.page_table + static_cast<long long>(b) * p.table_stride;
     for (int i = tid; i < npages; i += kQThreads) {
@@ -537,7 +571,6 @@ __global__ void __launch_bounds__(kQThreads, 1) csa_attend_kernel(QParams p) {
   if (tid == 0) {
     misc->thr = 0;
     misc->take_eq = 0xFFFFFFFFu;
-    misc->ncand = 0;
     misc->bin = 0;
     misc->above = 0;
     misc->cnt = 0;
@@ -546,13 +579,12 @@ __global__ void __launch_bounds__(kQThreads, 1) csa_attend_kernel(QParams p) {
   }
   // window rows other than the newest are cache state: prefetch them now
   {
-    const int pre = max(wl - 1, 0);
-    const __nv_bfloat16* wsrc = p.window + static_cast<long long>(b) * W * kHeadDim;
+    const int pre = max(0, min(wn, wl - 1 - w0));
+    const __nv_bfloat16* wsrc = p.window + (static_cast<long long>(b) * W + w0) * kHeadDim;
     for (int i = tid; i < pre * 16; i += kQThreads)
       cp_async16(winb + (i >> 4) * kWRow + (i & 15) * 16, wsrc + (i >> 4) * kHeadDim + (i & 15) * 8);
     asm volatile("cp.async.commit_group;" ::: "memory");
   }
-  stamp(1, tid == 0);
   // the block keys come from the score kernel (or a previous select)
   pdl_wait();
   stamp(2, tid == 0);
@@ -580,22 +612,22 @@ __global__ void __launch_bounds__(kQThreads, 1) csa_attend_kernel(QParams p) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) cnt += __shfl_xor_sync(0xffffffffu, cnt, o);
     if (lane == 0 && cnt) atomicAdd(&misc->nvalid, cnt);
-#pragma unroll
-    for (int v = 0; v < PER / 4; ++v)
-      *reinterpret_cast<uint4*>(scores + i0 + 4 * v) = make_uint4(kr[4 * v], kr[4 * v + 1], kr[4 * v + 2], kr[4 * v + 3]);
   }
   __syncthreads();
   stamp(3, tid == 0);
   const int nvalid = static_cast<int>(misc->nvalid);
   const int K = min(p.top_k, nvalid);
-  if (p.score_out && !explicit_list) {
-    float* so = p.score_out + static_cast<long long>(b) * p.score_stride + chunk * kMaxKeys;
-    for (int i = tid; i < n; i += kQThreads) so[i] = __uint_as_float(scores[i] - 1u);
+  if (p.score_out && !explicit_list && r == 0) {
+    float* so = p.score_out + static_cast<long long>(b) * p.score_stride + chunk * kMaxKeys + i0;
+#pragma unroll
+    for (int j = 0; j < PER; ++j)
+      if (i0 + j < n) so[j] = __uint_as_float(kr[j] - 1u);
   }
 
   // ------------------------------------------------------------- select
   // Result: every key > thr is taken, and the take_eq lowest-position keys
   // == thr.  Keys are >= 1 for real blocks, so thr = 0 takes all of them.
+  // The refinement histograms are built from the keys held in registers.
   if (nvalid > K) {
     uint32_t R = static_cast<uint32_t>(K);
     find_bin(hist, kL1Bins, R, wtot, misc, tid, lane, warp);
@@ -604,39 +636,29 @@ __global__ void __launch_bounds__(kQThreads, 1) csa_attend_kernel(QParams p) {
     if (misc->cnt == R) {
       if (tid == 0) misc->thr = b1 << 19;  // lowest key of bin b1: the whole bin is taken
     } else {
-      // refine inside bin b1 over its keys only: bits 18..8, then 7..0
-      uint32_t* cand = reinterpret_cast<uint32_t*>(smem + C::S_CAND);
-      uint32_t mine = 0;
-#pragma unroll
-      for (int j = 0; j < PER; ++j) mine += kr[j] != 0u && (kr[j] >> 19) == b1;
-      uint32_t off = 0;
-      if (mine) off = atomicAdd(&misc->ncand, mine);
-#pragma unroll
-      for (int j = 0; j < PER; ++j) {
-        const bool m = kr[j] != 0u && (kr[j] >> 19) == b1;
-        if (m) cand[off] = kr[j];
-        off += m;
-      }
       for (int i = tid; i < 2048; i += kQThreads) hist[i] = 0;
       __syncthreads();
-      const uint32_t nc = misc->ncand;
-      for (uint32_t i = tid; i < nc; i += kQThreads) atomicAdd(&hist[(cand[i] >> 8) & 2047u], 1u);
+#pragma unroll
+      for (int j = 0; j < PER; ++j)
+        if (kr[j] != 0u && (kr[j] >> 19) == b1) atomicAdd(&hist[(kr[j] >> 8) & 2047u], 1u);
       __syncthreads();
       find_bin(hist, 2048, R, wtot, misc, tid, lane, warp);
       const uint32_t b2 = misc->bin;
       R -= misc->above;
+      const uint32_t pfx = (b1 << 11) | b2;  // key >> 8
       if (misc->cnt == R) {
-        if (tid == 0) misc->thr = (b1 << 19) | (b2 << 8);  // the whole sub-bin is taken
+        if (tid == 0) misc->thr = pfx << 8;  // the whole sub-bin is taken
       } else {
         for (int i = tid; i < kQThreads; i += kQThreads) hist[i] = 0;
         __syncthreads();
-        for (uint32_t i = tid; i < nc; i += kQThreads)
-          if (((cand[i] >> 8) & 2047u) == b2) atomicAdd(&hist[cand[i] & 255u], 1u);
+#pragma unroll
+        for (int j = 0; j < PER; ++j)
+          if (kr[j] != 0u && (kr[j] >> 8) == pfx) atomicAdd(&hist[kr[j] & 255u], 1u);
         __syncthreads();
         find_bin(hist, kQThreads, R, wtot, misc, tid, lane, warp);  // 256 used bins of 512
         R -= misc->above;
         if (tid == 0) {
-          misc->thr = (b1 << 19) | (b2 << 8) | static_cast<uint32_t>(misc->bin);
+          misc->thr = (pfx << 8) | static_cast<uint32_t>(misc->bin);
           misc->take_eq = R;  // keys equal to thr: the lowest-position R of them
         }
       }
@@ -655,7 +677,7 @@ __global__ void __launch_bounds__(kQThreads, 1) csa_attend_kernel(QParams p) {
     }
     const uint32_t packed = cs | (ce << 16);
     const uint32_t exc = block_scan_incl(packed, wtot, lane, warp) - packed;
-    uint32_t sb = exc & 0xFFFFu, eb = exc >> 16;
+    uint32_t sb = exc & 0xFFFFu, eb = exc >> 16;  // 16-bit fields: at most 8192 keys
     if (cs | ce) {
 #pragma unroll
       for (int j = 0; j < PER; ++j) {
@@ -671,18 +693,20 @@ __global__ void __launch_bounds__(kQThreads, 1) csa_attend_kernel(QParams p) {
   stamp(5, tid == 0);
   // global block id of a source position
   const int32_t* cids = explicit_list ? p.cand_ids + static_cast<long long>(b) * p.cand_stride : nullptr;
-  auto gid_of = [&](int pos) -> int {
-    return explicit_list ? cids[pos] : p.id_base + chunk * kMaxKeys + pos;
-  };
+  auto gid_of = [&](int pos) -> int { return explicit_list ? cids[pos] : p.id_base + chunk * kMaxKeys + pos; };
   if (select_only) {
-    const long long o = static_cast<long long>(blockIdx.x) * p.sel_stride;
-    for (int i = tid; i < p.sel_stride; i += kQThreads) {
-      p.sel_keys_out[o + i] = i < K ? scores[sel[i]] : 0u;
-      p.sel_ids_out[o + i] = i < K ? gid_of(sel[i]) : -1;
+    if (r == 0) {
+      const uint32_t* kk = explicit_list ? p.cand_keys + static_cast<long long>(b) * p.cand_stride
+                                         : p.ws + static_cast<long long>(b) * p.ws_stride + chunk * kMaxKeys;
+      const long long o = static_cast<long long>(bc) * p.sel_stride;
+      for (int i = tid; i < p.sel_stride; i += kQThreads) {
+        p.sel_keys_out[o + i] = i < K ? __ldcg(kk + sel[i]) : 0u;
+        p.sel_ids_out[o + i] = i < K ? gid_of(sel[i]) : -1;
+      }
     }
     return;
   }
-  if (p.sel_out) {
+  if (p.sel_out && r == 0) {
     int32_t* so = p.sel_out + static_cast<long long>(b) * p.top_k;
     for (int i = tid; i < p.top_k; i += kQThreads) so[i] = i < K ? gid_of(sel[i]) : -1;
   }
@@ -704,9 +728,12 @@ __global__ void __launch_bounds__(kQThreads, 1) csa_attend_kernel(QParams p) {
   }
   __syncthreads();
   const int KO = static_cast<int>(misc->nown);
+  // this CTA's slice of the winners
+  const int slc = (((KO + CS - 1) / CS) + 15) & ~15;
+  const int s0 = min(KO, r * slc);
+  const int kc = max(0, min(KO - s0, slc));
 
   // --------------------------------------------------------- attention
-  // (the select-phase buffers are dead from here on)
   __half* Kc = reinterpret_cast<__half*>(smem + C::A_KC);
   uint8_t* raw = smem + C::A_RAW;
   float* ks = reinterpret_cast<float*>(smem + C::A_KS);
@@ -715,19 +742,19 @@ __global__ void __launch_bounds__(kQThreads, 1) csa_attend_kernel(QParams p) {
   float* logit = reinterpret_cast<float*>(smem + C::A_LOG);
   __half* P = reinterpret_cast<__half*>(smem + C::A_P);
   float* Obuf = reinterpret_cast<float*>(smem + C::A_O);
-  const int ntc = (KO + 15) / 16, ntw = (wl + 15) / 16;
+  const int ntc = (kc + 15) / 16, ntw = (wn + 15) / 16;
   {
     constexpr int CPR = C::RB_KV / 16;
-    for (int i = tid; i < KO * CPR; i += kQThreads) {
+    for (int i = tid; i < kc * CPR; i += kQThreads) {
       const int row = i / CPR, ch = i % CPR;
-      const int blk = min(max(own[row], 0), max(nb - 1, 0));
+      const int blk = min(max(own[s0 + row], 0), max(nb - 1, 0));
       const uint8_t* pg = p.kv_pages + static_cast<long long>(pt[blk >> 6]) * C::PB_KV;
       cp_async16(raw + row * C::RAWS + ch * 16, pg + (blk & 63) * C::RB_KV + ch * 16);
       if (ch == 0) cp_async4(ks + row, pg + kPage * C::RB_KV + (blk & 63) * 4);
     }
-    // newest window row (written by the previous step)
-    if (wl > 0 && tid < 16)
-      cp_async16(winb + (wl - 1) * kWRow + tid * 16,
+    // newest window row (written by the previous step), if it is in this slice
+    if (wl > 0 && wl - 1 >= w0 && wl - 1 < w0 + wsl && tid < 16)
+      cp_async16(winb + (wl - 1 - w0) * kWRow + tid * 16,
                  p.window + (static_cast<long long>(b) * W + wl - 1) * kHeadDim + tid * 8);
   }
   // queries: plain bf16 rows for the window, rotated fp16 rows for the codes
@@ -751,27 +778,26 @@ __global__ void __launch_bounds__(kQThreads, 1) csa_attend_kernel(QParams p) {
     *reinterpret_cast<uint2*>(Qr + h * C::KROW + lane * 4) =
         make_uint2(pack_half2(v[0] * cn, v[1] * cn), pack_half2(v[2] * cn, v[3] * cn));
   }
-  // zero window rows past wl up to the tile edge
-  for (int i = tid; i < (ntw * 16 - wl) * 16; i += kQThreads)
-    *reinterpret_cast<uint4*>(winb + (wl + (i >> 4)) * kWRow + (i & 15) * 16) = make_uint4(0, 0, 0, 0);
+  // zero window rows past wn up to the tile edge
+  for (int i = tid; i < (ntw * 16 - wn) * 16; i += kQThreads)
+    *reinterpret_cast<uint4*>(winb + (wn + (i >> 4)) * kWRow + (i & 15) * 16) = make_uint4(0, 0, 0, 0);
   cp_async_commit_wait_all();
   __syncthreads();
   stamp(6, tid == 0);
-  // codes -> exact fp16 rows (rows past K zero-filled to the tile edge)
+  // codes -> exact fp16 rows (rows past kc zero-filled to the tile edge)
   for (int i = tid; i < ntc * 16 * 16; i += kQThreads) {
     const int row = i >> 4, c8 = (i & 15) * 8;
     uint4 o = make_uint4(0, 0, 0, 0);
-    if (row < KO) {
+    if (row < kc) {
       if (BITS == 4) {
         const uint32_t w = *reinterpret_cast<const uint32_t*>(raw + row * C::RAWS + c8 / 2);
-        o = make_uint4(nib_byte_to_h2(w & 0xFFu), nib_byte_to_h2((w >> 8) & 0xFFu), nib_byte_to_h2((w >> 16) & 0xFFu),
-                       nib_byte_to_h2(w >> 24));
+        o = make_uint4(lut[w & 0xFFu], lut[(w >> 8) & 0xFFu], lut[(w >> 16) & 0xFFu], lut[w >> 24]);
       } else {
         const uint2 w = *reinterpret_cast<const uint2*>(raw + row * C::RAWS + c8);
         o = make_uint4(s8pair_to_h2(w.x & 0xFFFFu), s8pair_to_h2(w.x >> 16), s8pair_to_h2(w.y & 0xFFFFu),
                        s8pair_to_h2(w.y >> 16));
       }
-    } else if (row < kMaxTopK && (i & 15) == 0) {
+    } else if ((i & 15) == 0) {
       ks[row] = 0.f;
     }
     *reinterpret_cast<uint4*>(Kc + row * C::KROW + c8) = o;
@@ -779,49 +805,47 @@ __global__ void __launch_bounds__(kQThreads, 1) csa_attend_kernel(QParams p) {
   __syncthreads();
 
   // ---- S = Q K^T, one 16-source tile per warp iteration
-  {
-    for (int tile = warp; tile < ntc + ntw; tile += kQWarps) {
-      const bool comp = tile < ntc;
-      float acc[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
-      float acc2[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
-      if (comp) {
-        const __half* Kt = Kc + tile * 16 * C::KROW;
+  for (int tile = warp; tile < ntc + ntw; tile += kQWarps) {
+    const bool comp = tile < ntc;
+    float acc[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
+    float acc2[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
+    if (comp) {
+      const __half* Kt = Kc + tile * 16 * C::KROW;
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          uint32_t a[4], b0, b1, b2, b3;
-          ldsm_x4(a[0], a[1], a[2], a[3], Qr + (lane & 15) * C::KROW + kk * 16 + (lane >> 4) * 8);
-          ldsm_x4(b0, b1, b2, b3, Kt + ((lane & 7) + ((lane >> 4) << 3)) * C::KROW + kk * 16 + ((lane >> 3) & 1) * 8);
-          mma_f16((kk & 1) ? acc2[0] : acc[0], a, b0, b1);
-          mma_f16((kk & 1) ? acc2[1] : acc[1], a, b2, b3);
-        }
-      } else {
-        const uint8_t* wt = winb + (tile - ntc) * 16 * kWRow;
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          uint32_t a[4], b0, b1, b2, b3;
-          ldsm_x4(a[0], a[1], a[2], a[3], Qw + (lane & 15) * C::KROW + kk * 16 + (lane >> 4) * 8);
-          ldsm_x4(b0, b1, b2, b3, wt + ((lane & 7) + ((lane >> 4) << 3)) * kWRow + (kk * 16 + ((lane >> 3) & 1) * 8) * 2);
-          mma_bf16((kk & 1) ? acc2[0] : acc[0], a, b0, b1);
-          mma_bf16((kk & 1) ? acc2[1] : acc[1], a, b2, b3);
-        }
+      for (int kk = 0; kk < 8; ++kk) {
+        uint32_t a[4], b0, b1, b2, b3;
+        ldsm_x4(a[0], a[1], a[2], a[3], Qr + (lane & 15) * C::KROW + kk * 16 + (lane >> 4) * 8);
+        ldsm_x4(b0, b1, b2, b3, Kt + ((lane & 7) + ((lane >> 4) << 3)) * C::KROW + kk * 16 + ((lane >> 3) & 1) * 8);
+        mma_f16((kk & 1) ? acc2[0] : acc[0], a, b0, b1);
+        mma_f16((kk & 1) ? acc2[1] : acc[1], a, b2, b3);
       }
+    } else {
+      const uint8_t* wt = winb + (tile - ntc) * 16 * kWRow;
 #pragma unroll
-      for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-        for (int e = 0; e < 4; e += 2) {
-          const int h = g + (e >> 1) * 8;
-          const int src = tile * 16 + nt * 8 + 2 * t;
-          float z0 = acc[nt][e] + acc2[nt][e], z1 = acc[nt][e + 1] + acc2[nt][e + 1];
-          if (comp) {
-            z0 = src < KO ? z0 * ks[src] * p.softmax_scale : -INFINITY;
-            z1 = src + 1 < KO ? z1 * ks[src + 1] * p.softmax_scale : -INFINITY;
-          } else {
-            z0 = (src - ntc * 16) < wl ? z0 * p.softmax_scale : -INFINITY;
-            z1 = (src + 1 - ntc * 16) < wl ? z1 * p.softmax_scale : -INFINITY;
-          }
-          *reinterpret_cast<float2*>(logit + h * C::LST + src) = make_float2(z0, z1);
-        }
+      for (int kk = 0; kk < 8; ++kk) {
+        uint32_t a[4], b0, b1, b2, b3;
+        ldsm_x4(a[0], a[1], a[2], a[3], Qw + (lane & 15) * C::KROW + kk * 16 + (lane >> 4) * 8);
+        ldsm_x4(b0, b1, b2, b3, wt + ((lane & 7) + ((lane >> 4) << 3)) * kWRow + (kk * 16 + ((lane >> 3) & 1) * 8) * 2);
+        mma_bf16((kk & 1) ? acc2[0] : acc[0], a, b0, b1);
+        mma_bf16((kk & 1) ? acc2[1] : acc[1], a, b2, b3);
+      }
     }
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; e += 2) {
+        const int h = g + (e >> 1) * 8;
+        const int src = tile * 16 + nt * 8 + 2 * t;
+        float z0 = acc[nt][e] + acc2[nt][e], z1 = acc[nt][e + 1] + acc2[nt][e + 1];
+        if (comp) {
+          z0 = src < kc ? z0 * ks[src] * p.softmax_scale : -INFINITY;
+          z1 = src + 1 < kc ? z1 * ks[src + 1] * p.softmax_scale : -INFINITY;
+        } else {
+          z0 = (src - ntc * 16) < wn ? z0 * p.softmax_scale : -INFINITY;
+          z1 = (src + 1 - ntc * 16) < wn ? z1 * p.softmax_scale : -INFINITY;
+        }
+        *reinterpret_cast<float2*>(logit + h * C::LST + src) = make_float2(z0, z1);
+      }
   }
   __syncthreads();
   stamp(7, tid == 0);
@@ -858,17 +882,17 @@ __global__ void __launch_bounds__(kQThreads, 1) csa_attend_kernel(QParams p) {
   }
   __syncthreads();
   stamp(8, tid == 0);
-  // ---- O = P V; warp w owns output dims [8w, 8w+8)
+  // ---- O = P V; warp w owns output dims [8w, 8w+8); partials go to the
+  // head's owner CTA (slot r), which merges them
   {
-    float orot[4] = {0, 0, 0, 0}, orot2[4] = {0, 0, 0, 0}, owin[4] = {0, 0, 0, 0};
-#pragma unroll 2
+    float orot[4] = {0, 0, 0, 0}, owin[4] = {0, 0, 0, 0};
     for (int kt = 0; kt < ntc; ++kt) {
       uint32_t a[4], b0, b1;
       ldsm_x4(a[0], a[1], a[2], a[3], P + (lane & 15) * C::PST + kt * 16 + (lane >> 4) * 8);
       asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0,%1}, [%2];"
                    : "=r"(b0), "=r"(b1)
                    : "r"(smem_u32(Kc + (kt * 16 + (lane & 7) + ((lane >> 3) & 1) * 8) * C::KROW + warp * 8)));
-      mma_f16((kt & 1) ? orot2 : orot, a, b0, b1);
+      mma_f16(orot, a, b0, b1);
     }
     for (int kt = ntc; kt < ntc + ntw; ++kt) {
       uint32_t a[4], b0, b1;
@@ -879,49 +903,82 @@ __global__ void __launch_bounds__(kQThreads, 1) csa_attend_kernel(QParams p) {
                    : "r"(smem_u32(wt + ((lane & 7) + ((lane >> 3) & 1) * 8) * kWRow + warp * 16)));
       mma_f16(owin, a, bf2_to_h2(b0), bf2_to_h2(b1));
     }
-#pragma unroll
-    for (int e = 0; e < 4; ++e) orot[e] += orot2[e];
+    const int hpc = (p.H + CS - 1) / CS;
+    if constexpr (CS > 1) asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
 #pragma unroll
     for (int e = 0; e < 4; e += 2) {
       const int h = g + (e >> 1) * 8;
-      const int dd = warp * 8 + 2 * t;
-      *reinterpret_cast<float2*>(Obuf + h * kHeadDim + dd) = make_float2(orot[e], orot[e + 1]);
-      *reinterpret_cast<float2*>(Obuf + 16 * kHeadDim + h * kHeadDim + dd) = make_float2(owin[e], owin[e + 1]);
+      if (h < p.H) {
+        const int owner = h / hpc, lh = h % hpc;
+        float* slot = merge + (r * C::HPC + lh) * C::SLOT;
+        if constexpr (CS > 1) slot = cg::this_cluster().map_shared_rank(slot, owner);
+        const int dd = warp * 8 + 2 * t;
+        *reinterpret_cast<float2*>(slot + 4 + dd) = make_float2(orot[e], orot[e + 1]);
+        *reinterpret_cast<float2*>(slot + 4 + kHeadDim + dd) = make_float2(owin[e], owin[e + 1]);
+      }
     }
   }
-  __syncthreads();
+  if (warp == 0 && lane < p.H) {
+    const int hpc = (p.H + CS - 1) / CS;
+    const int h = lane, owner = h / hpc, lh = h % hpc;
+    float* slot = merge + (r * C::HPC + lh) * C::SLOT;
+    if constexpr (CS > 1) slot = cg::this_cluster().map_shared_rank(slot, owner);
+    slot[0] = misc->m_h[h];
+    slot[1] = misc->l_h[h];
+  }
+  if constexpr (CS > 1) cg::this_cluster().sync();
+  else __syncthreads();
   stamp(9, tid == 0);
-  // ---- per head: inverse rotation, then either the final sink-normalised
-  // bf16 output or the partial (O, max, sum) for a cross-device merge
-  if (warp < p.H) {
-    const int h = warp;
-    const float m = misc->m_h[h], l = misc->l_h[h];
-    const float4 o1 = *reinterpret_cast<const float4*>(Obuf + h * kHeadDim + lane * 4);
-    const float4 o2 = *reinterpret_cast<const float4*>(Obuf + 16 * kHeadDim + h * kHeadDim + lane * 4);
-    float vr[4] = {o1.x, o1.y, o1.z, o1.w};
-    const float vw[4] = {o2.x, o2.y, o2.z, o2.w};
-    warp_wht128(vr, lane);
-    float o[4];
+  // ---- owner: merge the CS partials of its heads, inverse rotation, then
+  // the final sink-normalised bf16 output or the partial (O, max, sum)
+  {
+    const int hpc = (p.H + CS - 1) / CS;
+    for (int lh = warp; lh < hpc; lh += kQWarps) {
+      const int h = r * hpc + lh;
+      if (h >= p.H) break;
+      float M = -INFINITY;
 #pragma unroll
-    for (int k = 0; k < 4; ++k) o[k] = vr[k] * 0.0883883461356163f * p.diag_kv[lane * 4 + k] + vw[k];
-    if (p.part_o) {
-      *reinterpret_cast<float4*>(p.part_o + (static_cast<long long>(b) * p.H + h) * kHeadDim + lane * 4) =
-          make_float4(o[0], o[1], o[2], o[3]);
-      if (lane == 0)
-        *reinterpret_cast<float2*>(p.part_ml + (static_cast<long long>(b) * p.H + h) * 2) = make_float2(m, l);
-    } else {
-      const float sk = p.sink[h];
-      const float M = fmaxf(m, sk);
-      const float a = m == -INFINITY ? 0.f : __expf(m - M);
-      const float inv = a / (l * a + __expf(sk - M));
-      __nv_bfloat162 o01 = __floats2bfloat162_rn(o[0] * inv, o[1] * inv), o23 = __floats2bfloat162_rn(o[2] * inv, o[3] * inv);
-      *reinterpret_cast<uint2*>(p.out + (static_cast<long long>(b) * p.H + h) * kHeadDim + lane * 4) =
-          make_uint2(*reinterpret_cast<uint32_t*>(&o01), *reinterpret_cast<uint32_t*>(&o23));
+      for (int rr = 0; rr < CS; ++rr) M = fmaxf(M, merge[(rr * C::HPC + lh) * C::SLOT]);
+      float L = 0.f, vr[4] = {0, 0, 0, 0}, vw[4] = {0, 0, 0, 0};
+#pragma unroll
+      for (int rr = 0; rr < CS; ++rr) {
+        const float* slot = merge + (rr * C::HPC + lh) * C::SLOT;
+        const float m = slot[0];
+        const float a = m == -INFINITY ? 0.f : __expf(m - M);
+        L += a * slot[1];
+        const float4 o1 = *reinterpret_cast<const float4*>(slot + 4 + lane * 4);
+        const float4 o2 = *reinterpret_cast<const float4*>(slot + 4 + kHeadDim + lane * 4);
+        vr[0] += a * o1.x; vr[1] += a * o1.y; vr[2] += a * o1.z; vr[3] += a * o1.w;
+        vw[0] += a * o2.x; vw[1] += a * o2.y; vw[2] += a * o2.z; vw[3] += a * o2.w;
+      }
+      warp_wht128(vr, lane);
+      float o[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) o[k] = vr[k] * 0.0883883461356163f * p.diag_kv[lane * 4 + k] + vw[k];
+      if (p.part_o) {
+        *reinterpret_cast<float4*>(p.part_o + (static_cast<long long>(b) * p.H + h) * kHeadDim + lane * 4) =
+            make_float4(o[0], o[1], o[2], o[3]);
+        if (lane == 0)
+          *reinterpret_cast<float2*>(p.part_ml + (static_cast<long long>(b) * p.H + h) * 2) = make_float2(M, L);
+      } else {
+        const float sk = p.sink[h];
+        const float Ms = fmaxf(M, sk);
+        const float a = M == -INFINITY ? 0.f : __expf(M - Ms);
+        const float inv = a / (L * a + __expf(sk - Ms));
+        __nv_bfloat162 o01 = __floats2bfloat162_rn(o[0] * inv, o[1] * inv);
+        __nv_bfloat162 o23 = __floats2bfloat162_rn(o[2] * inv, o[3] * inv);
+        *reinterpret_cast<uint2*>(p.out + (static_cast<long long>(b) * p.H + h) * kHeadDim + lane * 4) =
+            make_uint2(*reinterpret_cast<uint32_t*>(&o01), *reinterpret_cast<uint32_t*>(&o23));
+      }
     }
   }
   stamp(10, tid == 0);
 }
 
+#ifndef AETHER_ATTEND_CLUSTER
+#define AETHER_ATTEND_CLUSTER 2
+#endif
+constexpr int kAttendCluster = AETHER_ATTEND_CLUSTER;  // CTAs per sequence in the attention phase
 
 template <int BITS>
 static int set_smem_attrs() {
@@ -930,47 +987,68 @@ static int set_smem_attrs() {
     AETHER_CUDA_TRY(cudaFuncSetAttribute(csa_score_kernel<BITS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          SCfg<BITS>::SMEM),
                     "csa_decode: set shared memory size (score)");
-    AETHER_CUDA_TRY(cudaFuncSetAttribute(csa_attend_kernel<BITS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         QCfg<BITS>::SMEM),
+    AETHER_CUDA_TRY(cudaFuncSetAttribute(csa_attend_kernel<BITS, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         QCfg<BITS, 1>::SMEM),
+                    "csa_decode: set shared memory size (select)");
+    AETHER_CUDA_TRY(cudaFuncSetAttribute(csa_attend_kernel<BITS, kAttendCluster>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, QCfg<BITS, kAttendCluster>::SMEM),
                     "csa_decode: set shared memory size (attend)");
     done = true;
   }
   return 0;
 }
 
-static cudaLaunchAttribute g_pdl_attr = [] {
-  cudaLaunchAttribute a;
-  a.id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  a.val.programmaticStreamSerializationAllowed = 1;
-  return a;
-}();
-
 template <int BITS>
 static int launch_score(const QParams& p, int B, int max_nblocks, bool pdl, cudaStream_t st) {
   using CA = SCfg<BITS>;
   const int max_pages = (max_nblocks + kPage - 1) / kPage;
   const int splits = max(1, (max_pages + CA::PPC - 1) / CA::PPC);
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
   cudaLaunchConfig_t c = {};
   c.gridDim = dim3(B * splits);
   c.blockDim = dim3(kSThreads);
   c.dynamicSmemBytes = CA::SMEM;
   c.stream = st;
-  c.attrs = &g_pdl_attr;
+  c.attrs = at;
   c.numAttrs = pdl ? 1 : 0;
   AETHER_CUDA_TRY(cudaLaunchKernelEx(&c, csa_score_kernel<BITS>, p, splits), "csa_decode: launch (score)");
   return 0;
 }
 
+// select-only launches use single CTAs; attention launches a cluster per sequence
 template <int BITS>
 static int launch_attend(const QParams& p, int B, bool pdl, cudaStream_t st) {
+  const bool sel_only = p.sel_keys_out != nullptr;
+  const int cs = sel_only ? 1 : kAttendCluster;
+  cudaLaunchAttribute at[2];
+  int na = 0;
+  if (pdl) {
+    at[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  if (cs > 1) {
+    at[na].id = cudaLaunchAttributeClusterDimension;
+    at[na].val.clusterDim.x = cs;
+    at[na].val.clusterDim.y = 1;
+    at[na].val.clusterDim.z = 1;
+    ++na;
+  }
   cudaLaunchConfig_t c = {};
-  c.gridDim = dim3(B * p.chunks);
+  c.gridDim = dim3(B * p.chunks * cs);
   c.blockDim = dim3(kQThreads);
-  c.dynamicSmemBytes = QCfg<BITS>::SMEM;
   c.stream = st;
-  c.attrs = &g_pdl_attr;
-  c.numAttrs = pdl ? 1 : 0;
-  AETHER_CUDA_TRY(cudaLaunchKernelEx(&c, csa_attend_kernel<BITS>, p), "csa_decode: launch (attend)");
+  c.attrs = at;
+  c.numAttrs = na;
+  if (sel_only) {
+    c.dynamicSmemBytes = QCfg<BITS, 1>::SMEM;
+    AETHER_CUDA_TRY(cudaLaunchKernelEx(&c, csa_attend_kernel<BITS, 1>, p), "csa_decode: launch (select)");
+  } else {
+    c.dynamicSmemBytes = QCfg<BITS, kAttendCluster>::SMEM;
+    AETHER_CUDA_TRY(cudaLaunchKernelEx(&c, csa_attend_kernel<BITS, kAttendCluster>, p), "csa_decode: launch (attend)");
+  }
   return 0;
 }
 
@@ -1032,10 +1110,18 @@ static int run_decode(QParams p, int B, int max_nblocks, bool pdl, cudaStream_t 
   int rc = set_smem_attrs<BITS>();
   if (rc) return rc;
   p.ws = reinterpret_cast<uint32_t*>(workspace);
-  rc = launch_score<BITS>(p, B, max_nblocks, pdl, st);
-  if (rc) return rc;
+  static const int only = [] {  // profiling aid: 1 = score kernel only, 2 = attend kernel only
+    const char* e = getenv("AETHER_DECODE_ONLY");
+    return e ? atoi(e) : 0;
+  }();
+  if (only != 2) rc = launch_score<BITS>(p, B, max_nblocks, pdl, st);
+  if (rc || only == 1) return rc;
   const int chunks = (max_nblocks + kMaxKeys - 1) / kMaxKeys;
-  if (chunks <= 1) return launch_attend<BITS>(p, B, true, st);
+  static const bool attend_pdl = [] {
+    const char* e = getenv("AETHER_ATTEND_PDL");
+    return !(e && e[0] == '0');
+  }();
+  if (chunks <= 1) return launch_attend<BITS>(p, B, attend_pdl, st);
   // long sequences: top-k per 8192-block chunk, then top-k of the chunk winners
   uint32_t* ckeys = p.ws + static_cast<size_t>(B) * p.ws_stride;
   int32_t* cids = reinterpret_cast<int32_t*>(ckeys + static_cast<size_t>(B) * chunks * kMaxTopK);
@@ -1130,7 +1216,7 @@ extern "C" size_t aether_csa_decode_workspace_bytes(int B, int max_nblocks) {
 }
 
 extern "C" int aether_csa_decode_smem_bytes(int bits) {
-  return bits == 4 ? aether::QCfg<4>::SMEM : aether::QCfg<8>::SMEM;
+  return bits == 4 ? aether::QCfg<4, aether::kAttendCluster>::SMEM : aether::QCfg<8, aether::kAttendCluster>::SMEM;
 }
 
 // Context-parallel step 1: score this device's blocks [id_base, id_base +
