@@ -29,6 +29,12 @@ SIGNATURES = {
         _c_int,
         [_p, _c_int, _c_int, _c_int, _c_int, _c_int, _p, _p, _c_int, _p, _c_int, _p, _p, _p],
     ),
+    "aether_compress_emit": (
+        _c_int,
+        [_p, _p, _p, _c_int, _p, _p, _p, _c_int, _p, _c_int, _c_int, _c_int,   # segments, has_seg1, dtype, B, d
+         _p, _p, _c_int, _p, _c_f, _c_int, _p,                              # positions .. bits, diag
+         _p, _c_int, _p, _c_int, _p, _p, _p, _p],                           # page_table .. err, stream
+    ),
     "aether_tq_decode": (_c_int, [_p, _p, _c_ll, _c_int, _c_int, _p, _p, _c_int, _p]),
     "aether_wht": (_c_int, [_p, _p, _c_ll, _c_int, _p]),
     "aether_sparse_sink_attention": (

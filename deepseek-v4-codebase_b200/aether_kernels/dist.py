@@ -92,7 +92,9 @@ def lse_merge(part_o: torch.Tensor, part_ml: torch.Tensor, sink: torch.Tensor) -
     """part_o [G,B,H,128] fp32, part_ml [G,B,H,2] fp32, sink [H] fp32 -> bf16 [B,H,128]."""
     G, B, H, D = part_o.shape
     out = torch.empty(B, H, D, dtype=torch.bfloat16, device=part_o.device)
-    _lib.call("aether_lse_merge", part_o.contiguous().data_ptr(), part_ml.contiguous().data_ptr(), sink.data_ptr(),
+    # keep the contiguous copies alive until the launch is enqueued
+    part_o, part_ml = part_o.contiguous(), part_ml.contiguous()
+    _lib.call("aether_lse_merge", part_o.data_ptr(), part_ml.data_ptr(), sink.data_ptr(),
               G, B, H, out.data_ptr(), _stream(part_o.device))
     return out
 

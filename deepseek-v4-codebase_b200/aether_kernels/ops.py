@@ -90,6 +90,81 @@ def tq_encode_into_pages(x: torch.Tensor, bits: int, page_table: torch.Tensor, s
               page_pool.data_ptr(), None if err is None else err.data_ptr(), _stream(x.device))
 
 
+def compress_emit(c0: torch.Tensor, z0: torch.Tensor, bias0: Optional[torch.Tensor] = None,
+                  c1: Optional[torch.Tensor] = None, z1: Optional[torch.Tensor] = None,
+                  bias1: Optional[torch.Tensor] = None, has_seg1: Optional[torch.Tensor] = None,
+                  positions: Optional[torch.Tensor] = None, inv_freq: Optional[torch.Tensor] = None,
+                  norm_weight: Optional[torch.Tensor] = None, norm_eps: float = 1e-6, bits: int = 8,
+                  page_table: Optional[torch.Tensor] = None, slot_pos: Optional[torch.Tensor] = None,
+                  page_pool: Optional[torch.Tensor] = None, seed: int = 42, want_out: bool = True,
+                  err: Optional[torch.Tensor] = None) -> Optional[torch.Tensor]:
+    """Fused compress-on-emit for B finishing blocks of one stream.
+
+    ``entry = RMSNorm(RoPE(sum_r softmax_r(z_r + bias_r) * c_r))`` per channel
+    over the rows of segment 0 (c0 / z0 [B, m, d]) and, where has_seg1[b],
+    segment 1 (c1 / z1 [B, m1, d], CSA's previous-block half), as
+    aether_2b/serving.py:495-505 (HCA) and :540-575 (CSA main: RoPE + norm;
+    CSA index: neither).  RoPE applies when ``inv_freq`` is given (rope_dim =
+    2 * len(inv_freq)); RMSNorm when ``norm_weight`` is given.  With
+    ``page_pool`` the entry is TurboQuant-encoded into slot ``slot_pos[b]``
+    of sequence b's pages.  Returns the fp32 entry [B, d] when ``want_out``."""
+    _cuda(c0, "c0")
+    _cuda(z0, "z0")
+    _check(c0.dim() == 3 and z0.shape == c0.shape, "c0 and z0 must have the same shape [B, m, d]")
+    B, m0, d = c0.shape
+    _check(c0.dtype == z0.dtype, "c and z must share a dtype")
+    dev = c0.device
+
+    def f32(t, shape, nm):
+        if t is None:
+            return None
+        _cuda(t, nm)
+        _check(t.dtype == torch.float32 and tuple(t.shape) == tuple(shape), f"{nm} must be float32 {list(shape)}")
+        return t.contiguous()
+
+    bias0 = f32(bias0, (m0, d), "bias0")
+    m1 = 0
+    if c1 is not None:
+        _cuda(c1, "c1")
+        _cuda(z1, "z1")
+        _check(c1.dim() == 3 and z1.shape == c1.shape and c1.shape[0] == B and c1.shape[2] == d
+               and c1.dtype == c0.dtype, "c1 / z1 must be [B, m1, d] in c0's dtype")
+        m1 = c1.shape[1]
+        bias1 = f32(bias1, (m1, d), "bias1")
+        if has_seg1 is not None:
+            _cuda(has_seg1, "has_seg1")
+            _check(has_seg1.dtype == torch.int32 and has_seg1.numel() == B, "has_seg1 must be int32 [B]")
+    rope_dim = 0
+    if inv_freq is not None:
+        _cuda(inv_freq, "inv_freq")
+        rope_dim = 2 * inv_freq.numel()
+        _check(positions is not None and positions.is_cuda and positions.dtype == torch.int32
+               and positions.numel() == B, "RoPE needs positions int32 [B]")
+        inv_freq = inv_freq.float().contiguous()
+    norm_weight = f32(norm_weight, (d,), "norm_weight")
+    diag = None
+    if page_pool is not None:
+        for t, nm in ((page_table, "page_table"), (slot_pos, "slot_pos"), (page_pool, "page_pool")):
+            _cuda(t, nm)
+        _check(page_table.dtype == torch.int32 and slot_pos.dtype == torch.int32, "page tables must be int32")
+        rb = d * bits // 8
+        _check(page_pool.dtype == torch.uint8 and page_pool.dim() == 2 and page_pool.shape[1] == 64 * rb + 256,
+               "page_pool must be uint8 [P, 64 * row_bytes + 256]")
+        diag = rademacher_diag(d, seed, dev)
+    out = torch.empty(B, d, dtype=torch.float32, device=dev) if want_out else None
+    ptr = lambda t: None if t is None else t.data_ptr()
+    # contiguous copies are held in locals until the launch is enqueued
+    c0, z0 = c0.contiguous(), z0.contiguous()
+    if c1 is not None:
+        c1, z1 = c1.contiguous(), z1.contiguous()
+    _lib.call("aether_compress_emit", c0.data_ptr(), z0.data_ptr(), ptr(bias0), m0, ptr(c1), ptr(z1),
+              ptr(bias1 if c1 is not None else None), m1, ptr(has_seg1 if c1 is not None else None),
+              _dt(c0, "c0"), B, d, ptr(positions), ptr(inv_freq), rope_dim, ptr(norm_weight), float(norm_eps),
+              bits, ptr(diag), ptr(page_table), 0 if page_table is None else page_table.shape[1], ptr(slot_pos),
+              0 if page_pool is None else page_pool.shape[0], ptr(page_pool), ptr(out), ptr(err), _stream(dev))
+    return out
+
+
 def tq_decode(codes: torch.Tensor, scale: torch.Tensor, bits: int, seed: int = 42,
               out_dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
     _cuda(codes, "data")

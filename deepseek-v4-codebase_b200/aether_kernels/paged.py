@@ -28,7 +28,7 @@ from typing import List, Optional, Sequence, Tuple
 import torch
 
 from . import _lib
-from .ops import _check, _cuda, _stream, rademacher_diag, tq_encode_into_pages
+from .ops import _check, _cuda, _stream, compress_emit, rademacher_diag, tq_encode_into_pages
 
 PAGE = 64
 HEAD_DIM = 128
@@ -52,6 +52,27 @@ class TurboQuantPagedCache:
         self.idx_pages = (torch.zeros(num_pages, PAGE * self.idx_row + PAGE * 4, dtype=torch.uint8,
                                       device=self.device) if with_index else None)
         self._free: List[int] = list(range(num_pages - 1, -1, -1))
+
+    @classmethod
+    def from_pools(cls, kv_pages: torch.Tensor, idx_pages: Optional[torch.Tensor], bits: int,
+                   seed: int = 42) -> "TurboQuantPagedCache":
+        """Wrap existing page pools (e.g. ``PagedKVAllocator.pool('kv')``) without
+        copying; page allocation then belongs to whoever owns the pools."""
+        if bits not in (4, 8):
+            raise ValueError(f"bits must be 4 or 8, got {bits}")
+        self = cls.__new__(cls)
+        self.bits, self.seed = bits, seed
+        self.kv_row, self.idx_row = HEAD_DIM * bits // 8, INDEX_DIM * bits // 8
+        _check(kv_pages.dtype == torch.uint8 and kv_pages.dim() == 2
+               and kv_pages.shape[1] == PAGE * self.kv_row + PAGE * 4, "kv_pages must be uint8 [P, page_bytes]")
+        if idx_pages is not None:
+            _check(idx_pages.dtype == torch.uint8 and idx_pages.shape == (kv_pages.shape[0], PAGE * self.idx_row + PAGE * 4),
+                   "idx_pages must be uint8 [P, page_bytes] with kv_pages' page count")
+        self.kv_pages, self.idx_pages = kv_pages, idx_pages
+        self.num_pages = kv_pages.shape[0]
+        self.device = kv_pages.device
+        self._free = []
+        return self
 
     # ------------------------------------------------------------- views
     @staticmethod
@@ -110,6 +131,35 @@ class TurboQuantPagedCache:
             _check(self.idx_pages is not None, "this cache has no indexer stream")
             tq_encode_into_pages(index, self.bits, page_table, start_pos, self.idx_pages, self.seed, err)
 
+
+    # ---------------------------------------------------- compress-on-emit
+    def emit_hca(self, page_table: torch.Tensor, slot_pos: torch.Tensor, buffer_c: torch.Tensor,
+                 buffer_z: torch.Tensor, positions: torch.Tensor, inv_freq: torch.Tensor,
+                 norm_weight: torch.Tensor, norm_eps: float = 1e-6, err: Optional[torch.Tensor] = None) -> None:
+        """Finish one HCA block per sequence (aether_2b/serving.py:495-505):
+        buffer_c / buffer_z [B, 128, 128] (bias already in z), entry written
+        at logical position slot_pos[b]; one kernel launch."""
+        compress_emit(buffer_c, buffer_z, positions=positions, inv_freq=inv_freq, norm_weight=norm_weight,
+                      norm_eps=norm_eps, bits=self.bits, page_table=page_table, slot_pos=slot_pos,
+                      page_pool=self.kv_pages, seed=self.seed, want_out=False, err=err)
+
+    def emit_csa(self, page_table: torch.Tensor, slot_pos: torch.Tensor, main: Sequence[torch.Tensor],
+                 index: Sequence[torch.Tensor], has_prev: torch.Tensor, positions: torch.Tensor,
+                 inv_freq: torch.Tensor, norm_weight: torch.Tensor, norm_eps: float = 1e-6,
+                 err: Optional[torch.Tensor] = None) -> None:
+        """Finish one CSA block per sequence (aether_2b/serving.py:540-575).
+        ``main`` / ``index`` = (a_c, a_z, bias_a, prev_b_c, prev_b_z, bias_b)
+        with [B, 4, d] halves and [4, d] biases; has_prev int32 [B] (0 for a
+        sequence's first block).  Main entries get RoPE at ``positions`` and
+        RMSNorm, index entries neither; two kernel launches."""
+        _check(self.idx_pages is not None, "this cache has no indexer stream")
+        a_c, a_z, ba, b_c, b_z, bb = main
+        compress_emit(a_c, a_z, ba, b_c, b_z, bb, has_prev, positions=positions, inv_freq=inv_freq,
+                      norm_weight=norm_weight, norm_eps=norm_eps, bits=self.bits, page_table=page_table,
+                      slot_pos=slot_pos, page_pool=self.kv_pages, seed=self.seed, want_out=False, err=err)
+        a_c, a_z, ba, b_c, b_z, bb = index
+        compress_emit(a_c, a_z, ba, b_c, b_z, bb, has_prev, bits=self.bits, page_table=page_table,
+                      slot_pos=slot_pos, page_pool=self.idx_pages, seed=self.seed, want_out=False, err=err)
 
 def csa_workspace_bytes(batch: int, max_nblocks: int) -> int:
     """Workspace bytes of ``csa_decode_paged`` (u32 score key per visible block)."""

@@ -119,12 +119,47 @@ __device__ __forceinline__ bool resolve_row(const RowDst& r, long long row, int 
   return true;
 }
 
+// Quantise a rotated vector (absmax m already clamped) and store one row:
+// codes at row_codes (D or D/2 bytes), scale m / L at *scale.
+template <int D, int BITS>
+__device__ __forceinline__ void quantize_store(const float (&v)[D / 32], float m, int lane, uint8_t* row_codes,
+                                               float* scale) {
+  constexpr int EPL = D / 32;
+  constexpr float L = BITS == 8 ? 127.f : 7.f;
+  if (lane == 0) *scale = __fdiv_rn(m, L);
+  int q[EPL];
+#pragma unroll
+  for (int k = 0; k < EPL; ++k) {
+    float t = rintf(__fmul_rn(__fdiv_rn(v[k], m), L));
+    t = fminf(fmaxf(t, -L), L);
+    q[k] = static_cast<int>(t);
+  }
+  if (BITS == 8) {
+    uint32_t w = 0;
+#pragma unroll
+    for (int k = 0; k < EPL; ++k) w |= (static_cast<uint32_t>(q[k]) & 0xFFu) << (8 * k);
+    uint8_t* base = row_codes + lane * EPL;
+    if (EPL == 4)
+      *reinterpret_cast<uint32_t*>(base) = w;
+    else
+      *reinterpret_cast<uint16_t*>(base) = static_cast<uint16_t>(w);
+  } else {
+    uint32_t w = 0;
+#pragma unroll
+    for (int k = 0; k < EPL; ++k) w |= (static_cast<uint32_t>(q[k]) & 0xFu) << (4 * k);
+    uint8_t* base = row_codes + lane * (EPL / 2);
+    if (EPL == 4)
+      *reinterpret_cast<uint16_t*>(base) = static_cast<uint16_t>(w);
+    else
+      *base = static_cast<uint8_t>(w);
+  }
+}
+
 template <int D, int BITS, typename T>
 __global__ void __launch_bounds__(256) tq_encode_kernel(const T* __restrict__ x, const float* __restrict__ diag,
                                                        uint8_t* __restrict__ codes, float* __restrict__ scales,
                                                        long long rows, RowDst dst, int* err) {
   constexpr int EPL = D / 32;
-  constexpr float L = BITS == 8 ? 127.f : 7.f;
   const int lane = threadIdx.x & 31;
   const long long row = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   if (row >= rows) return;
@@ -144,32 +179,134 @@ __global__ void __launch_bounds__(256) tq_encode_kernel(const T* __restrict__ x,
   long long coff, soff;
   if (!resolve_row(dst, row, RB, err, coff, soff)) return;
   uint8_t* scale_base = dst.page_table ? codes : reinterpret_cast<uint8_t*>(scales);
-  if (lane == 0) *reinterpret_cast<float*>(scale_base + soff) = __fdiv_rn(m, L);
-  int q[EPL];
+  quantize_store<D, BITS>(v, m, lane, codes + coff, reinterpret_cast<float*>(scale_base + soff));
+}
+
+
+// ------------------------------------------------------------ compress-on-emit
+// One source segment of a compressed block: rows [B, rows, D] of values c and
+// gate logits z, plus an optional per-row bias [rows, D] added to z.
+struct EmitSeg {
+  const void* c;
+  const void* z;
+  const float* bias;
+  int rows;
+};
+
+struct EmitParams {
+  EmitSeg s0, s1;            // s1.rows == 0: single segment (HCA)
+  const int32_t* has_s1;     // [B] 0 => s1 skipped for that sequence (CSA first block); null => all use it
+  int B;
+  const int32_t* positions;  // [B] RoPE position of the emitted entry
+  const float* inv_freq;     // [rope_dim / 2]
+  int rope_dim;              // 0 => no RoPE
+  const float* norm_w;       // [D]; null => no RMSNorm
+  float norm_eps;
+  const float* diag;         // [D] Rademacher diagonal
+  uint8_t* pool;             // page pool; null => no cache write
+  float* out;                // [B, D] fp32 compressed entry before quantisation; may be null
+};
+
+// Online softmax over the rows of one segment, per channel.
+template <int D, typename T>
+__device__ __forceinline__ void emit_accumulate(const EmitSeg& sg, int b, int lane, float (&mx)[D / 32],
+                                                float (&den)[D / 32], float (&acc)[D / 32]) {
+  constexpr int EPL = D / 32;
+  const T* c = static_cast<const T*>(sg.c) + static_cast<long long>(b) * sg.rows * D;
+  const T* z = static_cast<const T*>(sg.z) + static_cast<long long>(b) * sg.rows * D;
+  for (int r = 0; r < sg.rows; ++r) {
+#pragma unroll
+    for (int k = 0; k < EPL; ++k) {
+      const int i = lane * EPL + k;
+      float zz = ld_as_float(z + r * D + i);
+      if (sg.bias) zz += sg.bias[r * D + i];
+      const float cc = ld_as_float(c + r * D + i);
+      if (zz > mx[k]) {
+        const float f = expf(mx[k] - zz);  // mx = -inf => 0
+        den[k] = den[k] * f + 1.f;
+        acc[k] = acc[k] * f + cc;
+        mx[k] = zz;
+      } else {
+        const float e = expf(zz - mx[k]);
+        den[k] += e;
+        acc[k] += e * cc;
+      }
+    }
+  }
+}
+
+// One warp per emitting sequence: gated softmax pooling over the block's
+// rows, RoPE of the last rope_dim channels (interleaved pairs), RMSNorm,
+// TurboQuant encode and the write into the sequence's page slot.
+template <int D, int BITS, typename T>
+__global__ void __launch_bounds__(256) compress_emit_kernel(EmitParams p, RowDst dst, int* err) {
+  constexpr int EPL = D / 32;
+  const int lane = threadIdx.x & 31;
+  const int b = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  if (b >= p.B) return;
+  float mx[EPL], den[EPL], acc[EPL];
 #pragma unroll
   for (int k = 0; k < EPL; ++k) {
-    float t = rintf(__fmul_rn(__fdiv_rn(v[k], m), L));
-    t = fminf(fmaxf(t, -L), L);
-    q[k] = static_cast<int>(t);
+    mx[k] = -INFINITY;
+    den[k] = 0.f;
+    acc[k] = 0.f;
   }
-  if (BITS == 8) {
-    uint32_t w = 0;
+  emit_accumulate<D, T>(p.s0, b, lane, mx, den, acc);
+  if (p.s1.rows > 0 && (p.has_s1 == nullptr || p.has_s1[b] != 0)) emit_accumulate<D, T>(p.s1, b, lane, mx, den, acc);
+  float v[EPL];
 #pragma unroll
-    for (int k = 0; k < EPL; ++k) w |= (static_cast<uint32_t>(q[k]) & 0xFFu) << (8 * k);
-    uint8_t* base = codes + coff + lane * EPL;
-    if (EPL == 4)
-      *reinterpret_cast<uint32_t*>(base) = w;
-    else
-      *reinterpret_cast<uint16_t*>(base) = static_cast<uint16_t>(w);
-  } else {
-    uint32_t w = 0;
+  for (int k = 0; k < EPL; ++k) v[k] = den[k] > 0.f ? acc[k] / den[k] : 0.f;
+
+  if (p.rope_dim > 0) {
+    const float pos = static_cast<float>(p.positions[b]);
+    const int first = D - p.rope_dim;
 #pragma unroll
-    for (int k = 0; k < EPL; ++k) w |= (static_cast<uint32_t>(q[k]) & 0xFu) << (4 * k);
-    uint8_t* base = codes + coff + lane * (EPL / 2);
-    if (EPL == 4)
-      *reinterpret_cast<uint16_t*>(base) = static_cast<uint16_t>(w);
-    else
-      *base = static_cast<uint8_t>(w);
+    for (int k = 0; k < EPL; k += 2) {
+      const int i = lane * EPL + k;  // even channel of the pair (i, i + 1)
+      if (i >= first) {
+        const float ang = pos * p.inv_freq[(i - first) >> 1];
+        const float cs = cosf(ang), sn = sinf(ang);
+        const float x0 = v[k], x1 = v[k + 1];
+        v[k] = x0 * cs - x1 * sn;
+        v[k + 1] = x1 * cs + x0 * sn;
+      }
+    }
+  }
+  if (p.norm_w) {
+    float ss = 0.f;
+#pragma unroll
+    for (int k = 0; k < EPL; ++k) ss += v[k] * v[k];
+    ss = warp_sum(ss);
+    const float r = rsqrtf(ss / D + p.norm_eps);
+#pragma unroll
+    for (int k = 0; k < EPL; ++k) v[k] = v[k] * r * p.norm_w[lane * EPL + k];
+  }
+  if (p.out) {
+#pragma unroll
+    for (int k = 0; k < EPL; ++k) p.out[static_cast<long long>(b) * D + lane * EPL + k] = v[k];
+  }
+  if (!p.pool) return;
+#pragma unroll
+  for (int k = 0; k < EPL; ++k) v[k] = __fmul_rn(v[k], p.diag[lane * EPL + k]);
+  warp_wht<D>(v, lane);
+  float m = 0.f;
+#pragma unroll
+  for (int k = 0; k < EPL; ++k) m = fmaxf(m, fabsf(v[k]));
+  m = warp_max(m);
+  m = fmaxf(m, 9.99999993922529e-09f);
+  constexpr int RB = BITS == 8 ? D : D / 2;
+  long long coff, soff;
+  if (!resolve_row(dst, b, RB, err, coff, soff)) return;
+  quantize_store<D, BITS>(v, m, lane, p.pool + coff, reinterpret_cast<float*>(p.pool + soff));
+}
+
+template <int D, int BITS>
+static void launch_emit_t(int dtype, const EmitParams& p, const RowDst& dst, int* err, cudaStream_t st) {
+  const int blocks = (p.B * 32 + 255) / 256;
+  switch (dtype) {
+    case kF32: compress_emit_kernel<D, BITS, float><<<blocks, 256, 0, st>>>(p, dst, err); break;
+    case kF16: compress_emit_kernel<D, BITS, __half><<<blocks, 256, 0, st>>>(p, dst, err); break;
+    default: compress_emit_kernel<D, BITS, __nv_bfloat16><<<blocks, 256, 0, st>>>(p, dst, err);
   }
 }
 
@@ -282,6 +419,35 @@ int aether_tq_encode_into_pages(const void* x, int dtype, int batch, int rows_pe
   RowDst dst{page_table, start_pos, table_stride, rows_per_seq > 0 ? rows_per_seq : 1, num_pages};
   return launch_encode(dtype, x, diag, page_pool, nullptr, static_cast<long long>(batch) * rows_per_seq, d, bits,
                        dst, err, static_cast<cudaStream_t>(stream));
+}
+
+int aether_compress_emit(const void* c0, const void* z0, const float* bias0, int rows0, const void* c1,
+                         const void* z1, const float* bias1, int rows1, const int32_t* has_seg1, int dtype, int B,
+                         int d, const int32_t* positions, const float* inv_freq, int rope_dim,
+                         const float* norm_weight, float norm_eps, int bits, const float* diag,
+                         const int32_t* page_table, int table_stride, const int32_t* slot_pos, int num_pages,
+                         uint8_t* page_pool, float* out, int* err, void* stream) {
+  AETHER_REQUIRE(d == 64 || d == 128, "compress_emit: dim must be 64 or 128, got %d", d);
+  AETHER_REQUIRE(bits == 4 || bits == 8, "bits must be 4 or 8, got %d", bits);
+  AETHER_REQUIRE(dtype >= 0 && dtype <= 2, "compress_emit: unsupported dtype code %d", dtype);
+  AETHER_REQUIRE(B >= 0 && rows0 > 0 && rows1 >= 0, "compress_emit: bad sizes B=%d rows0=%d rows1=%d", B, rows0,
+                 rows1);
+  AETHER_REQUIRE(c0 && z0 && (rows1 == 0 || (c1 && z1)), "compress_emit: missing segment tensors");
+  AETHER_REQUIRE(rope_dim >= 0 && rope_dim <= d && rope_dim % 2 == 0, "compress_emit: rope_dim must be even and <= dim");
+  AETHER_REQUIRE(rope_dim == 0 || (positions && inv_freq), "compress_emit: RoPE needs positions and inv_freq");
+  AETHER_REQUIRE(page_pool == nullptr || (diag && page_table && slot_pos),
+                 "compress_emit: a cache write needs diag, page_table and slot_pos");
+  AETHER_REQUIRE(page_pool != nullptr || out != nullptr, "compress_emit: nothing to write (no page_pool, no out)");
+  if (B == 0) return 0;
+  EmitParams p{{c0, z0, bias0, rows0}, {c1, z1, bias1, rows1}, has_seg1, B, positions, inv_freq, rope_dim,
+               norm_weight, norm_eps, diag, page_pool, out};
+  RowDst dst{page_table, slot_pos, table_stride, 1, num_pages};
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (d == 128 && bits == 8) launch_emit_t<128, 8>(dtype, p, dst, err, st);
+  if (d == 128 && bits == 4) launch_emit_t<128, 4>(dtype, p, dst, err, st);
+  if (d == 64 && bits == 8) launch_emit_t<64, 8>(dtype, p, dst, err, st);
+  if (d == 64 && bits == 4) launch_emit_t<64, 4>(dtype, p, dst, err, st);
+  return check_launch("compress_emit");
 }
 
 int aether_tq_decode(const uint8_t* codes, const float* scales, long long rows, int d, int bits,

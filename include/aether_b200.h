@@ -47,6 +47,26 @@ int aether_tq_encode_into_pages(const void* x, int dtype, int batch, int rows_pe
                                 const int32_t* start_pos, int num_pages, uint8_t* page_pool, int* err,
                                 void* stream);
 
+/* Compress-on-emit for B finishing blocks, one call per stream (replaces
+ * aether_2b/serving.py:495-505 _hca_emit and the main / index halves of
+ * :540-575 _emit_csa_block; model form modeling.py:273-287, 437-482):
+ *   out = RMSNorm(RoPE(sum_r softmax_r(z_r + bias_r) * c_r))   per channel,
+ * softmax over the rows of segment 0 ([B, rows0, d] c0 / z0, bias0 [rows0, d]
+ * or NULL) and, where has_seg1[b] != 0 (has_seg1 NULL = all), segment 1
+ * (CSA's previous-block b half; rows1 = 0 for HCA).  RoPE (rope_dim = 0 to
+ * skip) rotates the last rope_dim channels in interleaved pairs at
+ * positions[b] with inv_freq [rope_dim/2] (modeling.py:122-155);
+ * norm_weight [d] (NULL to skip) applies RMSNorm with norm_eps
+ * (modeling.py:32-41).  The result is TurboQuant-encoded into the page slot
+ * of logical position slot_pos[b] (page_table as aether_tq_encode_into_pages;
+ * page_pool NULL to skip) and, if out is not NULL, stored as fp32 [B, d]. */
+int aether_compress_emit(const void* c0, const void* z0, const float* bias0, int rows0, const void* c1,
+                         const void* z1, const float* bias1, int rows1, const int32_t* has_seg1, int dtype, int B,
+                         int d, const int32_t* positions, const float* inv_freq, int rope_dim,
+                         const float* norm_weight, float norm_eps, int bits, const float* diag,
+                         const int32_t* page_table, int table_stride, const int32_t* slot_pos, int num_pages,
+                         uint8_t* page_pool, float* out, int* err, void* stream);
+
 /* Replaces PolarQuant.decode (aether_2b/turbo_quant.py:168-211). */
 int aether_tq_decode(const uint8_t* codes, const float* scales, long long rows, int d, int bits,
                      const float* diag, void* out, int out_dtype, void* stream);

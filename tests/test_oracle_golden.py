@@ -98,3 +98,30 @@ def test_oracle_csa_step_matches_reference(bits):
                              T(p + "win")[None], torch.tensor([128]), ic, isc, kc, ks, table, torch.tensor([nb]),
                              bits, 256, 128 ** -0.5)
     torch.testing.assert_close(res32.out[0], T(p + "out")[0, 0], atol=1e-5, rtol=1e-5)
+
+
+def _emit_inputs(bits, kind):
+    p = f"emit{bits}_"
+    if kind == "hca":
+        return dict(c0=T(p + "hca_c"), z0=T(p + "hca_z"), positions=T(p + "hca_pos"), inv_freq=T(p + "inv_freq"),
+                    norm_weight=T(p + "norm_w")), (T(p + "hca_codes"), T(p + "hca_scale"))
+    q = p + "csa_"
+    main = dict(c0=T(q + "a_c"), z0=T(q + "a_z"), bias0=T(q + "bias_a"), c1=T(q + "b_c"), z1=T(q + "b_z"),
+                bias1=T(q + "bias_b"), has1=T(q + "has_prev"), positions=T(q + "pos"), inv_freq=T(p + "inv_freq"),
+                norm_weight=T(p + "norm_w"))
+    index = dict(c0=T(q + "ia_c"), z0=T(q + "ia_z"), bias0=T(q + "index_bias_a"), c1=T(q + "ib_c"),
+                 z1=T(q + "ib_z"), bias1=T(q + "index_bias_b"), has1=T(q + "has_prev"))
+    return (main, (T(q + "codes"), T(q + "scale"))), (index, (T(q + "icodes"), T(q + "iscale")))
+
+
+@pytest.mark.parametrize("bits", [8, 4])
+def test_oracle_emit_matches_reference_emit(bits):
+    """oracle.compress.emit reproduces Aether2BServingEngine._hca_emit and
+    _emit_csa_block (serving.py:495-505, 540-575) code for code."""
+    from oracle import compress as ocmp
+
+    cases = [_emit_inputs(bits, "hca")] + list(_emit_inputs(bits, "csa"))
+    for kw, (codes, scale) in cases:
+        _, c, s = ocmp.emit(**kw, bits=bits)
+        assert torch.equal(c, codes)
+        assert torch.equal(s, scale)
