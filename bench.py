@@ -292,7 +292,7 @@ def main():
     assert B % mb == 0
     mbs = B // mb
     side = [torch.cuda.Stream(dev) for _ in range(mb)]
-    ws = [torch.empty(max_ws_bytes(mbs), dtype=torch.uint8, device=dev) for _ in range(mb)]
+    ws = [torch.zeros(max_ws_bytes(mbs), dtype=torch.uint8, device=dev) for _ in range(mb)]
 
     def launch(i, lo, hi, pdl, w):
         s = sets[i % len(sets)]

@@ -211,7 +211,7 @@ def csa_decode_paged(
     [B, >= max_pages * 64]) receives every visible block's index score.
     ``workspace`` (optional uint8 tensor of ``csa_workspace_bytes(B, max_pages
     * 64)`` bytes) holds the per-block score keys between the two kernels;
-    it is allocated per call when not given.
+    it is allocated per call when not given (contents need no clearing).
     """
     B, H, D = q.shape
     _check(D == HEAD_DIM, f"head_dim must be {HEAD_DIM}")
@@ -241,7 +241,7 @@ def csa_decode_paged(
     )
     need = csa_workspace_bytes(B, page_table.shape[1] * PAGE)
     if workspace is None:
-        workspace = torch.empty(max(need, 16), dtype=torch.uint8, device=dev)
+        workspace = torch.zeros(max(need, 16), dtype=torch.uint8, device=dev)
     _check(workspace.is_cuda and workspace.numel() * workspace.element_size() >= need,
            f"workspace must hold {need} bytes")
     if scores is None:

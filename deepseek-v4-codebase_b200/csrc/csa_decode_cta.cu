@@ -49,7 +49,8 @@ constexpr int kMaxKeys = 8192;           // visible blocks per query (32K tokens
 constexpr int kMaxTopK = 256;
 constexpr int kWinMax = 128;
 constexpr int kWRow = kHeadDim * 2 + 16;  // padded bf16 window row (bytes)
-constexpr int kL1Bins = 4096;             // histogram of key >> 19
+constexpr int kL1Bins = 4096;            // histogram of key >> 19
+constexpr int kBoundMax = 512;           // boundary-bin keys ranked directly (more: radix levels)
 constexpr int kMaxPagesLocal = 4096;      // page-table entries per sequence on one device (262144 blocks)
 constexpr int kMaxBlocks = kMaxPagesLocal * kPage;
 
@@ -66,8 +67,8 @@ struct QCfg {
   static constexpr int HPC = (kMaxHeads + CS - 1) / CS;      // heads finalised per CTA (max)
   static constexpr int SLOT = 4 + 2 * kHeadDim;              // merge slot: m, l, pad, pad, O_rot, O_win
   // select phase (aliases the attention buffers below)
-  static constexpr int S_HIST = 0;                           // u32 [4096]
-  static constexpr int S_END = S_HIST + kL1Bins * 4;
+  static constexpr int S_HIST = 0;                           // u32 [4096], then uint2 [kBoundMax]
+  static constexpr int S_END = S_HIST + kL1Bins * 4 + kBoundMax * 8;
   // attention phase
   static constexpr int A_KC = 0;                             // f16 [SL][KROW] expanded codes
   static constexpr int A_KS = A_KC + SL * KROW * 2;          // fp32 [SL]
@@ -176,6 +177,18 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;"); }
 
+// kr[j] for a run-time j < 16 without local memory (binary select tree)
+__device__ __forceinline__ uint32_t pick16(const uint32_t (&kr)[16], int j) {
+  uint32_t a[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) a[i] = (j & 1) ? kr[2 * i + 1] : kr[2 * i];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) a[i] = (j & 2) ? a[2 * i + 1] : a[2 * i];
+#pragma unroll
+  for (int i = 0; i < 2; ++i) a[i] = (j & 4) ? a[2 * i + 1] : a[2 * i];
+  return (j & 8) ? a[1] : a[0];
+}
+
 // Block-wide inclusive scan of one u32 per thread; uses wtot[0..63].
 __device__ __forceinline__ uint32_t block_scan_incl(uint32_t v, uint32_t* wtot, int lane, int warp) {
   uint32_t inc = v;
@@ -204,8 +217,17 @@ __device__ __forceinline__ uint32_t block_scan_incl(uint32_t v, uint32_t* wtot, 
 __device__ __forceinline__ void find_bin(const uint32_t* hist, int nbins, uint32_t R, uint32_t* wtot, QMisc* misc,
                                          int tid, int lane, int warp) {
   const int per = nbins / kQThreads;
+  // thread tid owns the contiguous bins [nbins - per * (tid + 1), nbins - per * tid)
   uint32_t s = 0;
-  for (int k = 0; k < per; ++k) s += hist[nbins - 1 - (tid * per + k)];
+  const uint32_t* mine = hist + nbins - per * (tid + 1);
+  if (per % 4 == 0) {
+    for (int k = 0; k < per; k += 4) {
+      const uint4 v = *reinterpret_cast<const uint4*>(mine + k);
+      s += (v.x + v.y) + (v.z + v.w);
+    }
+  } else {
+    for (int k = 0; k < per; ++k) s += mine[k];
+  }
   const uint32_t inc = block_scan_incl(s, wtot, lane, warp);
   const uint32_t exc = inc - s;
   if (exc < R && inc >= R) {
@@ -354,12 +376,8 @@ __global__ void __launch_bounds__(kSThreads) csa_score_kernel(QParams p, int spl
   const int g = lane >> 2, t = lane & 3;
   // profiling aid: phase timestamps after the attend kernel's area
   long long* dbg = p.dbg ? p.dbg + 65536 + blockIdx.x * 8 : nullptr;
-  auto stamp = [&](int slot) {
-    if (dbg && tid == 0) {
-      long long ts;
-      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(ts));
-      dbg[slot] = ts;
-    }
+  auto stamp = [&](int slot) {  // SM clock cycles (phase durations)
+    if (dbg && tid == 0) dbg[slot] = clock64();
   };
   stamp(0);
   pdl_launch_dependents();
@@ -505,7 +523,10 @@ __global__ void __launch_bounds__(kSThreads) csa_score_kernel(QParams p, int spl
 }
 
 template <int BITS, int CS>
-__global__ void __launch_bounds__(kQThreads, CS > 1 ? 2 : 1) csa_attend_kernel(QParams p) {
+#ifndef AETHER_ATTEND_MINB
+#define AETHER_ATTEND_MINB 2
+#endif
+__global__ void __launch_bounds__(kQThreads, CS > 1 ? AETHER_ATTEND_MINB : 1) csa_attend_kernel(QParams p) {
   using C = QCfg<BITS, CS>;
   extern __shared__ __align__(128) uint8_t smem[];
   // grid: ((sequence * chunks) + chunk) * CS + rank; a cluster of CS CTAs
@@ -516,12 +537,8 @@ __global__ void __launch_bounds__(kQThreads, CS > 1 ? 2 : 1) csa_attend_kernel(Q
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, t = lane & 3;
   const bool select_only = p.sel_keys_out != nullptr;
-  auto stamp = [&](int slot, bool who) {
-    if (p.dbg && who) {
-      long long ts;
-      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(ts));
-      p.dbg[blockIdx.x * 16 + slot] = ts;
-    }
+  auto stamp = [&](int slot, bool who) {  // SM clock cycles (phase durations)
+    if (p.dbg && who) p.dbg[blockIdx.x * 16 + slot] = clock64();
   };
   stamp(0, tid == 0);
   pdl_launch_dependents();
@@ -566,7 +583,7 @@ __global__ void __launch_bounds__(kQThreads, CS > 1 ? 2 : 1) csa_attend_kernel(Q
       pt[i] = v;
     }
   }
-  for (int i = tid; i < kL1Bins; i += kQThreads) hist[i] = 0;
+  for (int i = tid; i < kL1Bins / 4; i += kQThreads) reinterpret_cast<uint4*>(hist)[i] = make_uint4(0, 0, 0, 0);
   if (tid < kMaxTopK) sel[tid] = 0;  // every slot holds a valid position
   if (tid == 0) {
     misc->thr = 0;
@@ -576,6 +593,7 @@ __global__ void __launch_bounds__(kQThreads, CS > 1 ? 2 : 1) csa_attend_kernel(Q
     misc->cnt = 0;
     misc->nvalid = 0;
     misc->nown = 0;
+    misc->ncand = 0;
   }
   // window rows other than the newest are cache state: prefetch them now
   {
@@ -600,6 +618,11 @@ __global__ void __launch_bounds__(kQThreads, CS > 1 ? 2 : 1) csa_attend_kernel(Q
       if (i0 + 4 * v < n) x = __ldcg(reinterpret_cast<const uint4*>(src) + v);
       kr[4 * v] = x.x; kr[4 * v + 1] = x.y; kr[4 * v + 2] = x.z; kr[4 * v + 3] = x.w;
     }
+  }
+  // the prologue's zero-fill of the histogram and of misc happens-before
+  // any update (the key loads above are already in flight)
+  __syncthreads();
+  {
     uint32_t cnt = 0;
 #pragma unroll
     for (int j = 0; j < PER; ++j) {
@@ -627,66 +650,103 @@ __global__ void __launch_bounds__(kQThreads, CS > 1 ? 2 : 1) csa_attend_kernel(Q
   // ------------------------------------------------------------- select
   // Result: every key > thr is taken, and the take_eq lowest-position keys
   // == thr.  Keys are >= 1 for real blocks, so thr = 0 takes all of them.
-  // The refinement histograms are built from the keys held in registers.
+  // After the bin b1 of the K-th largest key (bins of key >> 19) is known,
+  // later steps walk `wmask`, the bit set of this thread's keys in bins >= b1.
+  uint32_t wmask = 0;
+#pragma unroll
+  for (int j = 0; j < PER; ++j) wmask |= static_cast<uint32_t>(kr[j] != 0u) << j;
   if (nvalid > K) {
-    uint32_t R = static_cast<uint32_t>(K);
-    find_bin(hist, kL1Bins, R, wtot, misc, tid, lane, warp);
-    const uint32_t b1 = misc->bin;
-    R -= misc->above;
-    if (misc->cnt == R) {
+    find_bin(hist, kL1Bins, static_cast<uint32_t>(K), wtot, misc, tid, lane, warp);
+    const uint32_t b1 = misc->bin, ccnt = misc->cnt;
+    const uint32_t R = static_cast<uint32_t>(K) - misc->above;  // keys still to take from bin b1
+    wmask = 0;
+#pragma unroll
+    for (int j = 0; j < PER; ++j) wmask |= static_cast<uint32_t>(kr[j] != 0u && (kr[j] >> 19) >= b1) << j;
+    if (ccnt == R) {
       if (tid == 0) misc->thr = b1 << 19;  // lowest key of bin b1: the whole bin is taken
+    } else if (ccnt <= static_cast<uint32_t>(kBoundMax)) {
+      // rank the keys of bin b1 exactly: (key desc, position asc)
+      uint2* cand = reinterpret_cast<uint2*>(hist + kL1Bins);
+      for (uint32_t m = wmask; m; m &= m - 1u) {
+        const int j = __ffs(m) - 1;
+        const uint32_t kj = pick16(kr, j);
+        if ((kj >> 19) == b1) cand[atomicAdd(&misc->ncand, 1u)] = make_uint2(kj, i0 + j);
+      }
+      __syncthreads();
+      for (int i = tid; i < static_cast<int>(ccnt); i += kQThreads) {
+        const uint2 me = cand[i];
+        uint32_t rank = 0, eq_before = 0;
+        for (int k2 = 0; k2 < static_cast<int>(ccnt); ++k2) {
+          const uint2 o = cand[k2];
+          rank += o.x > me.x || (o.x == me.x && o.y < me.y);
+          eq_before += o.x == me.x && o.y < me.y;
+        }
+        if (rank == R - 1) {  // the last key taken
+          misc->thr = me.x;
+          misc->take_eq = eq_before + 1;
+        }
+      }
     } else {
+      // many keys share bin b1: two more radix levels over those keys
+      uint32_t R2 = R;
       for (int i = tid; i < 2048; i += kQThreads) hist[i] = 0;
       __syncthreads();
-#pragma unroll
-      for (int j = 0; j < PER; ++j)
-        if (kr[j] != 0u && (kr[j] >> 19) == b1) atomicAdd(&hist[(kr[j] >> 8) & 2047u], 1u);
+      for (uint32_t m = wmask; m; m &= m - 1u) {
+        const uint32_t kj = pick16(kr, __ffs(m) - 1);
+        if ((kj >> 19) == b1) atomicAdd(&hist[(kj >> 8) & 2047u], 1u);
+      }
       __syncthreads();
-      find_bin(hist, 2048, R, wtot, misc, tid, lane, warp);
+      find_bin(hist, 2048, R2, wtot, misc, tid, lane, warp);
       const uint32_t b2 = misc->bin;
-      R -= misc->above;
+      R2 -= misc->above;
       const uint32_t pfx = (b1 << 11) | b2;  // key >> 8
-      if (misc->cnt == R) {
+      if (misc->cnt == R2) {
         if (tid == 0) misc->thr = pfx << 8;  // the whole sub-bin is taken
       } else {
         for (int i = tid; i < kQThreads; i += kQThreads) hist[i] = 0;
         __syncthreads();
-#pragma unroll
-        for (int j = 0; j < PER; ++j)
-          if (kr[j] != 0u && (kr[j] >> 8) == pfx) atomicAdd(&hist[kr[j] & 255u], 1u);
+        for (uint32_t m = wmask; m; m &= m - 1u) {
+          const uint32_t kj = pick16(kr, __ffs(m) - 1);
+          if ((kj >> 8) == pfx) atomicAdd(&hist[kj & 255u], 1u);
+        }
         __syncthreads();
-        find_bin(hist, kQThreads, R, wtot, misc, tid, lane, warp);  // 256 used bins of 512
-        R -= misc->above;
+        find_bin(hist, kQThreads, R2, wtot, misc, tid, lane, warp);  // 256 used bins of 512
+        R2 -= misc->above;
         if (tid == 0) {
           misc->thr = (pfx << 8) | static_cast<uint32_t>(misc->bin);
-          misc->take_eq = R;  // keys equal to thr: the lowest-position R of them
+          misc->take_eq = R2;  // keys equal to thr: the lowest-position R2 of them
         }
       }
     }
   }
   __syncthreads();
   stamp(4, tid == 0);
-  // ordered compaction from registers: thread order is source order
+  // ordered compaction over wmask: thread order is source order.  On the
+  // implicit (single-device, in-order) source every winner is held here, so
+  // the attended list `own` is written directly.
+  const bool direct_own = !explicit_list && p.id_base == 0 && !select_only;
   {
     const uint32_t thr = misc->thr, take_eq = misc->take_eq;
     uint32_t cs = 0, ce = 0;
-#pragma unroll
-    for (int j = 0; j < PER; ++j) {
-      cs += kr[j] != 0u && kr[j] > thr;
-      ce += kr[j] != 0u && kr[j] == thr;
+    for (uint32_t m = wmask; m; m &= m - 1u) {
+      const uint32_t kj = pick16(kr, __ffs(m) - 1);
+      cs += kj > thr;
+      ce += kj == thr;
     }
     const uint32_t packed = cs | (ce << 16);
     const uint32_t exc = block_scan_incl(packed, wtot, lane, warp) - packed;
     uint32_t sb = exc & 0xFFFFu, eb = exc >> 16;  // 16-bit fields: at most 8192 keys
-    if (cs | ce) {
-#pragma unroll
-      for (int j = 0; j < PER; ++j) {
-        const bool st = kr[j] != 0u && kr[j] > thr, eq = kr[j] != 0u && kr[j] == thr;
-        const uint32_t pos = st ? sb + min(eb, take_eq) : sb + eb;
-        if ((st || (eq && eb < take_eq)) && pos < static_cast<uint32_t>(K)) sel[pos] = i0 + j;
-        sb += st;
-        eb += eq;
+    for (uint32_t m = (cs | ce) ? wmask : 0u; m; m &= m - 1u) {
+      const int j = __ffs(m) - 1;
+      const uint32_t kj = pick16(kr, j);
+      const bool st = kj > thr, eq = kj == thr;
+      const uint32_t pos = st ? sb + min(eb, take_eq) : sb + eb;
+      if ((st || (eq && eb < take_eq)) && pos < static_cast<uint32_t>(K)) {
+        sel[pos] = i0 + j;
+        if (direct_own) own[pos] = chunk * kMaxKeys + i0 + j;
       }
+      sb += st;
+      eb += eq;
     }
   }
   __syncthreads();
@@ -711,7 +771,9 @@ __global__ void __launch_bounds__(kQThreads, CS > 1 ? 2 : 1) csa_attend_kernel(Q
     for (int i = tid; i < p.top_k; i += kQThreads) so[i] = i < K ? gid_of(sel[i]) : -1;
   }
   // the selected blocks held on this device, as local ids (order kept)
-  if (warp == 0) {
+  if (direct_own) {
+    if (tid == 0) misc->nown = K;
+  } else if (warp == 0) {
     uint32_t base = 0;
     for (int r0 = 0; r0 < K; r0 += 32) {
       const int i = r0 + lane;
@@ -929,6 +991,7 @@ __global__ void __launch_bounds__(kQThreads, CS > 1 ? 2 : 1) csa_attend_kernel(Q
   if constexpr (CS > 1) cg::this_cluster().sync();
   else __syncthreads();
   stamp(9, tid == 0);
+
   // ---- owner: merge the CS partials of its heads, inverse rotation, then
   // the final sink-normalised bf16 output or the partial (O, max, sum)
   {
@@ -1114,9 +1177,9 @@ static int run_decode(QParams p, int B, int max_nblocks, bool pdl, cudaStream_t 
     const char* e = getenv("AETHER_DECODE_ONLY");
     return e ? atoi(e) : 0;
   }();
+  const int chunks = (max_nblocks + kMaxKeys - 1) / kMaxKeys;
   if (only != 2) rc = launch_score<BITS>(p, B, max_nblocks, pdl, st);
   if (rc || only == 1) return rc;
-  const int chunks = (max_nblocks + kMaxKeys - 1) / kMaxKeys;
   static const bool attend_pdl = [] {
     const char* e = getenv("AETHER_ATTEND_PDL");
     return !(e && e[0] == '0');
@@ -1207,8 +1270,9 @@ __global__ void lse_merge_kernel(const float* __restrict__ part_o, const float* 
 using namespace aether;
 
 // Profiling aid: when buf is non-null, later CSA decode launches record
-// per-CTA phase timestamps (%globaltimer, ns) of the attend kernel into
-// buf[cta * 16 + phase].
+// per-CTA phase timestamps (SM clock64 cycles) of the attend kernel into
+// buf[cta * 16 + phase] and of the score kernel into buf[65536 + cta * 8 +
+// phase]; buf must hold 65536 + 8 * (score grid size) entries.
 extern "C" void aether_csa_decode_set_debug_timer(long long* buf) { aether::g_cta_debug = buf; }
 
 extern "C" size_t aether_csa_decode_workspace_bytes(int B, int max_nblocks) {

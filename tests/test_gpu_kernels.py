@@ -315,3 +315,50 @@ def test_kernels_against_reference_golden_vectors(ak):
     got = ext.sparse_sink_attention(*(torch.from_numpy(G[k]).cuda() for k in ("sa_q", "sa_kv", "sa_idx", "sa_sink")),
                                     0.125)
     torch.testing.assert_close(got.cpu(), torch.from_numpy(G["sa_out"]), atol=1e-5, rtol=1e-5)
+
+
+def test_csa_decode_dirty_workspace(ak):
+    """Results never depend on the workspace's previous contents."""
+    from aether_kernels.paged import csa_decode_paged, csa_workspace_bytes
+    from aether_kernels.synthetic import make_decode_batch
+
+    batch = make_decode_batch("csa", 8, 4000, 30000, 4, 4, seed=23, device="cuda")
+    args = (batch.q, batch.index_q, batch.index_weight, batch.sink, batch.window, batch.window_len, batch.cache,
+            batch.page_table, batch.nblocks, batch.softmax_scale)
+    need = csa_workspace_bytes(8, batch.page_table.shape[1] * 64)
+    ref_out, ref_sel = csa_decode_paged(*args, workspace=torch.zeros(need, dtype=torch.uint8, device="cuda"))
+    for fill in (7, 255):
+        ws = torch.full((need,), fill, dtype=torch.uint8, device="cuda")
+        out, sel = csa_decode_paged(*args, workspace=ws)
+        torch.cuda.synchronize()
+        assert torch.equal(sel, ref_sel)
+        assert torch.equal(out, ref_out)
+    _check_decode(batch, ref_out, ref_sel)
+
+
+@pytest.mark.parametrize("distinct", [2, 40, 300])
+def test_csa_decode_repeated_entries(ak, distinct):
+    """Index entries drawn from a few distinct vectors: scores repeat many
+    times, so the boundary of the top-k falls inside a run of equal keys
+    (lowest block indices must win) and the boundary bin holds from tens to
+    thousands of keys."""
+    from aether_kernels.synthetic import make_decode_batch
+
+    batch = make_decode_batch("csa", 3, 20000, 32000, 4, 4, seed=31 + distinct, device="cuda")
+    c = batch.cache
+    g = torch.Generator().manual_seed(distinct)
+    for row in range(3):
+        nbr = int(batch.nblocks[row])
+        pages = batch.page_table[row, : (nbr + 63) // 64].long()
+        codes = c.idx_codes[pages].reshape(-1, c.idx_codes.shape[-1])[:nbr]
+        scales = c.idx_scale[pages].reshape(-1)[:nbr]
+        pick = torch.randint(0, distinct, (nbr,), generator=g).to(codes.device)
+        new_codes, new_scales = codes[:distinct][pick], scales[:distinct][pick]
+        flat_c = c.idx_codes[pages].reshape(-1, c.idx_codes.shape[-1])
+        flat_s = c.idx_scale[pages].reshape(-1)
+        flat_c[:nbr] = new_codes
+        flat_s[:nbr] = new_scales
+        c.idx_codes[pages] = flat_c.view(len(pages), 64, -1)
+        c.idx_scale[pages] = flat_s.view(len(pages), 64)
+    out, sel = _run_decode(ak, batch)
+    _check_decode(batch, out, sel)
