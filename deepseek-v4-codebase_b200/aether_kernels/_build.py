@@ -13,7 +13,7 @@ from typing import List, Optional
 
 PKG = Path(__file__).resolve().parent
 CSRC = PKG.parent / "csrc"
-SOURCES = ["capi.cu", "tq.cu", "compat.cu", "csa_decode.cu", "csa_decode_cta.cu"]
+SOURCES = ["capi.cu", "tq.cu", "compat.cu", "csa_decode.cu", "csa_decode_cta.cu", "csa_prefill.cu"]
 OUT = PKG / "libaether_b200.so"
 
 NVCC_FLAGS = [

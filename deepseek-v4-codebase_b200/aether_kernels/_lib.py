@@ -91,6 +91,12 @@ SIGNATURES = {
          _c_int, _c_int, _c_int, _c_int, _c_int, _c_f, _p, _p, _p, _p, _p, _p],
     ),
     "aether_lse_merge": (_c_int, [_p, _p, _p, _c_int, _c_int, _c_int, _p, _p]),
+    "aether_csa_prefill_topk": (
+        _c_int,
+        [_p, _p, _p, _p, _c_int, _c_int,     # index_q, index_w, idx_pages, page_table, stride, num_pages
+         _p, _p, _c_int, _c_int, _p, _c_int, _c_int,  # req_info, tiles, ntiles, compression, diag, bits, top_k
+         _p, _p, _p, _p],                    # cand_keys, cand_ids, err, stream
+    ),
     "aether_hca_decode_paged": (
         _c_int,
         [

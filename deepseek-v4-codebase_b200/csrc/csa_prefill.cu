@@ -1,0 +1,563 @@
+// Chunked-prefill CSA indexer on the 5th-generation tensor cores (sm_100a):
+// tcgen05.mma with operands in shared memory and accumulators in TMEM.
+//
+// Semantics (reference itz-sayak/deepseek-v4-codebase, aether_2b/modeling.py
+// :591-615): for every query token t of a prefill chunk
+//   score[s] = sum_h softplus(w_h) * relu(q_h . k_s)   over the causally
+//   visible compressed blocks s < t // compression (modeling.py:612-614),
+// and the exact top-k (score desc, block index asc) of those blocks.  Keys
+// come from the paged TurboQuant cache (codes c, per-entry scale); queries
+// are rotated once (q . decode(c) = scale * (WHT(diag * q) . c)).
+//
+// Numerics.  The rotated query of head h is put in 22-bit fixed point,
+// q_int = rint(q_rot / s_h) with s_h = max|q_rot| / 2^21, and split into two
+// limbs q_int = 2048 a + b with |a|, |b| <= 1024, both exact in fp16.  Codes
+// are exact in fp16 (|c| <= 127).  Each limb's 64-term dot product is an
+// integer below 2^24, so the fp32 tensor-core accumulation is exact; the
+// epilogue forms dot = 2048 D_a + D_b (one rounding), then
+// score = (sum_h alpha_h relu(dot_h)) * scale with alpha_h = softplus(w_h) s_h.
+//
+// Tiling.  One CTA serves 32 query tokens of one request.  The MMA is
+//   D[128 keys x 256] = A[128 keys x 64 dims] * B[256 x 64 dims]^T
+// with B's 256 rows = 32 queries x 4 heads x 2 limbs, so the head sum is
+// within one TMEM lane (no shuffles).  Two 256-column accumulators in TMEM
+// (512 columns) let the epilogue of tile j overlap the MMAs of tile j + 1.
+//
+// Warp roles (512 threads):
+//   warp 0       bulk (TMA) copies of the two index pages of each key tile
+//   warp 1       MMA issue (one thread) and tcgen05.commit
+//   warps 4-7    codes -> fp16 in the canonical no-swizzle K-major layout
+//   warps 8-15   epilogue: TMEM -> registers, scores, streaming top-k
+// Streaming top-k: per query a candidate buffer (key, block) with a running
+// threshold T; a key enters if key > T.  When a buffer passes 384 entries a
+// warp radix-selects the k-th largest (ties to the lower block index), keeps
+// exactly k entries and raises T to that key; later keys equal to T lose the
+// tie (they have higher block indices).  At the end the exact top-k of the
+// buffer is written in ascending block order.
+#include "capi_util.cuh"
+#include "common.cuh"
+
+namespace aether {
+namespace prefill {
+
+constexpr int kThreads = 512;
+constexpr int kQ = 32;                  // query tokens per CTA
+constexpr int kTileKeys = 128;          // keys per MMA tile (M)
+constexpr int kN = kQ * kIdxHeads * 2;  // 256 accumulator columns per tile
+constexpr int kCap = 512;               // candidate buffer entries per query
+constexpr int kPruneAt = kCap - kTileKeys;
+constexpr int kMaxK = 256;
+constexpr uint32_t kLBO = 128, kSBO = 1024;  // canonical layout strides (bytes)
+
+template <int BITS>
+struct Cfg {
+  static constexpr int RB = kIdxDim * BITS / 8;
+  static constexpr int PB = page_bytes(RB);
+  static constexpr int RAW_SLOTS = BITS == 4 ? 3 : 2;
+  static constexpr int RAW_BYTES = 2 * PB;  // two pages per 128-key tile
+  static constexpr int OFF_B = 0;                               // fp16 [256][64] canonical
+  static constexpr int OFF_A = OFF_B + kN * kIdxDim * 2;        // fp16 [2][128][64] canonical
+  static constexpr int OFF_RAW = OFF_A + 2 * kTileKeys * kIdxDim * 2;
+  static constexpr int OFF_SCL = OFF_RAW + RAW_SLOTS * ((RAW_BYTES + 127) & ~127);  // fp32 [4][128]
+  static constexpr int OFF_BUF = OFF_SCL + 4 * kTileKeys * 4;   // uint2 [32][kCap]
+  static constexpr int OFF_HIST = OFF_BUF + kQ * kCap * 8;      // u32 [8 warps][256]
+  static constexpr int OFF_MISC = OFF_HIST + 8 * 256 * 4;
+  static constexpr int SMEM = OFF_MISC + 2048;
+  static_assert(SMEM <= 232448, "shared memory");
+  static_assert(OFF_MISC % 16 == 0 && OFF_BUF % 16 == 0 && OFF_SCL % 16 == 0, "alignment");
+};
+
+struct alignas(16) Misc {
+  float alpha[kQ][kIdxHeads];  // first: read as float4
+  uint64_t raw_full[3], raw_empty[3], a_full[2], a_empty[2], acc_full[2], acc_empty[2];
+  uint32_t tmem;
+  int abort_flag;
+  int ntiles;
+  uint32_t thr[kQ];
+  uint32_t cnt[kQ];
+  int vis[kQ];
+};
+static_assert(sizeof(Misc) <= 2048, "misc area");
+
+struct Params {
+  const float* index_q;    // [Qtot][4][64]
+  const float* index_w;    // [Qtot][4]
+  const uint8_t* idx_pages;
+  const int32_t* page_table;
+  const int32_t* req_info;  // [R][4]: first query row, query count, position of query 0, blocks in cache
+  const int32_t* tiles;     // [ntiles][2]: request, first query within the request
+  const float* diag_idx;
+  uint32_t* cand_keys;      // [Qtot][top_k]
+  int32_t* cand_ids;        // [Qtot][top_k]
+  int* err;
+  int table_stride, num_pages, compression, top_k;
+};
+
+__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>((kLBO >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>((kSBO >> 4) & 0x3FFFu) << 32;
+  d |= static_cast<uint64_t>(1) << 46;  // sm100 descriptor version; no swizzle, base offset 0
+  return d;
+}
+// kind::f16 instruction descriptor: D f32, A and B f16, both K-major, N x M
+__host__ __device__ constexpr uint32_t umma_idesc(int n, int m) {
+  return (1u << 4) | (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
+}
+// byte offset of element (row r, k) in the canonical no-swizzle K-major layout
+__device__ __forceinline__ uint32_t canon(int r, int k) {
+  return (r >> 3) * kSBO + (k >> 3) * kLBO + (r & 7) * 16 + (k & 7) * 2;
+}
+
+__device__ __forceinline__ void mbar_arrive_cta(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+// Bounded wait; a timeout sets the CTA's abort flag so every role winds down.
+__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, Misc* m, int* err) {
+  if (*reinterpret_cast<volatile int*>(&m->abort_flag)) return false;
+  if (mbar_wait(bar, parity, err)) return true;
+  *reinterpret_cast<volatile int*>(&m->abort_flag) = 1;
+  return false;
+}
+__device__ __forceinline__ void named_sync(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+// nibble pair of one byte -> half2(lo, hi), exact signed values
+__device__ __forceinline__ uint32_t nib2h2(uint32_t byte) {
+  uint32_t y = (byte & 0xFu) | ((byte & 0xF0u) << 12);
+  y = (y ^ 0x00080008u) | 0x64006400u;  // 1024 + (v + 8)
+  __half2 h = *reinterpret_cast<__half2*>(&y);
+  h = __hsub2(h, __halves2half2(__ushort_as_half(0x6408), __ushort_as_half(0x6408)));  // - 1032
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+// two int8 codes (low 16 bits of w) -> half2
+__device__ __forceinline__ uint32_t s8x2h2(uint32_t w) {
+  uint32_t y = __byte_perm(w ^ 0x8080u, 0x64646464u, 0x5140);  // 1024 + (v + 128)
+  __half2 h = *reinterpret_cast<__half2*>(&y);
+  h = __hsub2(h, __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480)));  // - 1152
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// ---------------------------------------------------------------- selection
+// One warp: the K-th largest key of n entries (key desc, block asc), keeping
+// exactly min(K, n) of them at the front of buf (order not kept).  Returns
+// the threshold key.  MSB-first radix select over 8-bit digits with a
+// warp-private 256-bin histogram.
+__device__ uint32_t warp_prune(uint2* buf, int n, int K, uint32_t* hist, int lane) {
+  uint32_t prefix = 0, R = static_cast<uint32_t>(K);
+  for (int d = 3; d >= 0; --d) {
+    for (int i = lane; i < 256; i += 32) hist[i] = 0;
+    __syncwarp();
+    for (int i = lane; i < n; i += 32) {
+      const uint32_t k = buf[i].x;
+      if (d == 3 || ((k ^ prefix) >> (8 * (d + 1))) == 0u) atomicAdd(&hist[(k >> (8 * d)) & 255u], 1u);
+    }
+    __syncwarp();
+    // lane l owns bins [248 - 8 l, 256 - 8 l), scanned from the top
+    uint32_t c[8], s = 0;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      c[k] = hist[255 - 8 * lane - k];
+      s += c[k];
+    }
+    uint32_t inc = s;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t u = __shfl_up_sync(0xffffffffu, inc, o);
+      if (lane >= o) inc += u;
+    }
+    const int L = __ffs(__ballot_sync(0xffffffffu, inc >= R)) - 1;
+    uint32_t digit = 0, above = 0;
+    if (lane == L) {
+      uint32_t cum = inc - s;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        if (cum + c[k] >= R) {
+          digit = 255u - 8u * lane - k;
+          above = cum;
+          break;
+        }
+        cum += c[k];
+      }
+    }
+    digit = __shfl_sync(0xffffffffu, digit, L);
+    above = __shfl_sync(0xffffffffu, above, L);
+    prefix |= digit << (8 * d);
+    R -= above;
+    __syncwarp();
+  }
+  const uint32_t thr = prefix, take_eq = R;
+  // equal keys beyond take_eq: keep the lowest block indices
+  uint32_t eq = 0;
+  for (int i = lane; i < n; i += 32) eq += buf[i].x == thr;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) eq += __shfl_xor_sync(0xffffffffu, eq, o);
+  // keep flags first (one bit per round and lane; n <= 512), then an
+  // in-order compaction whose writes never pass the reads of the same round
+  uint32_t keepm = 0;
+  for (int i0 = 0, rd = 0; i0 < n; i0 += 32, ++rd) {
+    const int i = i0 + lane;
+    bool keep = false;
+    if (i < n) {
+      const uint2 e = buf[i];
+      keep = e.x > thr;
+      if (e.x == thr) {
+        if (eq <= take_eq) {
+          keep = true;
+        } else {
+          uint32_t before = 0;
+          for (int j = 0; j < n; ++j) {
+            const uint2 o = buf[j];
+            before += o.x == thr && o.y < e.y;
+          }
+          keep = before < take_eq;
+        }
+      }
+    }
+    keepm |= static_cast<uint32_t>(keep) << rd;
+  }
+  __syncwarp();
+  uint32_t out = 0;
+  for (int i0 = 0, rd = 0; i0 < n; i0 += 32, ++rd) {
+    const int i = i0 + lane;
+    const bool keep = (keepm >> rd) & 1u;
+    const uint2 e = keep ? buf[i] : make_uint2(0, 0);
+    const uint32_t bal = __ballot_sync(0xffffffffu, keep);
+    __syncwarp();
+    if (keep) buf[out + __popc(bal & ((1u << lane) - 1u))] = e;
+    out += __popc(bal);
+    __syncwarp();
+  }
+  return thr;
+}
+
+template <int BITS>
+__global__ void __launch_bounds__(kThreads, 1) csa_prefill_index_kernel(Params p) {
+  using C = Cfg<BITS>;
+  extern __shared__ __align__(1024) uint8_t smem[];
+  Misc* m = reinterpret_cast<Misc*>(smem + C::OFF_MISC);
+  uint2* cbuf = reinterpret_cast<uint2*>(smem + C::OFF_BUF);
+  float* sscl = reinterpret_cast<float*>(smem + C::OFF_SCL);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int req = p.tiles[blockIdx.x * 2], q0 = p.tiles[blockIdx.x * 2 + 1];
+  const int row0 = p.req_info[req * 4], nq = p.req_info[req * 4 + 1];
+  const int pos0 = p.req_info[req * 4 + 2], nblk = p.req_info[req * 4 + 3];
+  const int32_t* ptab = p.page_table + static_cast<long long>(req) * p.table_stride;
+
+  if (tid == 0) {
+    for (int i = 0; i < C::RAW_SLOTS; ++i) {
+      mbar_init(&m->raw_full[i], 1);
+      mbar_init(&m->raw_empty[i], 128);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&m->a_full[i], 128);
+      mbar_init(&m->a_empty[i], 1);
+      mbar_init(&m->acc_full[i], 1);
+      mbar_init(&m->acc_empty[i], 8);
+    }
+    m->abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_u32(&m->tmem)));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  // ---- prologue: rotated fixed-point query limbs (B operand), head weights
+  // and causal limits; one warp per (query, head)
+  for (int v = warp; v < kQ * kIdxHeads; v += kThreads / 32) {
+    const int qi = v >> 2, h = v & 3;
+    const int q = q0 + qi;
+    const bool valid = q < nq;
+    float x0 = 0.f, x1 = 0.f, w = 0.f;
+    if (valid) {
+      const float* src = p.index_q + (static_cast<long long>(row0 + q) * kIdxHeads + h) * kIdxDim;
+      x0 = src[2 * lane] * p.diag_idx[2 * lane];
+      x1 = src[2 * lane + 1] * p.diag_idx[2 * lane + 1];
+      w = p.index_w[static_cast<long long>(row0 + q) * kIdxHeads + h];
+    }
+    {  // normalised 64-point WHT, 2 values per lane
+      const float a = x0, b = x1;
+      x0 = a + b;
+      x1 = a - b;
+    }
+#pragma unroll
+    for (int ld = 1; ld < 32; ld <<= 1) {
+      const bool up = (lane & ld) != 0;
+      const float o0 = __shfl_xor_sync(0xffffffffu, x0, ld), o1 = __shfl_xor_sync(0xffffffffu, x1, ld);
+      x0 = up ? o0 - x0 : x0 + o0;
+      x1 = up ? o1 - x1 : x1 + o1;
+    }
+    x0 *= 0.125f;
+    x1 *= 0.125f;
+    const float am = warp_max(fmaxf(fabsf(x0), fabsf(x1)));
+    const float s = am > 0.f ? am / 2097152.0f : 1.0f;  // 2^21
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const int qint = valid ? __float2int_rn(__fdiv_rn(k ? x1 : x0, s)) : 0;
+      const int a = (qint + 1024) >> 11, b = qint - a * 2048;
+      const int d = 2 * lane + k;
+      const int n0 = (qi * kIdxHeads + h) * 2;
+      *reinterpret_cast<__half*>(smem + C::OFF_B + canon(n0, d)) = __int2half_rn(a);
+      *reinterpret_cast<__half*>(smem + C::OFF_B + canon(n0 + 1, d)) = __int2half_rn(b);
+    }
+    if (lane == 0) m->alpha[qi][h] = valid ? softplus_f(w) * s : 0.f;
+  }
+  if (tid < kQ) {
+    const int q = q0 + tid;
+    m->vis[tid] = q < nq ? min(nblk, (pos0 + q) / p.compression) : 0;
+    m->thr[tid] = 0;
+    m->cnt[tid] = 0;
+  }
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // B operand -> tensor core
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  if (tid == 0) {
+    int mv = 0;
+    for (int i = 0; i < kQ; ++i) mv = max(mv, m->vis[i]);
+    m->ntiles = (mv + kTileKeys - 1) / kTileKeys;
+  }
+  __syncthreads();
+  const int ntiles = m->ntiles;
+  const uint32_t tmem = m->tmem;
+
+  if (warp == 0) {
+    // ------------------------------------------------ page producer
+    if (lane == 0) {
+      const int npages = min((nblk + kPage - 1) / kPage, p.table_stride);
+      for (int j = 0; j < ntiles; ++j) {
+        const int slot = j % C::RAW_SLOTS, use = j / C::RAW_SLOTS;
+        if (use > 0 && !wait_or_abort(&m->raw_empty[slot], (use - 1) & 1, m, p.err)) break;
+        uint8_t* dst = smem + C::OFF_RAW + slot * ((C::RAW_BYTES + 127) & ~127);
+        const int np = min(2, npages - 2 * j);
+        mbar_expect_tx(&m->raw_full[slot], static_cast<uint32_t>(max(np, 0) * C::PB));
+        for (int k = 0; k < np; ++k) {
+          int phys = ptab[2 * j + k];
+          if (phys < 0 || phys >= p.num_pages) {
+            report_error(p.err, kErrBadPage);
+            phys = 0;
+          }
+          bulk_g2s(dst + k * C::PB, p.idx_pages + static_cast<long long>(phys) * C::PB, C::PB, &m->raw_full[slot]);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------ MMA issue
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc(kN, kTileKeys);
+      const uint32_t sB = smem_u32(smem + C::OFF_B);
+      for (int j = 0; j < ntiles; ++j) {
+        const int st = j & 1, use = j >> 1;
+        if (!wait_or_abort(&m->a_full[st], use & 1, m, p.err)) break;
+        if (use > 0 && !wait_or_abort(&m->acc_empty[st], (use - 1) & 1, m, p.err)) break;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t sA = smem_u32(smem + C::OFF_A + st * kTileKeys * kIdxDim * 2);
+        const uint32_t dt = tmem + st * kN;
+#pragma unroll
+        for (int kk = 0; kk < kIdxDim / 16; ++kk) {
+          const uint64_t da = umma_desc(sA + kk * 2 * kLBO), db = umma_desc(sB + kk * 2 * kLBO);
+          asm volatile(
+              "{ .reg .pred p; setp.ne.u32 p, %4, 0;\n"
+              "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p; }" ::"r"(dt),
+              "l"(da), "l"(db), "r"(idesc), "r"(static_cast<uint32_t>(kk)));
+        }
+        asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                         smem_u32(&m->a_empty[st]))
+                     : "memory");
+        asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                         smem_u32(&m->acc_full[st]))
+                     : "memory");
+      }
+    }
+  } else if (warp >= 4 && warp < 8) {
+    // ------------------------------------------------ code conversion
+    const int r = tid - 128;  // key row of the tile
+    for (int j = 0; j < ntiles; ++j) {
+      const int slot = j % C::RAW_SLOTS, ruse = j / C::RAW_SLOTS, st = j & 1, ause = j >> 1;
+      if (!wait_or_abort(&m->raw_full[slot], ruse & 1, m, p.err)) break;
+      if (ause > 0 && !wait_or_abort(&m->a_empty[st], (ause - 1) & 1, m, p.err)) break;
+      const uint8_t* page = smem + C::OFF_RAW + slot * ((C::RAW_BYTES + 127) & ~127) + (r >> 6) * C::PB;
+      const uint8_t* row = page + (r & 63) * C::RB;
+      uint8_t* A = smem + C::OFF_A + st * kTileKeys * kIdxDim * 2;
+      if (BITS == 4) {
+        const uint4 v0 = *reinterpret_cast<const uint4*>(row), v1 = *reinterpret_cast<const uint4*>(row + 16);
+        const uint32_t wv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+#pragma unroll
+        for (int g = 0; g < 8; ++g)  // 8 dims = 4 bytes per core-matrix row
+          *reinterpret_cast<uint4*>(A + canon(r, 8 * g)) =
+              make_uint4(nib2h2(wv[g] & 0xFFu), nib2h2((wv[g] >> 8) & 0xFFu), nib2h2((wv[g] >> 16) & 0xFFu),
+                         nib2h2(wv[g] >> 24));
+      } else {
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          const uint4 v = *reinterpret_cast<const uint4*>(row + 16 * g);
+          *reinterpret_cast<uint4*>(A + canon(r, 16 * g)) =
+              make_uint4(s8x2h2(v.x & 0xFFFFu), s8x2h2(v.x >> 16), s8x2h2(v.y & 0xFFFFu), s8x2h2(v.y >> 16));
+          *reinterpret_cast<uint4*>(A + canon(r, 16 * g + 8)) =
+              make_uint4(s8x2h2(v.z & 0xFFFFu), s8x2h2(v.z >> 16), s8x2h2(v.w & 0xFFFFu), s8x2h2(v.w >> 16));
+        }
+      }
+      sscl[(j & 3) * kTileKeys + r] = *reinterpret_cast<const float*>(page + kPage * C::RB + (r & 63) * 4);
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      mbar_arrive_cta(&m->a_full[st]);
+      mbar_arrive_cta(&m->raw_empty[slot]);
+    }
+  } else if (warp >= 8) {
+    // ------------------------------------------------ epilogue + top-k
+    const int e = warp - 8;                  // 0..7
+    const int quad = warp & 3, half = e >> 2;  // TMEM lanes 32 quad.., queries 16 half..
+    const int r = 32 * quad + lane;          // key row of the tile
+    uint32_t* hist = reinterpret_cast<uint32_t*>(smem + C::OFF_HIST) + e * 256;
+    for (int j = 0; j < ntiles; ++j) {
+      const int st = j & 1, use = j >> 1;
+      // a timed-out wait sets the abort flag; all epilogue warps leave
+      // together after the next named barrier
+      const bool got = wait_or_abort(&m->acc_full[st], use & 1, m, p.err);
+      if (!got) {
+        named_sync(1, 256);
+        break;
+      }
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const float kscale = sscl[(j & 3) * kTileKeys + r];
+      const int blk = j * kTileKeys + r;
+      uint32_t keys[16];
+#pragma unroll
+      for (int c2 = 0; c2 < 2; ++c2) {  // 2 x 64 columns = 8 queries each
+        uint32_t v[64];
+        const uint32_t ta = tmem + (static_cast<uint32_t>(32 * quad) << 16) + st * kN + half * 128 + c2 * 64;
+        asm volatile(
+            "tcgen05.ld.sync.aligned.32x32b.x64.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+            "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32,%33,%34,%35,%36,%37,%38,%39,"
+            "%40,%41,%42,%43,%44,%45,%46,%47,%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, "
+            "[%64];"
+            : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+              "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]),
+              "=r"(v[15]), "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]),
+              "=r"(v[22]), "=r"(v[23]), "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]),
+              "=r"(v[29]), "=r"(v[30]), "=r"(v[31]), "=r"(v[32]), "=r"(v[33]), "=r"(v[34]), "=r"(v[35]),
+              "=r"(v[36]), "=r"(v[37]), "=r"(v[38]), "=r"(v[39]), "=r"(v[40]), "=r"(v[41]), "=r"(v[42]),
+              "=r"(v[43]), "=r"(v[44]), "=r"(v[45]), "=r"(v[46]), "=r"(v[47]), "=r"(v[48]), "=r"(v[49]),
+              "=r"(v[50]), "=r"(v[51]), "=r"(v[52]), "=r"(v[53]), "=r"(v[54]), "=r"(v[55]), "=r"(v[56]),
+              "=r"(v[57]), "=r"(v[58]), "=r"(v[59]), "=r"(v[60]), "=r"(v[61]), "=r"(v[62]), "=r"(v[63])
+            : "r"(ta));
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+        for (int qq = 0; qq < 8; ++qq) {
+          const int qi = half * 16 + c2 * 8 + qq;
+          const float4 al = *reinterpret_cast<const float4*>(m->alpha[qi]);
+          const float alh[4] = {al.x, al.y, al.z, al.w};
+          float sc = 0.f;
+#pragma unroll
+          for (int h = 0; h < 4; ++h) {
+            const float dot = fmaf(2048.f, __uint_as_float(v[qq * 8 + h * 2]), __uint_as_float(v[qq * 8 + h * 2 + 1]));
+            sc = fmaf(alh[h], fmaxf(dot, 0.f), sc);
+          }
+          keys[c2 * 8 + qq] = __float_as_uint(__fmul_rn(sc, kscale)) + 1u;
+        }
+      }
+      // this warp's TMEM reads are done: the accumulator may be overwritten
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cta(&m->acc_empty[st]);
+      // append the keys above each query's threshold (block order within a
+      // warp; buffers are unordered)
+#pragma unroll
+      for (int qq = 0; qq < 16; ++qq) {
+        const int qi = half * 16 + qq;
+        const bool pass = blk < m->vis[qi] && keys[qq] > m->thr[qi];
+        const uint32_t bal = __ballot_sync(0xffffffffu, pass);
+        if (bal) {
+          uint32_t base = 0;
+          if (lane == 0) base = atomicAdd(&m->cnt[qi], static_cast<uint32_t>(__popc(bal)));
+          base = __shfl_sync(0xffffffffu, base, 0);
+          if (pass) cbuf[qi * kCap + base + __popc(bal & ((1u << lane) - 1u))] = make_uint2(keys[qq], blk);
+        }
+      }
+      named_sync(1, 256);
+      if (*reinterpret_cast<volatile int*>(&m->abort_flag)) break;
+      // prune full buffers: warp e owns queries 4e .. 4e + 3
+#pragma unroll 1
+      for (int qq = 0; qq < 4; ++qq) {
+        const int qi = 4 * e + qq;
+        const int n = static_cast<int>(m->cnt[qi]);
+        if (n > kPruneAt) {
+          const uint32_t t = warp_prune(cbuf + qi * kCap, n, p.top_k, hist, lane);
+          if (lane == 0) {
+            m->thr[qi] = t;
+            m->cnt[qi] = p.top_k;
+          }
+        }
+      }
+      named_sync(1, 256);
+    }
+    // ---- final exact top-k per query, written in ascending block order
+    const bool ok = !*reinterpret_cast<volatile int*>(&m->abort_flag);
+#pragma unroll 1
+    for (int qq = 0; qq < 4; ++qq) {
+      const int qi = 4 * e + qq, q = q0 + qi;
+      if (q >= nq) continue;
+      uint2* b = cbuf + qi * kCap;
+      int n = ok ? static_cast<int>(m->cnt[qi]) : 0;
+      const int K = min(p.top_k, m->vis[qi]);
+      if (n > K) {
+        warp_prune(b, n, K, hist, lane);
+        n = K;
+      }
+      __syncwarp();
+      uint32_t* ok_keys = p.cand_keys + static_cast<long long>(row0 + q) * p.top_k;
+      int32_t* ok_ids = p.cand_ids + static_cast<long long>(row0 + q) * p.top_k;
+      for (int i = lane; i < n; i += 32) {  // rank by block index (distinct)
+        const uint2 me = b[i];
+        int rank = 0;
+        for (int k2 = 0; k2 < n; ++k2) rank += b[k2].y < me.y;
+        ok_keys[rank] = me.x;
+        ok_ids[rank] = static_cast<int32_t>(me.y);
+      }
+      for (int i = n + lane; i < p.top_k; i += 32) {
+        ok_keys[i] = 0u;
+        ok_ids[i] = -1;
+      }
+    }
+  }
+  // ---- teardown: every role is done with TMEM
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem));
+}
+
+template <int BITS>
+static int launch(const Params& p, int ntiles, cudaStream_t st) {
+  static bool attr = false;
+  if (!attr) {
+    AETHER_CUDA_TRY(cudaFuncSetAttribute(csa_prefill_index_kernel<BITS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         Cfg<BITS>::SMEM),
+                    "csa_prefill: set shared memory size");
+    attr = true;
+  }
+  csa_prefill_index_kernel<BITS><<<ntiles, kThreads, Cfg<BITS>::SMEM, st>>>(p);
+  return check_launch("csa_prefill_topk");
+}
+
+}  // namespace prefill
+}  // namespace aether
+
+using namespace aether;
+
+extern "C" int aether_csa_prefill_topk(const float* index_q, const float* index_w, const uint8_t* idx_pages,
+                                       const int32_t* page_table, int table_stride, int num_pages,
+                                       const int32_t* req_info, const int32_t* tiles, int ntiles, int compression,
+                                       const float* diag_idx, int bits, int top_k, uint32_t* cand_keys,
+                                       int32_t* cand_ids, int* err, void* stream) {
+  AETHER_REQUIRE(bits == 4 || bits == 8, "bits must be 4 or 8, got %d", bits);
+  AETHER_REQUIRE(top_k >= 1 && top_k <= prefill::kMaxK, "top_k must be in [1, %d], got %d", prefill::kMaxK, top_k);
+  AETHER_REQUIRE(compression >= 1, "compression must be positive");
+  AETHER_REQUIRE(table_stride >= 1 && num_pages >= 1, "page table / pool must be non-empty");
+  AETHER_REQUIRE(ntiles >= 0, "negative tile count");
+  if (ntiles == 0) return 0;
+  prefill::Params p{index_q, index_w, idx_pages, page_table, req_info, tiles, diag_idx, cand_keys, cand_ids, err,
+                    table_stride, num_pages, compression, top_k};
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  return bits == 4 ? prefill::launch<4>(p, ntiles, st) : prefill::launch<8>(p, ntiles, st);
+}

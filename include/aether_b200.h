@@ -193,6 +193,25 @@ int aether_csa_attend_candidates(const void* q, const float* sink, const void* w
 int aether_lse_merge(const float* part_o, const float* part_ml, const float* sink, int G, int B, int H, void* out,
                      void* stream);
 
+/* ------------------------------------------------ chunked prefill
+ * Indexer top-k for the query tokens of prefill chunks against the paged
+ * cache (the per-query-row indexer of aether_2b/modeling.py:605-615 with the
+ * causal block mask s < t // compression of :612-614), on tcgen05 tensor
+ * cores.  R requests: req_info [R][4] int32 = (first row of the request's
+ * queries in index_q / index_w / the outputs, number of queries, absolute
+ * position t of its first query, compressed blocks held in the cache, its
+ * own chunk's blocks included); request r uses page_table row r.
+ * tiles [ntiles][2] int32 = (request, first query within the request), one
+ * per 32 consecutive queries.  index_q [Q][4][64], index_w [Q][4] fp32 raw.
+ * cand_keys / cand_ids [Q][top_k]: order-preserving u32 score keys and block
+ * ids of the exact top min(top_k, t // compression) blocks (score desc, lower
+ * block first among equal scores), ids ascending, padding key 0 / id -1;
+ * top_k <= 256.  The rows feed aether_csa_attend_candidates. */
+int aether_csa_prefill_topk(const float* index_q, const float* index_w, const uint8_t* idx_pages,
+                            const int32_t* page_table, int table_stride, int num_pages, const int32_t* req_info,
+                            const int32_t* tiles, int ntiles, int compression, const float* diag_idx, int bits,
+                            int top_k, uint32_t* cand_keys, int32_t* cand_ids, int* err, void* stream);
+
 /* Workspace bytes of aether_csa_decode_paged (cluster 0). */
 size_t aether_csa_decode_workspace_bytes(int B, int max_nblocks);
 

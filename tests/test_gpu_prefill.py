@@ -1,0 +1,100 @@
+"""GPU parity of the tcgen05 chunked-prefill indexer: exact top-k block sets
+per query token against the CPU oracle (aether_2b/modeling.py:591-615 with
+the causal block mask), near-tie rows reported, not failed."""
+import pytest
+import torch
+
+from oracle import prefill as opf
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def lib(cuda_device):
+    from aether_kernels import _lib
+
+    _lib.load()
+
+
+def _requests(batch, nq_list):
+    from aether_kernels.prefill import PrefillRequest
+
+    reqs, row = [], 0
+    for b, nq in enumerate(nq_list):
+        toks = batch.tokens[b]
+        nblk = int(batch.nblocks[b])
+        pos0 = max(0, toks - nq)
+        reqs.append(PrefillRequest(row, nq, pos0, nblk))
+        row += nq
+    return reqs, row
+
+
+def _run(batch, nq_list, top_k=256, seed=0):
+    from aether_kernels.prefill import csa_prefill_topk
+
+    reqs, Q = _requests(batch, nq_list)
+    g = torch.Generator().manual_seed(seed)
+    iq = torch.randn(Q, 4, 64, generator=g)
+    iw = torch.randn(Q, 4, generator=g)
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    keys, ids = csa_prefill_topk(iq.cuda(), iw.cuda(), batch.cache, batch.page_table, reqs, top_k=top_k, err=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    c = batch.cache
+    sels, ties = opf.prefill_topk(iq, iw, c.idx_codes.cpu(), c.idx_scale.cpu(), batch.page_table.cpu(),
+                                  [(r.first_row, r.num_queries, r.position, r.nblocks) for r in reqs], batch.bits,
+                                  top_k)
+    ids = ids.cpu()
+    keys = keys.cpu()
+    mism = 0
+    for row, (ref, tie) in enumerate(zip(sels, ties)):
+        k = ref.numel()
+        got = ids[row]
+        assert (got[k:] == -1).all() and (keys[row, k:] == 0).all(), f"row {row}: padding"
+        got = got[:k].long()
+        assert torch.equal(got, torch.sort(got).values), f"row {row}: ids not ascending"
+        if not torch.equal(got, ref):
+            assert tie, f"row {row}: selection differs outside the near-tie band"
+            mism += 1
+    return mism, len(sels)
+
+
+@pytest.mark.parametrize("bits", [4, 8])
+def test_prefill_topk_matches_oracle(lib, bits):
+    from aether_kernels.synthetic import make_decode_batch
+
+    batch = make_decode_batch("csa", 3, 2400, 14000, bits, 4, seed=50 + bits, device="cuda")
+    mism, n = _run(batch, [70, 33, 130], seed=bits)
+    assert mism <= max(1, n // 100)
+
+
+def test_prefill_topk_short_context_and_small_k(lib):
+    """Queries that see fewer blocks than top_k take them all; top_k < 256."""
+    from aether_kernels.synthetic import make_decode_batch
+
+    batch = make_decode_batch("csa", 2, 500, 1100, 4, 4, seed=7, device="cuda")
+    mism, _ = _run(batch, [64, 40], top_k=256, seed=3)
+    assert mism == 0
+    mism, _ = _run(batch, [64, 40], top_k=40, seed=4)
+    assert mism <= 1
+
+
+def test_prefill_topk_repeated_entries(lib):
+    """Identical index entries: equal scores; the lower block index wins."""
+    from aether_kernels.synthetic import make_decode_batch
+
+    batch = make_decode_batch("csa", 2, 6000, 8000, 8, 4, seed=9, device="cuda")
+    c = batch.cache
+    g = torch.Generator().manual_seed(1)
+    for row in range(2):
+        nbr = int(batch.nblocks[row])
+        pages = batch.page_table[row, : (nbr + 63) // 64].long()
+        flat_c = c.idx_codes[pages].reshape(-1, c.idx_codes.shape[-1])
+        flat_s = c.idx_scale[pages].reshape(-1)
+        pick = torch.randint(0, 5, (nbr,), generator=g).to(flat_c.device)
+        flat_c[:nbr] = flat_c[:5][pick].clone()
+        flat_s[:nbr] = flat_s[:5][pick].clone()
+        c.idx_codes[pages] = flat_c.view(len(pages), 64, -1)
+        c.idx_scale[pages] = flat_s.view(len(pages), 64)
+    mism, _ = _run(batch, [40, 50], seed=5)
+    assert mism == 0
