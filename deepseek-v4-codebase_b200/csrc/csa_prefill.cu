@@ -29,11 +29,12 @@
 //   warps 4-7    codes -> fp16 in the canonical no-swizzle K-major layout
 //   warps 8-15   epilogue: TMEM -> registers, scores, streaming top-k
 // Streaming top-k: per query a candidate buffer (key, block) with a running
-// threshold T; a key enters if key > T.  When a buffer passes 384 entries a
-// warp radix-selects the k-th largest (ties to the lower block index), keeps
-// exactly k entries and raises T to that key; later keys equal to T lose the
-// tie (they have higher block indices).  At the end the exact top-k of the
-// buffer is written in ascending block order.
+// threshold T, owned by one warp; a key enters if key > T.  When a tile's
+// keys would overflow the buffer (512 entries, 448 at 8-bit), the owner radix-selects
+// the k-th largest (ties to the lower block index), keeps exactly k entries
+// and raises T to that key; later keys equal to T lose the tie (they have
+// higher block indices).  At the end the exact top-k of the buffer is
+// written in ascending block order.
 #include "capi_util.cuh"
 #include "common.cuh"
 
@@ -44,8 +45,7 @@ constexpr int kThreads = 512;
 constexpr int kQ = 32;                  // query tokens per CTA
 constexpr int kTileKeys = 128;          // keys per MMA tile (M)
 constexpr int kN = kQ * kIdxHeads * 2;  // 256 accumulator columns per tile
-constexpr int kCap = 512;               // candidate buffer entries per query
-constexpr int kPruneAt = kCap - kTileKeys;
+constexpr int kCapMax = 512;            // candidate buffer entries per query (largest variant)
 constexpr int kMaxK = 256;
 constexpr uint32_t kLBO = 128, kSBO = 1024;  // canonical layout strides (bytes)
 
@@ -54,14 +54,15 @@ struct Cfg {
   static constexpr int RB = kIdxDim * BITS / 8;
   static constexpr int PB = page_bytes(RB);
   static constexpr int RAW_SLOTS = BITS == 4 ? 3 : 2;
+  static constexpr int CAP = BITS == 4 ? 512 : 448;  // candidate entries per query
   static constexpr int RAW_BYTES = 2 * PB;  // two pages per 128-key tile
   static constexpr int OFF_B = 0;                               // fp16 [256][64] canonical
   static constexpr int OFF_A = OFF_B + kN * kIdxDim * 2;        // fp16 [2][128][64] canonical
   static constexpr int OFF_RAW = OFF_A + 2 * kTileKeys * kIdxDim * 2;
   static constexpr int OFF_SCL = OFF_RAW + RAW_SLOTS * ((RAW_BYTES + 127) & ~127);  // fp32 [4][128]
-  static constexpr int OFF_BUF = OFF_SCL + 4 * kTileKeys * 4;   // uint2 [32][kCap]
-  static constexpr int OFF_HIST = OFF_BUF + kQ * kCap * 8;      // u32 [8 warps][256]
-  static constexpr int OFF_MISC = OFF_HIST + 8 * 256 * 4;
+  static constexpr int OFF_BUF = OFF_SCL + 4 * kTileKeys * 4;   // uint2 [32][CAP]
+  static constexpr int OFF_X = OFF_BUF + kQ * CAP * 8;         // u32 [32][128] score exchange
+  static constexpr int OFF_MISC = OFF_X + kQ * kTileKeys * 4;
   static constexpr int SMEM = OFF_MISC + 2048;
   static_assert(SMEM <= 232448, "shared memory");
   static_assert(OFF_MISC % 16 == 0 && OFF_BUF % 16 == 0 && OFF_SCL % 16 == 0, "alignment");
@@ -73,9 +74,9 @@ struct alignas(16) Misc {
   uint32_t tmem;
   int abort_flag;
   int ntiles;
-  uint32_t thr[kQ];
-  uint32_t cnt[kQ];
   int vis[kQ];
+  uint32_t thr[kQ];  // per-query threshold and buffer count (owned by one warp)
+  uint32_t cnt[kQ];
 };
 static_assert(sizeof(Misc) <= 2048, "misc area");
 
@@ -90,6 +91,7 @@ struct Params {
   uint32_t* cand_keys;      // [Qtot][top_k]
   int32_t* cand_ids;        // [Qtot][top_k]
   int* err;
+  long long* dbg;  // per-CTA phase clocks [grid][16] (profiling aid), or null
   int table_stride, num_pages, compression, top_k;
 };
 
@@ -114,9 +116,23 @@ __device__ __forceinline__ void mbar_arrive_cta(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 // Bounded wait; a timeout sets the CTA's abort flag so every role winds down.
-__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, Misc* m, int* err) {
+// `backoff` roles (producer, MMA issue, conversion) sleep between polls so
+// their waiting leaves the issue slots to the epilogue warps.
+__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, Misc* m, int* err,
+                                              bool backoff = false) {
   if (*reinterpret_cast<volatile int*>(&m->abort_flag)) return false;
-  if (mbar_wait(bar, parity, err)) return true;
+  const uint32_t addr = smem_u32(bar);
+  for (int it = 0; it < (1 << 22); ++it) {
+    uint32_t done;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(done)
+        : "r"(addr), "r"(parity)
+        : "memory");
+    if (done) return true;
+    if (backoff) __nanosleep(64);
+  }
+  report_error(err, kErrWaitTimeout);
   *reinterpret_cast<volatile int*>(&m->abort_flag) = 1;
   return false;
 }
@@ -141,89 +157,81 @@ __device__ __forceinline__ uint32_t s8x2h2(uint32_t w) {
 }
 
 // ---------------------------------------------------------------- selection
-// One warp: the K-th largest key of n entries (key desc, block asc), keeping
-// exactly min(K, n) of them at the front of buf (order not kept).  Returns
-// the threshold key.  MSB-first radix select over 8-bit digits with a
-// warp-private 256-bin histogram.
-__device__ uint32_t warp_prune(uint2* buf, int n, int K, uint32_t* hist, int lane) {
-  uint32_t prefix = 0, R = static_cast<uint32_t>(K);
-  for (int d = 3; d >= 0; --d) {
-    for (int i = lane; i < 256; i += 32) hist[i] = 0;
-    __syncwarp();
-    for (int i = lane; i < n; i += 32) {
-      const uint32_t k = buf[i].x;
-      if (d == 3 || ((k ^ prefix) >> (8 * (d + 1))) == 0u) atomicAdd(&hist[(k >> (8 * d)) & 255u], 1u);
-    }
-    __syncwarp();
-    // lane l owns bins [248 - 8 l, 256 - 8 l), scanned from the top
-    uint32_t c[8], s = 0;
+// One warp: the K-th largest key of n <= CAP entries (key desc, block asc),
+// keeping exactly min(K, n) of them at the front of buf (order not kept).
+// Returns the threshold key.  The keys sit in registers (16 per lane) and
+// an MSB-first bitwise radix select counts matches with warp reductions:
+// no shared-memory atomics, which serialise when keys share their top bits.
+template <int CAP>
+__device__ __forceinline__ uint32_t warp_prune(uint2* buf, int n, int K, int lane) {
+  constexpr int PER = CAP / 32;
+  uint32_t kk[PER];
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      c[k] = hist[255 - 8 * lane - k];
-      s += c[k];
-    }
-    uint32_t inc = s;
+  for (int i = 0; i < PER; ++i) {
+    const int idx = i * 32 + lane;
+    kk[i] = idx < n ? buf[idx].x : 0u;  // 0 never matches: real keys are >= 1
+  }
+  // bits shared by every real key need no radix step: start below the
+  // highest bit where two keys differ
+  uint32_t kor = 0, kand = 0xFFFFFFFFu;
 #pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const uint32_t u = __shfl_up_sync(0xffffffffu, inc, o);
-      if (lane >= o) inc += u;
+  for (int i = 0; i < PER; ++i) {
+    if (i * 32 + lane < n) {
+      kor |= kk[i];
+      kand &= kk[i];
     }
-    const int L = __ffs(__ballot_sync(0xffffffffu, inc >= R)) - 1;
-    uint32_t digit = 0, above = 0;
-    if (lane == L) {
-      uint32_t cum = inc - s;
+  }
+  kor = __reduce_or_sync(0xffffffffu, kor);
+  kand = __reduce_and_sync(0xffffffffu, kand);
+  const uint32_t diff = kor ^ kand;
+  const int top = diff ? 31 - __clz(diff) : -1;
+  uint32_t prefix = top >= 31 ? 0u : (kand & ~((2u << top) - 1u)), R = static_cast<uint32_t>(K);
+  if (top < 0) prefix = kand;  // all keys equal
+#pragma unroll 1
+  for (int bit = top; bit >= 0; --bit) {
+    const uint32_t want = prefix | (1u << bit), hm = ~((1u << bit) - 1u);
+    uint32_t c = 0;
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        if (cum + c[k] >= R) {
-          digit = 255u - 8u * lane - k;
-          above = cum;
-          break;
-        }
-        cum += c[k];
-      }
-    }
-    digit = __shfl_sync(0xffffffffu, digit, L);
-    above = __shfl_sync(0xffffffffu, above, L);
-    prefix |= digit << (8 * d);
-    R -= above;
-    __syncwarp();
+    for (int i = 0; i < PER; ++i) c += (kk[i] & hm) == want;
+    c = __reduce_add_sync(0xffffffffu, c);
+    if (c >= R)
+      prefix = want;
+    else
+      R -= c;
   }
   const uint32_t thr = prefix, take_eq = R;
-  // equal keys beyond take_eq: keep the lowest block indices
   uint32_t eq = 0;
-  for (int i = lane; i < n; i += 32) eq += buf[i].x == thr;
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) eq += __shfl_xor_sync(0xffffffffu, eq, o);
-  // keep flags first (one bit per round and lane; n <= 512), then an
-  // in-order compaction whose writes never pass the reads of the same round
+  for (int i = 0; i < PER; ++i) eq += kk[i] == thr;
+  eq = __reduce_add_sync(0xffffffffu, eq);
+  // keep flags first, then an in-order compaction whose writes never pass
+  // the reads of the same round
   uint32_t keepm = 0;
-  for (int i0 = 0, rd = 0; i0 < n; i0 += 32, ++rd) {
-    const int i = i0 + lane;
-    bool keep = false;
-    if (i < n) {
-      const uint2 e = buf[i];
-      keep = e.x > thr;
-      if (e.x == thr) {
-        if (eq <= take_eq) {
-          keep = true;
-        } else {
-          uint32_t before = 0;
-          for (int j = 0; j < n; ++j) {
-            const uint2 o = buf[j];
-            before += o.x == thr && o.y < e.y;
-          }
-          keep = before < take_eq;
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    bool keep = kk[i] > thr;
+    if (kk[i] == thr) {
+      if (eq <= take_eq) {
+        keep = true;
+      } else {  // equal keys beyond take_eq: keep the lowest block indices
+        const uint32_t my = buf[i * 32 + lane].y;
+        uint32_t before = 0;
+        for (int j = 0; j < n; ++j) {
+          const uint2 o = buf[j];
+          before += o.x == thr && o.y < my;
         }
+        keep = before < take_eq;
       }
     }
-    keepm |= static_cast<uint32_t>(keep) << rd;
+    keepm |= static_cast<uint32_t>(keep) << i;
   }
   __syncwarp();
   uint32_t out = 0;
-  for (int i0 = 0, rd = 0; i0 < n; i0 += 32, ++rd) {
-    const int i = i0 + lane;
-    const bool keep = (keepm >> rd) & 1u;
-    const uint2 e = keep ? buf[i] : make_uint2(0, 0);
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    if (i * 32 >= n) break;
+    const bool keep = (keepm >> i) & 1u;
+    const uint2 e = keep ? buf[i * 32 + lane] : make_uint2(0, 0);
     const uint32_t bal = __ballot_sync(0xffffffffu, keep);
     __syncwarp();
     if (keep) buf[out + __popc(bal & ((1u << lane) - 1u))] = e;
@@ -231,6 +239,11 @@ __device__ uint32_t warp_prune(uint2* buf, int n, int K, uint32_t* hist, int lan
     __syncwarp();
   }
   return thr;
+}
+
+template <int CAP>
+__device__ __noinline__ uint32_t warp_prune_call(uint2* buf, int n, int K, int lane) {
+  return warp_prune<CAP>(buf, n, K, lane);
 }
 
 template <int BITS>
@@ -241,6 +254,10 @@ __global__ void __launch_bounds__(kThreads, 1) csa_prefill_index_kernel(Params p
   uint2* cbuf = reinterpret_cast<uint2*>(smem + C::OFF_BUF);
   float* sscl = reinterpret_cast<float*>(smem + C::OFF_SCL);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  auto stamp = [&](int slot) {
+    if (p.dbg) p.dbg[blockIdx.x * 16 + slot] = clock64();
+  };
+  if (tid == 0) stamp(0);
   const int req = p.tiles[blockIdx.x * 2], q0 = p.tiles[blockIdx.x * 2 + 1];
   const int row0 = p.req_info[req * 4], nq = p.req_info[req * 4 + 1];
   const int pos0 = p.req_info[req * 4 + 2], nblk = p.req_info[req * 4 + 3];
@@ -322,6 +339,7 @@ __global__ void __launch_bounds__(kThreads, 1) csa_prefill_index_kernel(Params p
   __syncthreads();
   const int ntiles = m->ntiles;
   const uint32_t tmem = m->tmem;
+  if (tid == 0) stamp(1);
 
   if (warp == 0) {
     // ------------------------------------------------ page producer
@@ -329,7 +347,7 @@ __global__ void __launch_bounds__(kThreads, 1) csa_prefill_index_kernel(Params p
       const int npages = min((nblk + kPage - 1) / kPage, p.table_stride);
       for (int j = 0; j < ntiles; ++j) {
         const int slot = j % C::RAW_SLOTS, use = j / C::RAW_SLOTS;
-        if (use > 0 && !wait_or_abort(&m->raw_empty[slot], (use - 1) & 1, m, p.err)) break;
+        if (use > 0 && !wait_or_abort(&m->raw_empty[slot], (use - 1) & 1, m, p.err, true)) break;
         uint8_t* dst = smem + C::OFF_RAW + slot * ((C::RAW_BYTES + 127) & ~127);
         const int np = min(2, npages - 2 * j);
         mbar_expect_tx(&m->raw_full[slot], static_cast<uint32_t>(max(np, 0) * C::PB));
@@ -342,6 +360,7 @@ __global__ void __launch_bounds__(kThreads, 1) csa_prefill_index_kernel(Params p
           bulk_g2s(dst + k * C::PB, p.idx_pages + static_cast<long long>(phys) * C::PB, C::PB, &m->raw_full[slot]);
         }
       }
+      stamp(2);
     }
   } else if (warp == 1) {
     // ------------------------------------------------ MMA issue
@@ -350,8 +369,8 @@ __global__ void __launch_bounds__(kThreads, 1) csa_prefill_index_kernel(Params p
       const uint32_t sB = smem_u32(smem + C::OFF_B);
       for (int j = 0; j < ntiles; ++j) {
         const int st = j & 1, use = j >> 1;
-        if (!wait_or_abort(&m->a_full[st], use & 1, m, p.err)) break;
-        if (use > 0 && !wait_or_abort(&m->acc_empty[st], (use - 1) & 1, m, p.err)) break;
+        if (!wait_or_abort(&m->a_full[st], use & 1, m, p.err, true)) break;
+        if (use > 0 && !wait_or_abort(&m->acc_empty[st], (use - 1) & 1, m, p.err, true)) break;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const uint32_t sA = smem_u32(smem + C::OFF_A + st * kTileKeys * kIdxDim * 2);
         const uint32_t dt = tmem + st * kN;
@@ -370,14 +389,15 @@ __global__ void __launch_bounds__(kThreads, 1) csa_prefill_index_kernel(Params p
                          smem_u32(&m->acc_full[st]))
                      : "memory");
       }
+      stamp(3);
     }
   } else if (warp >= 4 && warp < 8) {
     // ------------------------------------------------ code conversion
     const int r = tid - 128;  // key row of the tile
     for (int j = 0; j < ntiles; ++j) {
       const int slot = j % C::RAW_SLOTS, ruse = j / C::RAW_SLOTS, st = j & 1, ause = j >> 1;
-      if (!wait_or_abort(&m->raw_full[slot], ruse & 1, m, p.err)) break;
-      if (ause > 0 && !wait_or_abort(&m->a_empty[st], (ause - 1) & 1, m, p.err)) break;
+      if (!wait_or_abort(&m->raw_full[slot], ruse & 1, m, p.err, true)) break;
+      if (ause > 0 && !wait_or_abort(&m->a_empty[st], (ause - 1) & 1, m, p.err, true)) break;
       const uint8_t* page = smem + C::OFF_RAW + slot * ((C::RAW_BYTES + 127) & ~127) + (r >> 6) * C::PB;
       const uint8_t* row = page + (r & 63) * C::RB;
       uint8_t* A = smem + C::OFF_A + st * kTileKeys * kIdxDim * 2;
@@ -404,14 +424,24 @@ __global__ void __launch_bounds__(kThreads, 1) csa_prefill_index_kernel(Params p
       mbar_arrive_cta(&m->a_full[st]);
       mbar_arrive_cta(&m->raw_empty[slot]);
     }
+    if (tid == 128) stamp(4);
   } else if (warp >= 8) {
     // ------------------------------------------------ epilogue + top-k
-    const int e = warp - 8;                  // 0..7
+    // Each quad-warp turns its 32 keys x 16 queries of TMEM into score keys
+    // and writes them to the exchange area; after one barrier warp e owns
+    // queries 4e .. 4e + 3 for all 128 keys of the tile: it appends the keys
+    // above each query's threshold to that query's buffer and prunes it,
+    // with the threshold and count in registers.  Two barriers per tile
+    // order the exchange area's writes and reads.
+    const int e = warp - 8;                    // 0..7
     const int quad = warp & 3, half = e >> 2;  // TMEM lanes 32 quad.., queries 16 half..
-    const int r = 32 * quad + lane;          // key row of the tile
-    uint32_t* hist = reinterpret_cast<uint32_t*>(smem + C::OFF_HIST) + e * 256;
+    const int r = 32 * quad + lane;            // key row of the tile
+    uint32_t* xbuf = reinterpret_cast<uint32_t*>(smem + C::OFF_X);
+    long long t_wait = 0, t_ld = 0, t_ins = 0, t_prune = 0;
+    int nprune = 0;
     for (int j = 0; j < ntiles; ++j) {
       const int st = j & 1, use = j >> 1;
+      long long c0 = clock64();
       // a timed-out wait sets the abort flag; all epilogue warps leave
       // together after the next named barrier
       const bool got = wait_or_abort(&m->acc_full[st], use & 1, m, p.err);
@@ -420,9 +450,10 @@ __global__ void __launch_bounds__(kThreads, 1) csa_prefill_index_kernel(Params p
         break;
       }
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      long long c1 = clock64();
+      t_wait += c1 - c0;
       const float kscale = sscl[(j & 3) * kTileKeys + r];
-      const int blk = j * kTileKeys + r;
-      uint32_t keys[16];
+      uint32_t* xo = xbuf;
 #pragma unroll
       for (int c2 = 0; c2 < 2; ++c2) {  // 2 x 64 columns = 8 queries each
         uint32_t v[64];
@@ -454,43 +485,110 @@ __global__ void __launch_bounds__(kThreads, 1) csa_prefill_index_kernel(Params p
             const float dot = fmaf(2048.f, __uint_as_float(v[qq * 8 + h * 2]), __uint_as_float(v[qq * 8 + h * 2 + 1]));
             sc = fmaf(alh[h], fmaxf(dot, 0.f), sc);
           }
-          keys[c2 * 8 + qq] = __float_as_uint(__fmul_rn(sc, kscale)) + 1u;
+          xo[qi * kTileKeys + r] = __float_as_uint(__fmul_rn(sc, kscale)) + 1u;
         }
       }
       // this warp's TMEM reads are done: the accumulator may be overwritten
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
       __syncwarp();
       if (lane == 0) mbar_arrive_cta(&m->acc_empty[st]);
-      // append the keys above each query's threshold (block order within a
-      // warp; buffers are unordered)
-#pragma unroll
-      for (int qq = 0; qq < 16; ++qq) {
-        const int qi = half * 16 + qq;
-        const bool pass = blk < m->vis[qi] && keys[qq] > m->thr[qi];
-        const uint32_t bal = __ballot_sync(0xffffffffu, pass);
-        if (bal) {
-          uint32_t base = 0;
-          if (lane == 0) base = atomicAdd(&m->cnt[qi], static_cast<uint32_t>(__popc(bal)));
-          base = __shfl_sync(0xffffffffu, base, 0);
-          if (pass) cbuf[qi * kCap + base + __popc(bal & ((1u << lane) - 1u))] = make_uint2(keys[qq], blk);
-        }
-      }
       named_sync(1, 256);
+      long long c2 = clock64();
+      t_ld += c2 - c1;
       if (*reinterpret_cast<volatile int*>(&m->abort_flag)) break;
-      // prune full buffers: warp e owns queries 4e .. 4e + 3
-#pragma unroll 1
-      for (int qq = 0; qq < 4; ++qq) {
-        const int qi = 4 * e + qq;
-        const int n = static_cast<int>(m->cnt[qi]);
-        if (n > kPruneAt) {
-          const uint32_t t = warp_prune(cbuf + qi * kCap, n, p.top_k, hist, lane);
-          if (lane == 0) {
-            m->thr[qi] = t;
-            m->cnt[qi] = p.top_k;
+      // owner phase: queries 4e .. 4e + 3, all 128 keys of the tile; the
+      // four queries are processed side by side (independent latency chains)
+      {
+        uint32_t kv[4][4], pm[4], npass[4], thrq[4], cntq[4];
+        int visq[4];
+        const int b0 = j * kTileKeys + 4 * lane;
+#pragma unroll
+        for (int qq = 0; qq < 4; ++qq) {
+          const int qi = 4 * e + qq;
+          visq[qq] = m->vis[qi];
+          thrq[qq] = m->thr[qi];
+          cntq[qq] = m->cnt[qi];
+          const uint4 v4 = *reinterpret_cast<const uint4*>(xo + qi * kTileKeys + 4 * lane);
+          kv[qq][0] = v4.x; kv[qq][1] = v4.y; kv[qq][2] = v4.z; kv[qq][3] = v4.w;
+        }
+        uint32_t bal[4][4];
+#pragma unroll
+        for (int qq = 0; qq < 4; ++qq) {
+          pm[qq] = 0;
+          npass[qq] = 0;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const bool ps = b0 + i < visq[qq] && kv[qq][i] > thrq[qq];
+            pm[qq] |= static_cast<uint32_t>(ps) << i;
+            bal[qq][i] = __ballot_sync(0xffffffffu, ps);
+            npass[qq] += __popc(bal[qq][i]);
           }
         }
+        // rare: a buffer would overflow -> prune it (one inlined call site),
+        // then re-evaluate all four queries against the new thresholds
+        uint32_t need = 0;
+#pragma unroll
+        for (int qq = 0; qq < 4; ++qq) need |= static_cast<uint32_t>(cntq[qq] + npass[qq] > C::CAP) << qq;
+        if (need) {
+          const long long cp0 = clock64();
+          for (uint32_t mk = need; mk; mk &= mk - 1u) {
+            const int qi = 4 * e + __ffs(mk) - 1;
+            const int n = static_cast<int>(m->cnt[qi]);
+            const uint32_t t = warp_prune<C::CAP>(cbuf + qi * C::CAP, n, p.top_k, lane);
+            if (lane == 0) {
+              m->thr[qi] = t;
+              m->cnt[qi] = static_cast<uint32_t>(min(p.top_k, n));
+            }
+            ++nprune;
+            __syncwarp();
+          }
+          t_prune += clock64() - cp0;
+#pragma unroll
+          for (int qq = 0; qq < 4; ++qq) {
+            thrq[qq] = m->thr[4 * e + qq];
+            cntq[qq] = m->cnt[4 * e + qq];
+            pm[qq] = 0;
+            npass[qq] = 0;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const bool ps = b0 + i < visq[qq] && kv[qq][i] > thrq[qq];
+              pm[qq] |= static_cast<uint32_t>(ps) << i;
+              bal[qq][i] = __ballot_sync(0xffffffffu, ps);
+              npass[qq] += __popc(bal[qq][i]);
+            }
+          }
+        }
+        // append in block order (lane-major, then the lane's 4 keys)
+        const uint32_t lt = (1u << lane) - 1u;
+#pragma unroll
+        for (int qq = 0; qq < 4; ++qq) {
+          uint2* qb = cbuf + (4 * e + qq) * C::CAP;
+          uint32_t pos = cntq[qq] + __popc(bal[qq][0] & lt) + __popc(bal[qq][1] & lt) + __popc(bal[qq][2] & lt) +
+                         __popc(bal[qq][3] & lt);
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            if ((pm[qq] >> i) & 1u) qb[pos++] = make_uint2(kv[qq][i], static_cast<uint32_t>(b0 + i));
+        }
+        __syncwarp();
+        if (lane < 4) {
+          m->thr[4 * e + lane] = lane == 0 ? thrq[0] : lane == 1 ? thrq[1] : lane == 2 ? thrq[2] : thrq[3];
+          m->cnt[4 * e + lane] = lane == 0 ? cntq[0] + npass[0]
+                                 : lane == 1 ? cntq[1] + npass[1]
+                                 : lane == 2 ? cntq[2] + npass[2]
+                                             : cntq[3] + npass[3];
+        }
+        __syncwarp();
       }
-      named_sync(1, 256);
+      t_ins += clock64() - c2;
+      named_sync(1, 256);  // the exchange area is rewritten by the next tile
+    }
+    if (tid == 256 && p.dbg) {
+      p.dbg[blockIdx.x * 16 + 8] = t_wait;
+      p.dbg[blockIdx.x * 16 + 9] = t_ld;
+      p.dbg[blockIdx.x * 16 + 10] = t_ins;
+      p.dbg[blockIdx.x * 16 + 12] = nprune;
+      p.dbg[blockIdx.x * 16 + 11] = t_prune;
+      p.dbg[blockIdx.x * 16 + 5] = clock64();
     }
     // ---- final exact top-k per query, written in ascending block order
     const bool ok = !*reinterpret_cast<volatile int*>(&m->abort_flag);
@@ -498,11 +596,11 @@ __global__ void __launch_bounds__(kThreads, 1) csa_prefill_index_kernel(Params p
     for (int qq = 0; qq < 4; ++qq) {
       const int qi = 4 * e + qq, q = q0 + qi;
       if (q >= nq) continue;
-      uint2* b = cbuf + qi * kCap;
-      int n = ok ? static_cast<int>(m->cnt[qi]) : 0;
+      uint2* b = cbuf + qi * C::CAP;
+      int n = ok ? min(static_cast<int>(m->cnt[qi]), C::CAP) : 0;
       const int K = min(p.top_k, m->vis[qi]);
       if (n > K) {
-        warp_prune(b, n, K, hist, lane);
+        warp_prune_call<C::CAP>(b, n, K, lane);
         n = K;
       }
       __syncwarp();
@@ -524,8 +622,11 @@ __global__ void __launch_bounds__(kThreads, 1) csa_prefill_index_kernel(Params p
   // ---- teardown: every role is done with TMEM
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
+  if (tid == 0) stamp(6);
   if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem));
 }
+
+static long long* g_debug = nullptr;
 
 template <int BITS>
 static int launch(const Params& p, int ntiles, cudaStream_t st) {
@@ -557,7 +658,11 @@ extern "C" int aether_csa_prefill_topk(const float* index_q, const float* index_
   AETHER_REQUIRE(ntiles >= 0, "negative tile count");
   if (ntiles == 0) return 0;
   prefill::Params p{index_q, index_w, idx_pages, page_table, req_info, tiles, diag_idx, cand_keys, cand_ids, err,
-                    table_stride, num_pages, compression, top_k};
+                    prefill::g_debug, table_stride, num_pages, compression, top_k};
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   return bits == 4 ? prefill::launch<4>(p, ntiles, st) : prefill::launch<8>(p, ntiles, st);
 }
+
+// Profiling aid: when buf is non-null, later prefill launches record per-CTA
+// SM-clock phase stamps and per-phase cycle totals into buf[cta * 16 + i].
+extern "C" void aether_csa_prefill_set_debug(long long* buf) { aether::prefill::g_debug = buf; }
