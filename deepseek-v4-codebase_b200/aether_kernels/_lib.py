@@ -91,6 +91,13 @@ SIGNATURES = {
          _c_int, _c_int, _c_int, _c_int, _c_int, _c_f, _p, _p, _p, _p, _p, _p],
     ),
     "aether_lse_merge": (_c_int, [_p, _p, _p, _c_int, _c_int, _c_int, _p, _p]),
+    "aether_csa_prefill_attend": (
+        _c_int,
+        [_p, _p, _p, _p, _p, _p,             # q, sink, window, win_row, window_len, kv_pages
+         _p, _c_int, _c_int, _p, _p, _c_int,  # page_table, stride, num_pages, q_row, nblocks, max_nblocks
+         _p, _p, _p, _c_int, _c_int, _c_int, _c_int, _c_int, _c_f,  # diag, keys, ids, stride, B, H, bits, top_k, scale
+         _p, _p, _p, _p],                    # out, sel_out, err, stream
+    ),
     "aether_csa_prefill_topk": (
         _c_int,
         [_p, _p, _p, _p, _c_int, _c_int,     # index_q, index_w, idx_pages, page_table, stride, num_pages

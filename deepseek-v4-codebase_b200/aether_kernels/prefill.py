@@ -8,7 +8,10 @@ to those blocks plus its causal 128-token window with the sink.
 
 ``csa_prefill_topk`` runs the indexer on the tcgen05 tensor cores (kernel
 csa_prefill_index_kernel): 32 query tokens per CTA against 128-key tiles of
-the request's index pages.
+the request's index pages.  ``csa_prefill_attend`` runs the sparse sink
+attention of every query token over its top-k blocks and its causal window
+(the decode attention kernel in candidate-list mode, one 2-CTA cluster per
+query token).  ``csa_prefill_chunk`` chains the two.
 """
 from __future__ import annotations
 
@@ -19,7 +22,7 @@ import torch
 
 from . import _lib
 from .ops import _check, _cuda, _stream, rademacher_diag
-from .paged import INDEX_DIM, INDEX_HEADS, TurboQuantPagedCache
+from .paged import HEAD_DIM, INDEX_DIM, INDEX_HEADS, TurboQuantPagedCache
 
 QUERIES_PER_CTA = 32
 
@@ -71,3 +74,69 @@ def csa_prefill_topk(index_q: torch.Tensor, index_weight: torch.Tensor, cache: T
               int(compression), rademacher_diag(INDEX_DIM, cache.seed, dev).data_ptr(), cache.bits, int(top_k),
               keys.data_ptr(), ids.data_ptr(), None if err is None else err.data_ptr(), _stream(dev))
     return keys, ids
+
+
+def query_rows(requests: Sequence[PrefillRequest], compression: int, window: int, window_first_row: Sequence[int],
+               device) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Per query token: (page-table row, visible blocks, first window row,
+    window length) for a flat window buffer where request r's raw window
+    rows start at window_first_row[r] with the row of position
+    ``position - window + 1``."""
+    q_row, vis, wrow, wlen = [], [], [], []
+    for r, (req, w0) in enumerate(zip(requests, window_first_row)):
+        for i in range(req.num_queries):
+            t = req.position + i
+            q_row.append(r)
+            vis.append(min(req.nblocks, t // compression))
+            n = min(window, t + 1)
+            wlen.append(n)
+            wrow.append(w0 + i + (window - n))
+    return (torch.tensor(q_row, dtype=torch.int32, device=device), torch.tensor(vis, dtype=torch.int32, device=device),
+            torch.tensor(wrow, dtype=torch.int64, device=device), torch.tensor(wlen, dtype=torch.int32, device=device))
+
+
+def csa_prefill_attend(q: torch.Tensor, sink: torch.Tensor, window: torch.Tensor, win_row: torch.Tensor,
+                       window_len: torch.Tensor, cache: TurboQuantPagedCache, page_table: torch.Tensor,
+                       q_row: torch.Tensor, nblocks: torch.Tensor, cand_keys: torch.Tensor, cand_ids: torch.Tensor,
+                       softmax_scale: float, out: Optional[torch.Tensor] = None,
+                       indices: Optional[torch.Tensor] = None,
+                       err: Optional[torch.Tensor] = None) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Sparse sink attention of each query token over its candidate blocks
+    plus its window.  q [Q, H, 128] bf16, sink [H] fp32, window [rows, 128]
+    bf16 (flat), win_row [Q] int64, window_len [Q] int32 (<= 128), q_row [Q]
+    int32 page-table row, nblocks [Q] int32 visible blocks, cand_keys /
+    cand_ids [Q, top_k] from ``csa_prefill_topk``.  Returns (out [Q, H, 128]
+    bf16 before the inverse output RoPE, attended ids [Q, top_k])."""
+    for t, nm in ((q, "q"), (sink, "sink"), (window, "window"), (win_row, "win_row"), (window_len, "window_len"),
+                  (page_table, "page_table"), (q_row, "q_row"), (nblocks, "nblocks"), (cand_keys, "cand_keys"),
+                  (cand_ids, "cand_ids")):
+        _cuda(t, nm)
+    Q, H, D = q.shape
+    _check(D == HEAD_DIM and q.dtype == torch.bfloat16 and window.dtype == torch.bfloat16,
+           "q [Q, H, 128] and window [rows, 128] must be bfloat16")
+    _check(win_row.dtype == torch.int64 and q_row.dtype == torch.int32 and nblocks.dtype == torch.int32
+           and window_len.dtype == torch.int32, "win_row int64; q_row, nblocks, window_len int32")
+    top_k = cand_ids.shape[1]
+    dev = q.device
+    if out is None:
+        out = torch.empty(Q, H, D, dtype=torch.bfloat16, device=dev)
+    if indices is None:
+        indices = torch.empty(Q, top_k, dtype=torch.int32, device=dev)
+    _lib.call("aether_csa_prefill_attend", q.data_ptr(), sink.data_ptr(), window.data_ptr(), win_row.data_ptr(),
+              window_len.data_ptr(), cache.kv_pages.data_ptr(), page_table.data_ptr(), page_table.shape[1],
+              cache.num_pages, q_row.data_ptr(), nblocks.data_ptr(), page_table.shape[1] * 64,
+              rademacher_diag(HEAD_DIM, cache.seed, dev).data_ptr(), cand_keys.data_ptr(), cand_ids.data_ptr(),
+              cand_ids.shape[1], Q, H, cache.bits, int(top_k), float(softmax_scale), out.data_ptr(),
+              indices.data_ptr(), None if err is None else err.data_ptr(), _stream(dev))
+    return out, indices
+
+
+def csa_prefill_chunk(q, index_q, index_weight, sink, window, window_first_row: Sequence[int],
+                      cache: TurboQuantPagedCache, page_table, requests: Sequence[PrefillRequest],
+                      softmax_scale: float, compression: int = 4, top_k: int = 256, err=None):
+    """Indexer top-k then attention for every query token of the chunks.
+    Returns (out [Q, H, 128] bf16, selected block ids [Q, top_k])."""
+    keys, ids = csa_prefill_topk(index_q, index_weight, cache, page_table, requests, compression, top_k, err)
+    q_row, vis, wrow, wlen = query_rows(requests, compression, 128, window_first_row, q.device)
+    return csa_prefill_attend(q, sink, window, wrow, wlen, cache, page_table, q_row, vis, keys, ids, softmax_scale,
+                              err=err)

@@ -146,6 +146,11 @@ struct QParams {
   // and (max logit, sum) [B][H][2]; the sink is left to the merge
   float* part_o;
   float* part_ml;
+  // chunked prefill: query b reads page-table row q_row[b] and the window rows
+  // win_row[b] .. win_row[b] + window_len[b] - 1 of a flat [rows][128] buffer
+  // (null: row b, rows b * W ..)
+  const int32_t* q_row;
+  const long long* win_row;
   long long* dbg;  // per-CTA phase timestamps [grid][16] (profiling aid), or null
   int* err;
   int table_stride, num_pages, H, W, top_k;
@@ -569,11 +574,12 @@ __global__ void __launch_bounds__(kQThreads, CS > 1 ? AETHER_ATTEND_MINB : 1) cs
   const int npages = (nb + kPage - 1) / kPage;
   const int W = p.W;
   const int wl = select_only ? 0 : max(0, min(p.window_len[b], W));
+  const long long wbase = p.win_row ? p.win_row[b] : static_cast<long long>(b) * W;  // first window row
   const int wsl = (W + CS - 1) / CS;               // window rows per CTA
   const int w0 = r * wsl;                           // this CTA's first window row
   const int wn = max(0, min(wl - w0, wsl));         // its valid window rows
   if (!select_only) {
-    const int32_t* ptab = p.page_table + static_cast<long long>(b) * p.table_stride;
+    const int32_t* ptab = p.page_table + static_cast<long long>(p.q_row ? p.q_row[b] : b) * p.table_stride;
     for (int i = tid; i < npages; i += kQThreads) {
       int v = ptab[i];
       if (v < 0 || v >= p.num_pages) {
@@ -598,7 +604,7 @@ __global__ void __launch_bounds__(kQThreads, CS > 1 ? AETHER_ATTEND_MINB : 1) cs
   // window rows other than the newest are cache state: prefetch them now
   {
     const int pre = max(0, min(wn, wl - 1 - w0));
-    const __nv_bfloat16* wsrc = p.window + (static_cast<long long>(b) * W + w0) * kHeadDim;
+    const __nv_bfloat16* wsrc = p.window + (wbase + w0) * kHeadDim;
     for (int i = tid; i < pre * 16; i += kQThreads)
       cp_async16(winb + (i >> 4) * kWRow + (i & 15) * 16, wsrc + (i >> 4) * kHeadDim + (i & 15) * 8);
     asm volatile("cp.async.commit_group;" ::: "memory");
@@ -817,7 +823,7 @@ __global__ void __launch_bounds__(kQThreads, CS > 1 ? AETHER_ATTEND_MINB : 1) cs
     // newest window row (written by the previous step), if it is in this slice
     if (wl > 0 && wl - 1 >= w0 && wl - 1 < w0 + wsl && tid < 16)
       cp_async16(winb + (wl - 1 - w0) * kWRow + tid * 16,
-                 p.window + (static_cast<long long>(b) * W + wl - 1) * kHeadDim + tid * 8);
+                 p.window + (wbase + wl - 1) * kHeadDim + tid * 8);
   }
   // queries: plain bf16 rows for the window, rotated fp16 rows for the codes
   {
@@ -1359,6 +1365,40 @@ extern "C" int aether_csa_attend_candidates(const void* q, const float* sink, co
   if (!rc) rc = bits == 4 ? launch_attend<4>(p, B, false, st) : launch_attend<8>(p, B, false, st);
   if (rc) return rc;
   return check_launch("csa_attend_candidates");
+}
+
+// Chunked prefill attention: query b attends its candidate list (the exact
+// top-k of aether_csa_prefill_topk) plus its causal window, reading
+// page-table row q_row[b] and window rows win_row[b] .. + window_len[b] - 1 of
+// a flat [rows][128] bf16 buffer.
+extern "C" int aether_csa_prefill_attend(const void* q, const float* sink, const void* window,
+                                         const long long* win_row, const int32_t* window_len, const uint8_t* kv_pages,
+                                         const int32_t* page_table, int table_stride, int num_pages,
+                                         const int32_t* q_row, const int32_t* nblocks, int max_nblocks,
+                                         const float* diag_kv, const uint32_t* cand_keys, const int32_t* cand_ids,
+                                         int cand_stride, int B, int H, int bits, int top_k, float softmax_scale,
+                                         void* out, int32_t* sel_out, int* err, void* stream) {
+  int rc = check_common(bits, H, kWinMax, top_k, max_nblocks, table_stride, num_pages);
+  if (rc) return rc;
+  AETHER_REQUIRE(cand_keys && cand_ids && win_row && q_row, "csa_prefill_attend: null argument");
+  AETHER_REQUIRE(cand_stride >= top_k && (cand_stride & 3) == 0,
+                 "csa_prefill_attend: cand_stride must be >= top_k and a multiple of 4");
+  if (B == 0) return 0;
+  QParams p = base_params(q, nullptr, nullptr, sink, window, window_len, nullptr, kv_pages, page_table, table_stride,
+                          num_pages, nblocks, max_nblocks, nullptr, diag_kv, H, kWinMax, top_k, softmax_scale, err);
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.sel_out = sel_out;
+  p.cand_keys = cand_keys;
+  p.cand_ids = cand_ids;
+  p.cand_n = top_k;
+  p.cand_stride = cand_stride;
+  p.q_row = q_row;
+  p.win_row = win_row;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  rc = bits == 4 ? set_smem_attrs<4>() : set_smem_attrs<8>();
+  if (!rc) rc = bits == 4 ? launch_attend<4>(p, B, false, st) : launch_attend<8>(p, B, false, st);
+  if (rc) return rc;
+  return check_launch("csa_prefill_attend");
 }
 
 // Combine G partial attention results (from aether_csa_attend_candidates on

@@ -212,6 +212,21 @@ int aether_csa_prefill_topk(const float* index_q, const float* index_w, const ui
                             const int32_t* tiles, int ntiles, int compression, const float* diag_idx, int bits,
                             int top_k, uint32_t* cand_keys, int32_t* cand_ids, int* err, void* stream);
 
+/* Chunked-prefill attention (aether_2b/modeling.py:616-640 per query row):
+ * query b attends the blocks of its candidate row (cand_keys / cand_ids from
+ * aether_csa_prefill_topk, cand_stride >= top_k) plus its window, with the
+ * sink.  q [B][H][128] bf16; page-table row q_row[b]; visible blocks
+ * nblocks[b] (<= max_nblocks); window rows win_row[b] .. win_row[b] +
+ * window_len[b] - 1 (oldest first, window_len <= 128) of the flat bf16
+ * buffer window [rows][128].  out [B][H][128] bf16 (before the inverse output
+ * RoPE); sel_out [B][top_k] (optional) the attended block ids. */
+int aether_csa_prefill_attend(const void* q, const float* sink, const void* window, const long long* win_row,
+                              const int32_t* window_len, const uint8_t* kv_pages, const int32_t* page_table,
+                              int table_stride, int num_pages, const int32_t* q_row, const int32_t* nblocks,
+                              int max_nblocks, const float* diag_kv, const uint32_t* cand_keys,
+                              const int32_t* cand_ids, int cand_stride, int B, int H, int bits, int top_k,
+                              float softmax_scale, void* out, int32_t* sel_out, int* err, void* stream);
+
 /* Workspace bytes of aether_csa_decode_paged (cluster 0). */
 size_t aether_csa_decode_workspace_bytes(int B, int max_nblocks);
 
