@@ -97,13 +97,19 @@ struct QCfg {
 };
 
 // Score kernel: a CTA stages PPC index pages and scores them.
-constexpr int kSThreads = 256;
+#ifndef AETHER_SCORE_THREADS
+#define AETHER_SCORE_THREADS 256
+#endif
+constexpr int kSThreads = AETHER_SCORE_THREADS;
 constexpr int kSWarps = kSThreads / 32;
 template <int BITS>
 struct SCfg {
   static constexpr int RB_IDX = kIdxDim * BITS / 8;
   static constexpr int PB_IDX = page_bytes(RB_IDX);
-  static constexpr int PPC = BITS == 4 ? 16 : 8;             // pages per CTA (36 / 34 KB)
+#ifndef AETHER_SCORE_PPC4
+#define AETHER_SCORE_PPC4 16
+#endif
+  static constexpr int PPC = BITS == 4 ? AETHER_SCORE_PPC4 : 8;  // pages per CTA (36 / 34 KB at 16 / 8)
   static constexpr int OFF_LIMB = PPC * PB_IDX;              // s8 [4 heads][3 limbs][64]
   static constexpr int OFF_MISC = OFF_LIMB + kIdxHeads * 3 * kIdxDim;
   static constexpr int OFF_BAR = OFF_MISC + 128;
