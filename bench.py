@@ -264,9 +264,10 @@ def main():
                     help="split each step's batch into this many independent micro-batches on separate streams")
     ap.add_argument("--profile-launches", type=int, default=0,
                     help="profiling mode: build the sets, run this many plain launches, print timings, exit")
-    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "hca"],
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "hca", "long"],
                     help="decode: BASELINE config 1 (the headline); prefill: config 4 chunked prefill; "
-                         "hca: config 2 HCA decode")
+                         "hca: config 2 HCA decode; long: config 3 single 262K-token sequence, block range "
+                         "split over the ranks (context parallel, NCCL)")
     ap.add_argument("--prefill-requests", type=int, default=8)
     ap.add_argument("--prefill-queries", type=int, default=4096)
     ap.add_argument("--prefill-cached", type=int, default=65536)
@@ -276,6 +277,9 @@ def main():
         return
     if args.workload == "hca":
         run_hca(args)
+        return
+    if args.workload == "long":
+        run_long(args)
         return
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -386,80 +390,50 @@ def main():
     achieved = bytes_launch / (ms_step / 1e3) / 1e9
     peak, peak_src = read_peak()
 
-    # ---- e2e through the public API with host buffers.  Every step copies
-    # its inputs (q, index q, head weights, window lengths, block counts of
-    # that step's cache set) from pinned host memory in one packed copy, calls
-    # csa_decode_paged, and reads the output and selected indices back in one
-    # packed copy.  Copies run on their own streams with double-buffered
-    # slots, so step i's transfers overlap the kernels of steps i - 1 / i + 1;
-    # every transfer is inside the timed region.
-    fields = ("q", "index_q", "index_weight", "window_len", "nblocks")
+    # ---- e2e through the public C-ABI call with host buffers: every step is
+    # one aether_csa_decode_paged_host call (csa_decode_paged_host), which
+    # enqueues the copy of that step's packed inputs (q, index q, head
+    # weights, window lengths, block counts of the step's cache set) from
+    # pinned host memory, the decode, and the copy of the packed output and
+    # selected indices back to pinned host memory.
+    from aether_kernels.paged import CopyStreams, HostDecodeBuffers, csa_decode_paged_host
 
-    def layout(tensors):
-        offs, off = [], 0
-        for t in tensors:
-            offs.append(off)
-            off += (t.numel() * t.element_size() + 255) // 256 * 256
-        return offs, off
-
-    in_offs, in_bytes = layout([getattr(sets[0], f) for f in fields])
-    host_packs = []
-    for st in sets:
-        hp = torch.empty(in_bytes, dtype=torch.uint8).pin_memory()
-        for f, o in zip(fields, in_offs):
-            t = getattr(st, f)
-            hp[o: o + t.numel() * t.element_size()].copy_(t.contiguous().view(torch.uint8).view(-1).cpu())
-        host_packs.append(hp)
-
-    def views(buf, like, offs):
-        return [buf[o: o + t.numel() * t.element_size()].view(t.dtype).view(t.shape) for t, o in zip(like, offs)]
-
-    like_in = [getattr(sets[0], f) for f in fields]
-    out_like = [torch.empty(B, CFG["heads"], 128, dtype=torch.bfloat16), torch.empty(B, CFG["top_k"], dtype=torch.int32)]
-    out_offs, out_bytes = layout(out_like)
-    slots = []
-    for _ in range(2):
-        din = torch.empty(in_bytes, dtype=torch.uint8, device=dev)
-        dout = torch.empty(out_bytes, dtype=torch.uint8, device=dev)
-        slots.append(dict(din=din, vin=views(din, like_in, in_offs), dout=dout, vout=views(dout, out_like, out_offs),
-                          hout=torch.empty(out_bytes, dtype=torch.uint8).pin_memory(),
-                          ws=torch.zeros(max_ws_bytes(B), dtype=torch.uint8, device=dev),
-                          h2d=torch.cuda.Event(), comp=torch.cuda.Event(), d2h=torch.cuda.Event()))
-    s_h2d, s_d2h = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
-    h2d, d2h = in_bytes, out_bytes
+    # two staging slots on copy streams: a step's copies overlap its
+    # neighbours' kernels
+    slot_bufs = [HostDecodeBuffers(B, CFG["heads"], CFG["top_k"], dev) for _ in range(2)]
+    bufs = slot_bufs[0]
+    copies = CopyStreams(dev)
+    host_ins = [bufs.pack_inputs(st.q, st.index_q, st.index_weight, st.window_len, st.nblocks) for st in sets]
+    host_outs = [bufs.new_host_output() for _ in range(2)]
+    ws_e2e = torch.zeros(max_ws_bytes(B), dtype=torch.uint8, device=dev)
+    h2d, d2h = bufs.in_bytes, bufs.out_bytes
 
     def e2e_step(i):
-        sl, st = slots[i & 1], sets[i % len(sets)]
-        s_h2d.wait_event(sl["comp"])          # the slot's inputs were consumed
-        with torch.cuda.stream(s_h2d):
-            sl["din"].copy_(host_packs[i % len(sets)], non_blocking=True)
-            sl["h2d"].record(s_h2d)
-        stream.wait_event(sl["h2d"])
-        stream.wait_event(sl["d2h"])          # the slot's outputs were read back
-        with torch.cuda.stream(stream):
-            q_, iq_, iw_, wl_, nb_ = sl["vin"]
-            csa_decode_paged(q_, iq_, iw_, st.sink, st.window, wl_, cache, st.page_table, nb_, st.softmax_scale,
-                             top_k=st.top_k, out=sl["vout"][0], indices=sl["vout"][1], workspace=sl["ws"],
-                             err=err)
-            sl["comp"].record(stream)
-        s_d2h.wait_event(sl["comp"])
-        with torch.cuda.stream(s_d2h):
-            sl["hout"].copy_(sl["dout"], non_blocking=True)
-            sl["d2h"].record(s_d2h)
+        st = sets[i % len(sets)]
+        csa_decode_paged_host(slot_bufs[i & 1], host_ins[i % len(sets)], host_outs[i & 1], st.sink, st.window,
+                              cache, st.page_table, st.softmax_scale, ws_e2e, err, copies=copies, slot=i & 1)
 
-    for i in range(4):
-        e2e_step(i)
-    torch.cuda.synchronize(dev)
-    if world > 1:
-        torch.distributed.barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    s_h2d.wait_stream(stream)  # the first upload starts inside the timed region
-    for i in range(args.e2e_steps):
-        e2e_step(i)
-    for sl in slots:
-        stream.wait_event(sl["d2h"])
-    e1.record(stream)
+    with torch.cuda.stream(stream):
+        for i in range(4):
+            e2e_step(i)
+        stream.synchronize()
+        # the host copy of a result matches the device-resident path
+        ref_o, ref_s = csa_decode_paged(sets[3].q, sets[3].index_q, sets[3].index_weight, sets[3].sink,
+                                        sets[3].window, sets[3].window_len, cache, sets[3].page_table,
+                                        sets[3].nblocks, sets[3].softmax_scale, top_k=sets[3].top_k)
+        torch.cuda.synchronize(dev)
+        ho, hs = bufs.unpack_outputs(host_outs[1])
+        assert torch.equal(hs, ref_s.cpu()) and torch.equal(ho, ref_o.cpu()), "host-buffer decode differs"
+        if world > 1:
+            torch.distributed.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        copies.h2d.wait_stream(stream)  # the first input copy starts inside the timed region
+        for i in range(args.e2e_steps):
+            e2e_step(i)
+        for sl in range(2):
+            stream.wait_event(copies.last_output(sl))
+        e1.record(stream)
     e1.synchronize()
     assert int(err.item()) == 0, f"kernel error flag {int(err.item())}"
     e2e_ms = e0.elapsed_time(e1)
@@ -496,6 +470,104 @@ def main():
         print(json.dumps(line), flush=True)
     if world > 1:
         torch.distributed.destroy_process_group()
+
+
+LONG_METRIC = "CSA 8-bit-KV decode queries/s, one 262K-token sequence (65536 blocks) split over the GPUs"
+
+
+def run_long(args):
+    """batch 1, 262144-token context (65536 compressed
+    blocks), 8-bit, YaRN factor 8.  On N ranks each holds a contiguous 1/N of
+    the blocks (the window on the last rank): local candidates, NCCL
+    all-gather, exact global top-256, attention over the owned winners,
+    all-gather of the partials, LSE merge (aether_kernels.dist).  One rank:
+    the single-device path (per-chunk top-256, then the top-256 of the chunk
+    winners).  Cache sets cycle so every step reads cold HBM."""
+    import torch.distributed as dist
+
+    from aether_kernels.dist import csa_decode_context_parallel
+    from aether_kernels.paged import PAGE, TurboQuantPagedCache, csa_decode_paged, csa_workspace_bytes
+    from aether_kernels.rope import RopeConfig
+    from aether_kernels.synthetic import make_decode_batch
+
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+    NB, bits = 65536, 8
+    assert NB % (world * PAGE) == 0
+    per = NB // world
+    nsets = 40
+    cache = TurboQuantPagedCache(nsets * (NB // PAGE), bits, dev)
+    sets, slices = [], []
+    for i in range(nsets):
+        # identical query and cache contents on every rank (seeded by set)
+        st = make_decode_batch("csa", 1, 4 * NB, 4 * NB, bits, 4, seed=500 + i, device=dev,
+                               rope=RopeConfig.yarn(8.0), cache=cache, gen_device=str(dev))
+        lo = rank * per
+        table = st.page_table[:, lo // PAGE: (lo + per) // PAGE].contiguous()
+        wl = st.window_len if rank == world - 1 else torch.zeros_like(st.window_len)
+        slices.append((table, torch.full_like(st.nblocks, per), wl))
+        sets.append(st)
+    out = torch.empty(1, 12, 128, dtype=torch.bfloat16, device=dev)
+    ws = torch.zeros(csa_workspace_bytes(1, NB), dtype=torch.uint8, device=dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+
+    def step(i):
+        st = sets[i % nsets]
+        table, nb, wl = slices[i % nsets]
+        if world == 1:
+            csa_decode_paged(st.q, st.index_q, st.index_weight, st.sink, st.window, st.window_len, cache, table, nb,
+                             st.softmax_scale, out=out, workspace=ws, err=err)
+        else:
+            csa_decode_context_parallel(st.q, st.index_q, st.index_weight, st.sink, st.window, wl, cache, table, nb,
+                                        rank * per, st.softmax_scale, err=err)
+
+    for i in range(max(args.warmup, 3)):
+        step(i)
+    torch.cuda.synchronize(dev)
+    assert int(err.item()) == 0, f"kernel error flag {int(err.item())}"
+    steps = max(nsets, min(args.steps, 2000))
+    sampler = ClockSampler(local)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    sampler.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(steps):
+        step(i)
+    e1.record()
+    e1.synchronize()
+    clocks = sampler.stop()
+    ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_step = ms / steps
+    per_q = algorithmic_bytes([NB], [128], bits)
+    achieved = per_q / (ms_step / 1e3) / 1e9
+    peak, src = read_peak()
+    if rank == 0:
+        print(json.dumps({
+            "metric": LONG_METRIC, "value": round(steps / (ms / 1e3), 1), "unit": "queries/s", "n_gpus": world,
+            "steps": steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 6), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "u8", "data": "synthetic",
+            "config": {"workload": "csa_decode_8bit_b1_ctx262k", "nblocks": NB, "blocks_per_gpu": per, "bits": bits,
+                       "rope": "yarn x8", "cache_sets": nsets, "parallelism": f"context-parallel x{world}",
+                       "l2_policy": "inputs larger than L2: each step reads a different cache set",
+                       "timing": "CUDA events, stream launches"},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": round(peak * world, 1),
+                         "unit": "GB/s", "frac": round(achieved / (peak * world), 4), "peak_source": src,
+                         "traffic": None, "algorithmic_bytes_per_launch": per_q},
+            "clocks": clocks,
+        }), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
 
 
 HCA_METRIC = "HCA 4-bit-KV decode queries/s at 131K ctx (batch 32/GPU, 1024 blocks)"

@@ -104,6 +104,15 @@ SIGNATURES = {
          _p, _p, _c_int, _c_int, _p, _c_int, _c_int,  # req_info, tiles, ntiles, compression, diag, bits, top_k
          _p, _p, _p, _p],                    # cand_keys, cand_ids, err, stream
     ),
+    "aether_csa_decode_paged_host": (
+        _c_int,
+        [_p, _p, ctypes.c_size_t, _p, _p, ctypes.c_size_t,  # host_in, dev_in, in_bytes, host_out, dev_out, out_bytes
+         _p, _p, _p, _p, _p, _p,                              # q, index_q, index_w, sink, window, window_len
+         _p, _p, _p, _c_int, _c_int, _p, _c_int,             # idx_pages, kv_pages, page_table, stride, num_pages, nblocks, max_nb
+         _p, _p, _c_int, _c_int, _c_int, _c_int, _c_int, _c_f,  # diag_idx, diag_kv, B, H, W, bits, top_k, scale
+         _p, _p, _p, _p, _c_int, _p,                          # out, sel_out, workspace, err, pdl, stream
+         _p, _p, _p, _p, _p],                                 # h2d_stream, d2h_stream, ev_h2d, ev_comp, ev_d2h
+    ),
     "aether_hca_decode_paged": (
         _c_int,
         [

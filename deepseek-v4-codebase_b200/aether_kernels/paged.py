@@ -256,6 +256,116 @@ def csa_decode_paged(
     return out, indices
 
 
+
+class HostDecodeBuffers:
+    """Device staging for ``csa_decode_paged_host``: the step inputs packed as
+    [q | index_q | index_weight | window_len | nblocks] and the results as
+    [out | indices], each field 256-byte aligned."""
+
+    FIELDS = ("q", "index_q", "index_weight", "window_len", "nblocks")
+
+    def __init__(self, batch: int, heads: int = 12, top_k: int = 256, device="cuda"):
+        self.batch, self.heads, self.top_k = batch, heads, top_k
+        self.device = torch.device(device)
+        self.in_shapes = [((batch, heads, HEAD_DIM), torch.bfloat16), ((batch, INDEX_HEADS, INDEX_DIM), torch.float32),
+                          ((batch, INDEX_HEADS), torch.float32), ((batch,), torch.int32), ((batch,), torch.int32)]
+        self.out_shapes = [((batch, heads, HEAD_DIM), torch.bfloat16), ((batch, top_k), torch.int32)]
+        self.in_offsets, self.in_bytes = self._layout(self.in_shapes)
+        self.out_offsets, self.out_bytes = self._layout(self.out_shapes)
+        self.dev_in = torch.empty(self.in_bytes, dtype=torch.uint8, device=self.device)
+        self.dev_out = torch.empty(self.out_bytes, dtype=torch.uint8, device=self.device)
+        self.inputs = self._views(self.dev_in, self.in_shapes, self.in_offsets)
+        self.out, self.indices = self._views(self.dev_out, self.out_shapes, self.out_offsets)
+
+    @staticmethod
+    def _layout(shapes):
+        offs, off = [], 0
+        for shape, dt in shapes:
+            offs.append(off)
+            n = 1
+            for d in shape:
+                n *= d
+            off += (n * torch.empty((), dtype=dt).element_size() + 255) // 256 * 256
+        return offs, off
+
+    @staticmethod
+    def _views(buf, shapes, offs):
+        out = []
+        for (shape, dt), o in zip(shapes, offs):
+            n = 1
+            for d in shape:
+                n *= d
+            es = torch.empty((), dtype=dt).element_size()
+            out.append(buf[o: o + n * es].view(dt).view(shape))
+        return out
+
+    def pack_inputs(self, q, index_q, index_weight, window_len, nblocks) -> torch.Tensor:
+        """Pinned host buffer holding one step's inputs in the packed layout."""
+        host = torch.empty(self.in_bytes, dtype=torch.uint8).pin_memory()
+        for t, (shape, dt), o in zip((q, index_q, index_weight, window_len, nblocks), self.in_shapes, self.in_offsets):
+            _check(tuple(t.shape) == shape and t.dtype == dt, f"input must be {dt} {list(shape)}")
+            b = t.detach().contiguous().cpu().view(torch.uint8).view(-1)
+            host[o: o + b.numel()].copy_(b)
+        return host
+
+    def new_host_output(self) -> torch.Tensor:
+        return torch.empty(self.out_bytes, dtype=torch.uint8).pin_memory()
+
+    def unpack_outputs(self, host_out: torch.Tensor):
+        """(out [B, H, 128] bf16, indices [B, top_k] int32) views of a host result buffer."""
+        return tuple(self._views(host_out, self.out_shapes, self.out_offsets))
+
+
+class CopyStreams:
+    """Copy streams and per-slot events for overlapped ``csa_decode_paged_host``
+    calls: a step's input copy runs on ``h2d``, its output copy on ``d2h``;
+    callers alternate two staging slots (``HostDecodeBuffers``)."""
+
+    def __init__(self, device, slots: int = 2):
+        self.h2d = torch.cuda.Stream(device)
+        self.d2h = torch.cuda.Stream(device)
+        self.events = [tuple(torch.cuda.Event() for _ in range(3)) for _ in range(slots)]
+        # torch creates an event's CUDA handle on its first record
+        for evs in self.events:
+            for e in evs:
+                e.record(self.h2d)
+        self.h2d.synchronize()
+
+    def last_output(self, slot: int) -> torch.cuda.Event:
+        """Event recorded after the slot's latest output copy."""
+        return self.events[slot][2]
+
+
+def csa_decode_paged_host(bufs: HostDecodeBuffers, host_in: torch.Tensor, host_out: torch.Tensor,
+                          sink: torch.Tensor, window: torch.Tensor, cache: TurboQuantPagedCache,
+                          page_table: torch.Tensor, softmax_scale: float, workspace: torch.Tensor,
+                          err: Optional[torch.Tensor] = None, copies: Optional[CopyStreams] = None,
+                          slot: int = 0) -> None:
+    """One CSA decode step with host buffers, enqueued by a single C call: the
+    packed inputs are copied from pinned ``host_in`` to the device, the decode
+    runs on the current stream, and the packed output and indices are copied
+    to pinned ``host_out`` (read them with ``bufs.unpack_outputs`` once the
+    copy has completed).  With ``copies`` the transfers run on its streams,
+    ordered by the slot's events; pass a different ``bufs`` per slot."""
+    _check(host_in.is_pinned() and host_out.is_pinned(), "host buffers must be pinned")
+    _check(host_in.numel() >= bufs.in_bytes and host_out.numel() >= bufs.out_bytes, "host buffers too small")
+    _check(cache.idx_pages is not None, "CSA decode needs a cache with an indexer stream")
+    q, iq, iw, wl, nb = bufs.inputs
+    dev = bufs.device
+    need = csa_workspace_bytes(bufs.batch, page_table.shape[1] * PAGE)
+    _check(workspace.is_cuda and workspace.numel() * workspace.element_size() >= need,
+           f"workspace must hold {need} bytes")
+    _lib.call("aether_csa_decode_paged_host", host_in.data_ptr(), bufs.dev_in.data_ptr(), bufs.in_bytes,
+              host_out.data_ptr(), bufs.dev_out.data_ptr(), bufs.out_bytes, q.data_ptr(), iq.data_ptr(),
+              iw.data_ptr(), sink.data_ptr(), window.data_ptr(), wl.data_ptr(), cache.idx_pages.data_ptr(),
+              cache.kv_pages.data_ptr(), page_table.data_ptr(), page_table.shape[1], cache.num_pages, nb.data_ptr(),
+              page_table.shape[1] * PAGE, rademacher_diag(INDEX_DIM, cache.seed, dev).data_ptr(),
+              rademacher_diag(HEAD_DIM, cache.seed, dev).data_ptr(), bufs.batch, bufs.heads, window.shape[1],
+              cache.bits, bufs.top_k, float(softmax_scale), bufs.out.data_ptr(), bufs.indices.data_ptr(),
+              workspace.data_ptr(), _opt_ptr(err), 0, _stream(dev),
+              *((copies.h2d.cuda_stream, copies.d2h.cuda_stream, *[e.cuda_event for e in copies.events[slot]])
+                if copies is not None else (None,) * 5))
+
 def hca_decode_paged(
     q: torch.Tensor,
     sink: torch.Tensor,

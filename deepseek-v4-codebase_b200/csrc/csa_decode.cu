@@ -939,6 +939,58 @@ int aether_csa_decode_paged(const void* q, const float* index_q, const float* in
                     top_k, softmax_scale, out, sel_out, err, cluster, stream);
 }
 
+// aether_csa_decode_paged with host buffers: copies in_bytes of packed
+// step inputs from (pinned) host_in to dev_in, runs the decode, and copies
+// out_bytes of packed results from dev_out to (pinned) host_out, all
+// enqueued by this one call.  The device pointers (q, index_q, ..., out,
+// sel_out) point into dev_in / dev_out.  With h2d_stream / d2h_stream and the
+// slot's three events (ev_h2d, ev_comp, ev_d2h) given, the input copy runs on
+// h2d_stream after the slot's previous decode, the decode on `stream` after
+// the input copy and the slot's previous output copy, and the output copy on
+// d2h_stream after the decode; alternating two slots (staging buffers and
+// events) lets one step's copies overlap its neighbours' kernels.  With
+// them null everything runs on `stream` in order.
+int aether_csa_decode_paged_host(const void* host_in, void* dev_in, size_t in_bytes, void* host_out,
+                                 const void* dev_out, size_t out_bytes, const void* q, const float* index_q,
+                                 const float* index_w, const float* sink, const void* window,
+                                 const int32_t* window_len, const uint8_t* idx_pages, const uint8_t* kv_pages,
+                                 const int32_t* page_table, int table_stride, int num_pages, const int32_t* nblocks,
+                                 int max_nblocks, const float* diag_idx, const float* diag_kv, int B, int H, int W,
+                                 int bits, int top_k, float softmax_scale, void* out, int32_t* sel_out,
+                                 uint32_t* workspace, int* err, int pdl, void* stream, void* h2d_stream,
+                                 void* d2h_stream, void* ev_h2d, void* ev_comp, void* ev_d2h) {
+  AETHER_REQUIRE(host_in && dev_in && host_out && dev_out, "csa_decode_paged_host: null buffer");
+  const bool split = h2d_stream != nullptr;
+  AETHER_REQUIRE(!split || (d2h_stream && ev_h2d && ev_comp && ev_d2h),
+                 "csa_decode_paged_host: copy streams need d2h_stream and the slot's three events");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaStream_t sin = split ? static_cast<cudaStream_t>(h2d_stream) : st;
+  cudaStream_t sout = split ? static_cast<cudaStream_t>(d2h_stream) : st;
+  cudaEvent_t eh = static_cast<cudaEvent_t>(ev_h2d), ec = static_cast<cudaEvent_t>(ev_comp),
+              ed = static_cast<cudaEvent_t>(ev_d2h);
+  if (split) AETHER_CUDA_TRY(cudaStreamWaitEvent(sin, ec, 0), "csa_decode_paged_host: order input copy");
+  AETHER_CUDA_TRY(cudaMemcpyAsync(dev_in, host_in, in_bytes, cudaMemcpyHostToDevice, sin),
+                  "csa_decode_paged_host: input copy");
+  if (split) {
+    AETHER_CUDA_TRY(cudaEventRecord(eh, sin), "csa_decode_paged_host: record input copy");
+    AETHER_CUDA_TRY(cudaStreamWaitEvent(st, eh, 0), "csa_decode_paged_host: wait input copy");
+    AETHER_CUDA_TRY(cudaStreamWaitEvent(st, ed, 0), "csa_decode_paged_host: wait output slot");
+  }
+  const int rc = aether_csa_decode_paged(q, index_q, index_w, sink, window, window_len, idx_pages, kv_pages,
+                                         page_table, table_stride, num_pages, nblocks, max_nblocks, diag_idx, diag_kv,
+                                         B, H, W, bits, top_k, softmax_scale, out, sel_out, workspace, err, 0, pdl,
+                                         stream);
+  if (rc) return rc;
+  if (split) {
+    AETHER_CUDA_TRY(cudaEventRecord(ec, st), "csa_decode_paged_host: record decode");
+    AETHER_CUDA_TRY(cudaStreamWaitEvent(sout, ec, 0), "csa_decode_paged_host: wait decode");
+  }
+  AETHER_CUDA_TRY(cudaMemcpyAsync(host_out, dev_out, out_bytes, cudaMemcpyDeviceToHost, sout),
+                  "csa_decode_paged_host: output copy");
+  if (split) AETHER_CUDA_TRY(cudaEventRecord(ed, sout), "csa_decode_paged_host: record output copy");
+  return 0;
+}
+
 int aether_hca_decode_paged(const void* q, const float* sink, const void* window, const int32_t* window_len,
                             const uint8_t* kv_pages, const int32_t* page_table,
                             int table_stride, int num_pages, const int32_t* nblocks, int max_nblocks,

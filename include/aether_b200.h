@@ -152,6 +152,26 @@ int aether_csa_decode_paged_scores(const void* q, const float* index_q, const fl
                                    int score_stride, uint32_t* workspace, int* err, int cluster, int pdl,
                                    void* stream);
 
+/* aether_csa_decode_paged with host buffers: one call enqueues the copy of
+ * in_bytes of packed step inputs from pinned host_in to dev_in, the decode
+ * (score + select/attend kernels), and the copy of out_bytes of packed
+ * results from dev_out to pinned host_out.  q, index_q, index_w, window_len,
+ * nblocks point into dev_in; out, sel_out into dev_out.  h2d_stream,
+ * d2h_stream and the staging slot's events ev_h2d / ev_comp / ev_d2h
+ * (cudaEvent_t) are optional (NULL: everything in order on `stream`); with
+ * them the input copy waits for the slot's previous decode, the decode for the
+ * input copy and the slot's previous output copy, and the output copy for the
+ * decode, so callers alternating two slots overlap copies with kernels. */
+int aether_csa_decode_paged_host(const void* host_in, void* dev_in, size_t in_bytes, void* host_out,
+                                 const void* dev_out, size_t out_bytes, const void* q, const float* index_q,
+                                 const float* index_w, const float* sink, const void* window,
+                                 const int32_t* window_len, const uint8_t* idx_pages, const uint8_t* kv_pages,
+                                 const int32_t* page_table, int table_stride, int num_pages, const int32_t* nblocks,
+                                 int max_nblocks, const float* diag_idx, const float* diag_kv, int B, int H, int W,
+                                 int bits, int top_k, float softmax_scale, void* out, int32_t* sel_out,
+                                 uint32_t* workspace, int* err, int pdl, void* stream, void* h2d_stream,
+                                 void* d2h_stream, void* ev_h2d, void* ev_comp, void* ev_d2h);
+
 /* One HCA decode step (replaces aether_2b/serving.py:507-522): attention over
  * every visible compressed block plus the window; nblocks <= 1024. */
 int aether_hca_decode_paged(const void* q, const float* sink, const void* window, const int32_t* window_len,

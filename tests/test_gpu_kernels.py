@@ -362,3 +362,23 @@ def test_csa_decode_repeated_entries(ak, distinct):
         c.idx_scale[pages] = flat_s.view(len(pages), 64)
     out, sel = _run_decode(ak, batch)
     _check_decode(batch, out, sel)
+
+
+def test_csa_decode_host_buffers_match_device_path(ak):
+    """aether_csa_decode_paged_host (one call: host->device copy, decode,
+    device->host copy) returns exactly the device-resident path's result."""
+    from aether_kernels.paged import HostDecodeBuffers, csa_decode_paged, csa_decode_paged_host, csa_workspace_bytes
+    from aether_kernels.synthetic import make_decode_batch
+
+    b = make_decode_batch("csa", 8, 3000, 20000, 4, 4, seed=77, device="cuda")
+    ref_o, ref_s = csa_decode_paged(b.q, b.index_q, b.index_weight, b.sink, b.window, b.window_len, b.cache,
+                                    b.page_table, b.nblocks, b.softmax_scale)
+    bufs = HostDecodeBuffers(8, 12, 256, "cuda")
+    hin = bufs.pack_inputs(b.q, b.index_q, b.index_weight, b.window_len, b.nblocks)
+    hout = bufs.new_host_output()
+    ws = torch.zeros(csa_workspace_bytes(8, b.page_table.shape[1] * 64), dtype=torch.uint8, device="cuda")
+    csa_decode_paged_host(bufs, hin, hout, b.sink, b.window, b.cache, b.page_table, b.softmax_scale, ws)
+    torch.cuda.synchronize()
+    o, s = bufs.unpack_outputs(hout)
+    assert torch.equal(s, ref_s.cpu())
+    assert torch.equal(o, ref_o.cpu())
