@@ -91,6 +91,7 @@ SIGNATURES = {
          _c_int, _c_int, _c_int, _c_int, _c_int, _c_f, _p, _p, _p, _p, _p, _p],
     ),
     "aether_lse_merge": (_c_int, [_p, _p, _p, _c_int, _c_int, _c_int, _p, _p]),
+    "aether_lse_merge_strided": (_c_int, [_p, _p, _c_ll, _c_ll, _p, _c_int, _c_int, _c_int, _p, _p]),
     "aether_csa_prefill_attend": (
         _c_int,
         [_p, _p, _p, _p, _p, _p,             # q, sink, window, win_row, window_len, kv_pages

@@ -73,8 +73,10 @@ def attend_candidates(q, sink, window, window_len, cache: TurboQuantPagedCache, 
     n = cand_keys.shape[1]
     sel = torch.empty(B, top_k, dtype=torch.int32, device=dev)
     if partial:
-        po = torch.empty(B, H, D, dtype=torch.float32, device=dev)
-        pml = torch.empty(B, H, 2, dtype=torch.float32, device=dev)
+        # O and (max, sum) adjacent in one buffer: one collective moves both
+        flat = torch.empty(B * H * (D + 2), dtype=torch.float32, device=dev)
+        po = flat[: B * H * D].view(B, H, D)
+        pml = flat[B * H * D:].view(B, H, 2)
         out_ptr, po_ptr, pml_ptr = None, po.data_ptr(), pml.data_ptr()
     else:
         out = torch.empty(B, H, D, dtype=torch.bfloat16, device=dev)
@@ -89,13 +91,15 @@ def attend_candidates(q, sink, window, window_len, cache: TurboQuantPagedCache, 
 
 
 def lse_merge(part_o: torch.Tensor, part_ml: torch.Tensor, sink: torch.Tensor) -> torch.Tensor:
-    """part_o [G,B,H,128] fp32, part_ml [G,B,H,2] fp32, sink [H] fp32 -> bf16 [B,H,128]."""
+    """part_o [G,B,H,128] fp32, part_ml [G,B,H,2] fp32, sink [H] fp32 -> bf16 [B,H,128].
+    Each rank's block must be contiguous; the rank dimension may be strided
+    (rows of an all-gathered packed buffer)."""
     G, B, H, D = part_o.shape
     out = torch.empty(B, H, D, dtype=torch.bfloat16, device=part_o.device)
-    # keep the contiguous copies alive until the launch is enqueued
-    part_o, part_ml = part_o.contiguous(), part_ml.contiguous()
-    _lib.call("aether_lse_merge", part_o.data_ptr(), part_ml.data_ptr(), sink.data_ptr(),
-              G, B, H, out.data_ptr(), _stream(part_o.device))
+    if not (part_o[0].is_contiguous() and part_ml[0].is_contiguous()):
+        part_o, part_ml = part_o.contiguous(), part_ml.contiguous()  # kept alive past the launch
+    _lib.call("aether_lse_merge_strided", part_o.data_ptr(), part_ml.data_ptr(), part_o.stride(0),
+              part_ml.stride(0), sink.data_ptr(), G, B, H, out.data_ptr(), _stream(part_o.device))
     return out
 
 
@@ -112,18 +116,30 @@ def context_parallel_step(candidates_fn: Callable[[], Tuple[torch.Tensor, torch.
     r-th contiguous block range."""
     world = dist.get_world_size(group)
     keys, ids = candidates_fn()
-    kl = [torch.empty_like(keys) for _ in range(world)]
-    il = [torch.empty_like(ids) for _ in range(world)]
-    dist.all_gather(kl, keys.contiguous(), group=group)
-    dist.all_gather(il, ids.contiguous(), group=group)
-    all_keys = torch.cat(kl, dim=1).contiguous()
-    all_ids = torch.cat(il, dim=1).contiguous()
+
+    def gather_rows(t):  # per rank t -> [world, *t.shape] (flat buffers: every backend accepts them)
+        g = torch.empty(world * t.numel(), dtype=t.dtype, device=t.device)
+        dist.all_gather_into_tensor(g, t.contiguous().view(-1), group=group)
+        return g.view((world,) + tuple(t.shape))
+
+    if keys.dtype == ids.dtype and keys.shape == ids.shape:  # one collective for both
+        g = gather_rows(torch.stack([keys, ids]))             # [world, 2, B, n]
+        gk, gi = g[:, 0], g[:, 1]
+    else:
+        gk, gi = gather_rows(keys), gather_rows(ids)
+    B = keys.shape[0]
+    all_keys = gk.transpose(0, 1).reshape(B, -1).contiguous()
+    all_ids = gi.transpose(0, 1).reshape(B, -1).contiguous()
     po, pml, sel = attend_fn(all_keys, all_ids)
-    pol = [torch.empty_like(po) for _ in range(world)]
-    pmll = [torch.empty_like(pml) for _ in range(world)]
-    dist.all_gather(pol, po.contiguous(), group=group)
-    dist.all_gather(pmll, pml.contiguous(), group=group)
-    return merge_fn(torch.stack(pol), torch.stack(pmll)), sel
+    npo = po.numel()
+    adjacent = (po.is_contiguous() and pml.is_contiguous() and po.dtype == pml.dtype
+                and pml.data_ptr() == po.data_ptr() + npo * po.element_size())
+    flat = torch.as_strided(po, (npo + pml.numel(),), (1,)) if adjacent else \
+        torch.cat([po.reshape(-1), pml.reshape(-1)])
+    gp = torch.empty(world * flat.numel(), dtype=flat.dtype, device=flat.device)
+    dist.all_gather_into_tensor(gp, flat, group=group)
+    gp = gp.view(world, flat.numel())
+    return merge_fn(gp[:, :npo].view(world, *po.shape), gp[:, npo:].view(world, *pml.shape)), sel
 
 
 def csa_decode_context_parallel(q, index_q, index_weight, sink, window, window_len, cache: TurboQuantPagedCache,

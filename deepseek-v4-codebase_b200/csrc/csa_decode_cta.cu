@@ -1249,22 +1249,23 @@ int csa_decode_cta(const void* q, const float* index_q, const float* index_w, co
 // M = max(max_r m_r, sink_h): partial attention over disjoint source sets
 // combined exactly (the sink counted once).  One warp per (b, h).
 __global__ void lse_merge_kernel(const float* __restrict__ part_o, const float* __restrict__ part_ml,
-                                 const float* __restrict__ sink, int G, int B, int H,
-                                 __nv_bfloat16* __restrict__ out) {
+                                 long long stride_o, long long stride_ml, const float* __restrict__ sink, int G,
+                                 int B, int H, __nv_bfloat16* __restrict__ out) {
+  // rank r's partials: part_o + r * stride_o [B][H][128], part_ml + r * stride_ml [B][H][2]
   const int lane = threadIdx.x & 31;
   const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   if (w >= B * H) return;
   const int h = w % H;
-  const long long stride_r = static_cast<long long>(B) * H;
   float M = sink[h];
-  for (int r = 0; r < G; ++r) M = fmaxf(M, part_ml[(r * stride_r + w) * 2]);
+  for (int r = 0; r < G; ++r) M = fmaxf(M, part_ml[r * stride_ml + w * 2]);
   float L = __expf(sink[h] - M);
   float acc[4] = {0, 0, 0, 0};
   for (int r = 0; r < G; ++r) {
-    const float m = part_ml[(r * stride_r + w) * 2], l = part_ml[(r * stride_r + w) * 2 + 1];
+    const float m = part_ml[r * stride_ml + w * 2], l = part_ml[r * stride_ml + w * 2 + 1];
     const float a = m == -INFINITY ? 0.f : __expf(m - M);
     L += a * l;
-    const float4 o = *reinterpret_cast<const float4*>(part_o + (r * stride_r + w) * kHeadDim + lane * 4);
+    const float4 o = *reinterpret_cast<const float4*>(part_o + r * stride_o + static_cast<long long>(w) * kHeadDim +
+                                                      lane * 4);
     acc[0] += a * o.x;
     acc[1] += a * o.y;
     acc[2] += a * o.z;
@@ -1415,7 +1416,24 @@ extern "C" int aether_lse_merge(const float* part_o, const float* part_ml, const
   AETHER_REQUIRE(G >= 1 && B >= 0 && H >= 1, "lse_merge: bad sizes");
   if (B == 0) return 0;
   const int warps = B * H;
+  const long long bh = static_cast<long long>(B) * H;
   lse_merge_kernel<<<(warps * 32 + 255) / 256, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      part_o, part_ml, sink, G, B, H, static_cast<__nv_bfloat16*>(out));
+      part_o, part_ml, bh * kHeadDim, bh * 2, sink, G, B, H, static_cast<__nv_bfloat16*>(out));
   return check_launch("lse_merge");
+}
+
+// As aether_lse_merge with rank r's partials at part_o + r * stride_o and
+// part_ml + r * stride_ml (float elements), e.g. rows of an all-gathered
+// buffer that packs each rank's [B][H][128] O and [B][H][2] (max, sum).
+extern "C" int aether_lse_merge_strided(const float* part_o, const float* part_ml, long long stride_o,
+                                        long long stride_ml, const float* sink, int G, int B, int H, void* out,
+                                        void* stream) {
+  AETHER_REQUIRE(G >= 1 && B >= 0 && H >= 1, "lse_merge: bad sizes");
+  AETHER_REQUIRE(stride_o % 4 == 0 && (reinterpret_cast<uintptr_t>(part_o) & 15) == 0,
+                 "lse_merge_strided: part_o rows must be 16-byte aligned");
+  if (B == 0) return 0;
+  const int warps = B * H;
+  lse_merge_kernel<<<(warps * 32 + 255) / 256, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      part_o, part_ml, stride_o, stride_ml, sink, G, B, H, static_cast<__nv_bfloat16*>(out));
+  return check_launch("lse_merge_strided");
 }

@@ -247,6 +247,12 @@ int aether_csa_prefill_attend(const void* q, const float* sink, const void* wind
                               const int32_t* cand_ids, int cand_stride, int B, int H, int bits, int top_k,
                               float softmax_scale, void* out, int32_t* sel_out, int* err, void* stream);
 
+/* As aether_lse_merge with rank r's partials at part_o + r * stride_o and
+ * part_ml + r * stride_ml (float elements; part_o rows 16-byte aligned), e.g.
+ * the rows of one all-gathered buffer packing each rank's O and (max, sum). */
+int aether_lse_merge_strided(const float* part_o, const float* part_ml, long long stride_o, long long stride_ml,
+                             const float* sink, int G, int B, int H, void* out, void* stream);
+
 /* Workspace bytes of aether_csa_decode_paged (cluster 0). */
 size_t aether_csa_decode_workspace_bytes(int B, int max_nblocks);
 
