@@ -526,21 +526,44 @@ def run_long(args):
             csa_decode_context_parallel(st.q, st.index_q, st.index_weight, st.sink, st.window, wl, cache, table, nb,
                                         rank * per, st.softmax_scale, err=err)
 
-    for i in range(max(args.warmup, 3)):
-        step(i)
+    stream = torch.cuda.Stream(dev)
+    with torch.cuda.stream(stream):
+        for i in range(max(args.warmup, 3)):
+            step(i)
     torch.cuda.synchronize(dev)
     assert int(err.item()) == 0, f"kernel error flag {int(err.item())}"
-    steps = max(nsets, min(args.steps, 2000))
+    # one GPU: a CUDA graph of nsets steps replayed.  Several GPUs: eager
+    # launches (a captured graph holding NCCL collectives left the ranks
+    # hanging in process-group teardown, so collectives are not captured)
+    graph = None
+    if world == 1:
+      try:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for i in range(nsets):
+                step(i)
+        g.replay()
+        torch.cuda.synchronize(dev)
+        graph = g
+      except Exception as exc:  # noqa: BLE001
+        print(f"graph capture unavailable ({exc}); eager launches", file=sys.stderr)
+    replays = max(1, min(args.steps, 2000) // nsets)
+    steps = replays * nsets
     sampler = ClockSampler(local)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize(dev)
     sampler.start()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for i in range(steps):
-        step(i)
-    e1.record()
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for r in range(replays):
+            if graph is not None:
+                graph.replay()
+            else:
+                for i in range(nsets):
+                    step(i)
+        e1.record(stream)
     e1.synchronize()
     clocks = sampler.stop()
     ms = e0.elapsed_time(e1)
@@ -560,7 +583,7 @@ def run_long(args):
             "config": {"workload": "csa_decode_8bit_b1_ctx262k", "nblocks": NB, "blocks_per_gpu": per, "bits": bits,
                        "rope": "yarn x8", "cache_sets": nsets, "parallelism": f"context-parallel x{world}",
                        "l2_policy": "inputs larger than L2: each step reads a different cache set",
-                       "timing": "CUDA events, stream launches"},
+                       "timing": "CUDA graph replay on 1 GPU, eager launches with NCCL on N > 1; CUDA events"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": round(peak * world, 1),
                          "unit": "GB/s", "frac": round(achieved / (peak * world), 4), "peak_source": src,
                          "traffic": None, "algorithmic_bytes_per_launch": per_q},
