@@ -537,16 +537,16 @@ def run_long(args):
     # hanging in process-group teardown, so collectives are not captured)
     graph = None
     if world == 1:
-      try:
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g, stream=stream):
-            for i in range(nsets):
-                step(i)
-        g.replay()
-        torch.cuda.synchronize(dev)
-        graph = g
-      except Exception as exc:  # noqa: BLE001
-        print(f"graph capture unavailable ({exc}); eager launches", file=sys.stderr)
+        try:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                for i in range(nsets):
+                    step(i)
+            g.replay()
+            torch.cuda.synchronize(dev)
+            graph = g
+        except Exception as exc:  # noqa: BLE001
+            print(f"graph capture unavailable ({exc}); eager launches", file=sys.stderr)
     replays = max(1, min(args.steps, 2000) // nsets)
     steps = replays * nsets
     sampler = ClockSampler(local)
