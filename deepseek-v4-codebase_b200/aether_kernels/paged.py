@@ -276,6 +276,7 @@ class HostDecodeBuffers:
         self.dev_out = torch.empty(self.out_bytes, dtype=torch.uint8, device=self.device)
         self.inputs = self._views(self.dev_in, self.in_shapes, self.in_offsets)
         self.out, self.indices = self._views(self.dev_out, self.out_shapes, self.out_offsets)
+        self._ws_key, self._ws_need, self._diags = None, 0, (0, 0)
 
     @staticmethod
     def _layout(shapes):
@@ -347,20 +348,25 @@ def csa_decode_paged_host(bufs: HostDecodeBuffers, host_in: torch.Tensor, host_o
     to pinned ``host_out`` (read them with ``bufs.unpack_outputs`` once the
     copy has completed).  With ``copies`` the transfers run on its streams,
     ordered by the slot's events; pass a different ``bufs`` per slot."""
-    _check(host_in.is_pinned() and host_out.is_pinned(), "host buffers must be pinned")
+    # host buffers from pack_inputs / new_host_output are pinned; others work
+    # but their copies are synchronous
     _check(host_in.numel() >= bufs.in_bytes and host_out.numel() >= bufs.out_bytes, "host buffers too small")
     _check(cache.idx_pages is not None, "CSA decode needs a cache with an indexer stream")
     q, iq, iw, wl, nb = bufs.inputs
     dev = bufs.device
-    need = csa_workspace_bytes(bufs.batch, page_table.shape[1] * PAGE)
-    _check(workspace.is_cuda and workspace.numel() * workspace.element_size() >= need,
-           f"workspace must hold {need} bytes")
+    key = (page_table.shape[1], cache.seed)
+    if bufs._ws_key != key:  # per-shape constants, computed once
+        bufs._ws_need = csa_workspace_bytes(bufs.batch, page_table.shape[1] * PAGE)
+        bufs._diags = (rademacher_diag(INDEX_DIM, cache.seed, dev).data_ptr(),
+                       rademacher_diag(HEAD_DIM, cache.seed, dev).data_ptr())
+        bufs._ws_key = key
+    _check(workspace.is_cuda and workspace.numel() * workspace.element_size() >= bufs._ws_need,
+           f"workspace must hold {bufs._ws_need} bytes")
     _lib.call("aether_csa_decode_paged_host", host_in.data_ptr(), bufs.dev_in.data_ptr(), bufs.in_bytes,
               host_out.data_ptr(), bufs.dev_out.data_ptr(), bufs.out_bytes, q.data_ptr(), iq.data_ptr(),
               iw.data_ptr(), sink.data_ptr(), window.data_ptr(), wl.data_ptr(), cache.idx_pages.data_ptr(),
               cache.kv_pages.data_ptr(), page_table.data_ptr(), page_table.shape[1], cache.num_pages, nb.data_ptr(),
-              page_table.shape[1] * PAGE, rademacher_diag(INDEX_DIM, cache.seed, dev).data_ptr(),
-              rademacher_diag(HEAD_DIM, cache.seed, dev).data_ptr(), bufs.batch, bufs.heads, window.shape[1],
+              page_table.shape[1] * PAGE, bufs._diags[0], bufs._diags[1], bufs.batch, bufs.heads, window.shape[1],
               cache.bits, bufs.top_k, float(softmax_scale), bufs.out.data_ptr(), bufs.indices.data_ptr(),
               workspace.data_ptr(), _opt_ptr(err), 0, _stream(dev),
               *((copies.h2d.cuda_stream, copies.d2h.cuda_stream, *[e.cuda_event for e in copies.events[slot]])
