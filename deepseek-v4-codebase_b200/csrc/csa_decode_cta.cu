@@ -102,6 +102,10 @@ struct QCfg {
 #endif
 constexpr int kSThreads = AETHER_SCORE_THREADS;
 constexpr int kSWarps = kSThreads / 32;
+#ifndef AETHER_SCORE_UNROLL
+#define AETHER_SCORE_UNROLL 4
+#endif
+constexpr int kSU = AETHER_SCORE_UNROLL;  // 16-key tiles a warp scores per loop iteration
 template <int BITS>
 struct SCfg {
   static constexpr int RB_IDX = kIdxDim * BITS / 8;
@@ -455,12 +459,12 @@ __global__ void __launch_bounds__(kSThreads) csa_score_kernel(QParams p, int spl
   stamp(3);
   uint32_t* out = p.ws + static_cast<long long>(b) * p.ws_stride;
   const int tiles = np * (kPage / 16);
-  for (int t0 = warp; t0 < tiles; t0 += 2 * kSWarps) {
-    uint32_t a[2][2][4];
-    int ra[2];
-    bool ok[2];
+  for (int t0 = warp; t0 < tiles; t0 += kSU * kSWarps) {
+    uint32_t a[kSU][2][4];
+    int ra[kSU];
+    bool ok[kSU];
 #pragma unroll
-    for (int u = 0; u < 2; ++u) {
+    for (int u = 0; u < kSU; ++u) {
       const int tile = t0 + u * kSWarps;
       ok[u] = tile < tiles;
       const uint8_t* page = smem + (ok[u] ? (tile >> 2) : 0) * C::PB_IDX;
@@ -483,24 +487,24 @@ __global__ void __launch_bounds__(kSThreads) csa_score_kernel(QParams p, int spl
         a[u][1][0] = va.z; a[u][1][1] = vb.z; a[u][1][2] = va.w; a[u][1][3] = vb.w;
       }
     }
-    int acc0[2][4], acc1[2][4];
+    int acc0[kSU][4], acc1[kSU][4];
 #pragma unroll
-    for (int u = 0; u < 2; ++u) {
+    for (int u = 0; u < kSU; ++u) {
       acc0[u][0] = c0i; acc0[u][1] = c1i; acc0[u][2] = c0i; acc0[u][3] = c1i;
       acc1[u][0] = c2i; acc1[u][1] = 0; acc1[u][2] = c2i; acc1[u][3] = 0;
     }
 #pragma unroll
     for (int j = 0; j < 2; ++j)
 #pragma unroll
-      for (int u = 0; u < 2; ++u) {
+      for (int u = 0; u < kSU; ++u) {
         mma_s8(acc0[u], a[u][j][0], a[u][j][1], a[u][j][2], a[u][j][3], bq[0][j][0], bq[0][j][1]);
         mma_s8(acc1[u], a[u][j][0], a[u][j][1], a[u][j][2], a[u][j][3], bq[1][j][0], bq[1][j][1]);
       }
     // thread t holds head t: limbs (acc0[0], acc0[1], acc1[0]) for row a,
     // (acc0[2], acc0[3], acc1[2]) for row a + 8
-    float sc[2][2];
+    float sc[kSU][2];
 #pragma unroll
-    for (int u = 0; u < 2; ++u)
+    for (int u = 0; u < kSU; ++u)
 #pragma unroll
       for (int r = 0; r < 2; ++r) {
         const float d = __fadd_rn(__fmul_rn(static_cast<float>(acc1[u][2 * r]), 65536.f),
@@ -509,14 +513,14 @@ __global__ void __launch_bounds__(kSThreads) csa_score_kernel(QParams p, int spl
         sc[u][r] = alpha_t * fmaxf(d, 0.f);
       }
 #pragma unroll
-    for (int u = 0; u < 2; ++u)
+    for (int u = 0; u < kSU; ++u)
 #pragma unroll
       for (int r = 0; r < 2; ++r) {
         sc[u][r] += __shfl_xor_sync(0xffffffffu, sc[u][r], 1);
         sc[u][r] += __shfl_xor_sync(0xffffffffu, sc[u][r], 2);
       }
 #pragma unroll
-    for (int u = 0; u < 2; ++u) {
+    for (int u = 0; u < kSU; ++u) {
       const int tile = t0 + u * kSWarps;
       if (ok[u] && t < 2) {
         const uint8_t* page = smem + (tile >> 2) * C::PB_IDX;
