@@ -85,7 +85,8 @@ def _worker(rank, world, port, q_out):
     out, sel = context_parallel_step(lambda: tuple(t[None] for t in cands()), attend,
                                      lambda po, pml: _merge(po[:, 0], pml[:, 0], sink))
     if rank == 0:
-        q_out.put((out, sel))
+        # by value: a tensor shared through the queue can outlive this process's fd listener
+        q_out.put((out.numpy().copy(), sel.numpy().copy()))
     dist.destroy_process_group()
 
 
@@ -97,6 +98,7 @@ def test_context_parallel_gloo_two_ranks():
     for p in procs:
         p.start()
     out, sel = q_out.get(timeout=120)
+    out, sel = torch.from_numpy(out), torch.from_numpy(sel)
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
