@@ -35,6 +35,8 @@ SIGNATURES = {
          _p, _p, _c_int, _p, _c_f, _c_int, _p,                              # positions .. bits, diag
          _p, _c_int, _p, _c_int, _p, _p, _p, _p],                           # page_table .. err, stream
     ),
+    "aether_tq_encode_lut": (_c_int, [_p, _c_int, _c_ll, _c_int, _c_int, _p, _p, _c_f, _p, _p, _p]),
+    "aether_tq_decode_lut": (_c_int, [_p, _p, _c_ll, _c_int, _c_int, _p, _p, _p, _c_int, _p]),
     "aether_tq_decode": (_c_int, [_p, _p, _c_ll, _c_int, _c_int, _p, _p, _c_int, _p]),
     "aether_wht": (_c_int, [_p, _p, _c_ll, _c_int, _p]),
     "aether_sparse_sink_attention": (

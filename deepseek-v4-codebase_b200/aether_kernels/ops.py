@@ -165,6 +165,40 @@ def compress_emit(c0: torch.Tensor, z0: torch.Tensor, bias0: Optional[torch.Tens
     return out
 
 
+def tq_encode_lut(x: torch.Tensor, bits: int, seed: int = 42) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Lloyd-Max level format: (codes uint8 [..., D] or [..., D/2], scale fp32 [..., 1])."""
+    from .codebook import device_codebook
+
+    d = x.shape[-1]
+    _cuda(x, "x")
+    lead = x.shape[:-1]
+    rows = x.numel() // d if d else 0
+    lv, th = device_codebook(bits, x.device)
+    codes = torch.empty(*lead, d if bits == 8 else d // 2, dtype=torch.uint8, device=x.device)
+    scale = torch.empty(*lead, 1, dtype=torch.float32, device=x.device)
+    _lib.call("aether_tq_encode_lut", x.data_ptr(), _dt(x, "x"), rows, d, bits,
+              rademacher_diag(d, seed, x.device).data_ptr(), th.data_ptr(), float(lv[-1].item()), codes.data_ptr(),
+              scale.data_ptr(), _stream(x.device))
+    return codes, scale
+
+
+def tq_decode_lut(codes: torch.Tensor, scale: torch.Tensor, bits: int, seed: int = 42,
+                  out_dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
+    from .codebook import device_codebook
+
+    _cuda(codes, "data")
+    scale = scale.contiguous().float()
+    d = codes.shape[-1] * (2 if bits == 4 else 1)
+    rows = codes.numel() // codes.shape[-1] if codes.shape[-1] else 0
+    _check(scale.numel() == rows, "scale must hold one value per vector")
+    lv, _ = device_codebook(bits, codes.device)
+    out = torch.empty(*codes.shape[:-1], d, dtype=out_dtype, device=codes.device)
+    _lib.call("aether_tq_decode_lut", codes.data_ptr(), scale.data_ptr(), rows, d, bits,
+              rademacher_diag(d, seed, codes.device).data_ptr(), lv.data_ptr(), out.data_ptr(), _dt(out, "out"),
+              _stream(codes.device))
+    return out
+
+
 def tq_decode(codes: torch.Tensor, scale: torch.Tensor, bits: int, seed: int = 42,
               out_dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
     _cuda(codes, "data")

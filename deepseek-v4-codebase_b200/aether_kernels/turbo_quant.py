@@ -28,11 +28,19 @@ class PolarQuant:
 
     bits=8 -> int8 codes [..., D]; bits=4 -> uint8 [..., D/2] with two signed
     4-bit codes per byte (even index in the low nibble).  Scale fp32 [..., 1].
+
+    ``codebook="lloyd-max"`` (not in the reference) selects the Lloyd-Max
+    level format for N(0, 1) instead of the uniform levels: codes are level
+    indices (uint8 [..., D], or index nibbles [..., D/2]).  The fused paged
+    decode kernels read the uniform format only.
     """
 
-    def __init__(self, bits: int, seed: int = 42) -> None:
+    def __init__(self, bits: int, seed: int = 42, codebook: str = "uniform") -> None:
         if bits not in (4, 8):
             raise ValueError(f"bits must be 4 or 8, got {bits}")
+        if codebook not in ("uniform", "lloyd-max"):
+            raise ValueError(f"codebook must be 'uniform' or 'lloyd-max', got {codebook!r}")
+        self.codebook = codebook
         self.bits = bits
         self._seed = seed
         self._diag_cache: Dict[Tuple[int, str], torch.Tensor] = {}
@@ -46,10 +54,14 @@ class PolarQuant:
     def encode(self, x: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
         if not x.is_cuda:
             raise RuntimeError("aether_kernels PolarQuant.encode requires a CUDA tensor")
+        if self.codebook == "lloyd-max":
+            return ops.tq_encode_lut(x.contiguous(), self.bits, self._seed)
         return ops.tq_encode(x.contiguous(), self.bits, self._seed)
 
     def decode(self, data: torch.Tensor, scale: torch.Tensor,
                out_dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
         if not data.is_cuda:
             raise RuntimeError("aether_kernels PolarQuant.decode requires a CUDA tensor")
+        if self.codebook == "lloyd-max":
+            return ops.tq_decode_lut(data.contiguous(), scale, self.bits, self._seed, out_dtype)
         return ops.tq_decode(data.contiguous(), scale, self.bits, self._seed, out_dtype)

@@ -310,6 +310,87 @@ static void launch_emit_t(int dtype, const EmitParams& p, const RowDst& dst, int
   }
 }
 
+// ------------------------------------------------- Lloyd-Max level format
+// Alternative to the uniform levels: y = WHT(diag * x), scale = max|y| /
+// c_max, and each element the index of the nearest of the 2^BITS levels
+// (thr: the 2^BITS - 1 ascending fp32 midpoints; code = number of
+// thresholds strictly below y / scale, i.e. the lower index on a midpoint).
+// 8-bit: one index byte per element; 4-bit: index nibbles, even element low.
+template <int D, int BITS, typename T>
+__global__ void __launch_bounds__(256) tq_encode_lut_kernel(const T* __restrict__ x, const float* __restrict__ diag,
+                                                           const float* __restrict__ thr, float cmax,
+                                                           uint8_t* __restrict__ codes, float* __restrict__ scales,
+                                                           long long rows) {
+  constexpr int EPL = D / 32;
+  constexpr int NT = (1 << BITS) - 1;
+  const int lane = threadIdx.x & 31;
+  const long long row = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  if (row >= rows) return;
+  float v[EPL];
+#pragma unroll
+  for (int k = 0; k < EPL; ++k) {
+    const int i = lane * EPL + k;
+    v[k] = __fmul_rn(ld_as_float(x + row * D + i), diag[i]);
+  }
+  warp_wht<D>(v, lane);
+  float m = 0.f;
+#pragma unroll
+  for (int k = 0; k < EPL; ++k) m = fmaxf(m, fabsf(v[k]));
+  m = warp_max(m);
+  m = fmaxf(m, 9.99999993922529e-09f);
+  const float scale = __fdiv_rn(m, cmax);
+  if (lane == 0) scales[row] = scale;
+  int q[EPL];
+#pragma unroll
+  for (int k = 0; k < EPL; ++k) {
+    const float u = __fdiv_rn(v[k], scale);
+    int lo = 0, hi = NT;  // first threshold >= u
+    while (lo < hi) {
+      const int mid = (lo + hi) >> 1;
+      if (thr[mid] < u)
+        lo = mid + 1;
+      else
+        hi = mid;
+    }
+    q[k] = lo;
+  }
+  if (BITS == 8) {
+    uint8_t* base = codes + row * D + lane * EPL;
+#pragma unroll
+    for (int k = 0; k < EPL; ++k) base[k] = static_cast<uint8_t>(q[k]);
+  } else {
+    uint8_t* base = codes + row * (D / 2) + lane * (EPL / 2);
+#pragma unroll
+    for (int k = 0; k < EPL / 2; ++k) base[k] = static_cast<uint8_t>(q[2 * k] | (q[2 * k + 1] << 4));
+  }
+}
+
+template <int D, int BITS, typename T>
+__global__ void __launch_bounds__(256) tq_decode_lut_kernel(const uint8_t* __restrict__ codes,
+                                                           const float* __restrict__ scales,
+                                                           const float* __restrict__ diag,
+                                                           const float* __restrict__ levels, T* __restrict__ out,
+                                                           long long rows) {
+  constexpr int EPL = D / 32;
+  const int lane = threadIdx.x & 31;
+  const long long row = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  if (row >= rows) return;
+  const float s = scales[row];
+  float v[EPL];
+#pragma unroll
+  for (int k = 0; k < EPL; ++k) {
+    const int i = lane * EPL + k;
+    const int c = BITS == 8 ? codes[row * D + i] : (codes[row * (D / 2) + i / 2] >> (4 * (i & 1))) & 0xF;
+    v[k] = __fmul_rn(levels[c], s);
+  }
+  warp_wht<D>(v, lane);
+#pragma unroll
+  for (int k = 0; k < EPL; ++k) {
+    const int i = lane * EPL + k;
+    st_from_float<T>(out + row * D + i, __fmul_rn(v[k], diag[i]));
+  }
+}
+
 template <int D, int BITS, typename T>
 __global__ void __launch_bounds__(256) tq_decode_kernel(const uint8_t* __restrict__ codes,
                                                        const float* __restrict__ scales,
@@ -448,6 +529,64 @@ int aether_compress_emit(const void* c0, const void* z0, const float* bias0, int
   if (d == 64 && bits == 8) launch_emit_t<64, 8>(dtype, p, dst, err, st);
   if (d == 64 && bits == 4) launch_emit_t<64, 4>(dtype, p, dst, err, st);
   return check_launch("compress_emit");
+}
+
+int aether_tq_encode_lut(const void* x, int dtype, long long rows, int d, int bits, const float* diag,
+                         const float* thresholds, float cmax, uint8_t* codes, float* scales, void* stream) {
+  AETHER_REQUIRE(d == 64 || d == 128, "turbo_quant encode: last dim must be 64 or 128, got %d", d);
+  AETHER_REQUIRE(bits == 4 || bits == 8, "bits must be 4 or 8, got %d", bits);
+  AETHER_REQUIRE(dtype >= 0 && dtype <= 2, "turbo_quant encode: unsupported dtype code %d", dtype);
+  AETHER_REQUIRE(cmax > 0.f && thresholds, "turbo_quant encode: bad codebook");
+  if (rows == 0) return 0;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const long long blocks = (rows * 32 + 255) / 256;
+#define AETHER_ENC_LUT(DD, BB)                                                                                   \
+  if (d == DD && bits == BB) {                                                                                   \
+    if (dtype == kF32)                                                                                           \
+      tq_encode_lut_kernel<DD, BB, float><<<blocks, 256, 0, st>>>(static_cast<const float*>(x), diag,          \
+                                                                  thresholds, cmax, codes, scales, rows);      \
+    else if (dtype == kF16)                                                                                      \
+      tq_encode_lut_kernel<DD, BB, __half><<<blocks, 256, 0, st>>>(static_cast<const __half*>(x), diag,        \
+                                                                   thresholds, cmax, codes, scales, rows);     \
+    else                                                                                                         \
+      tq_encode_lut_kernel<DD, BB, __nv_bfloat16><<<blocks, 256, 0, st>>>(                                     \
+          static_cast<const __nv_bfloat16*>(x), diag, thresholds, cmax, codes, scales, rows);                  \
+  }
+  AETHER_ENC_LUT(128, 8)
+  AETHER_ENC_LUT(128, 4)
+  AETHER_ENC_LUT(64, 8)
+  AETHER_ENC_LUT(64, 4)
+#undef AETHER_ENC_LUT
+  return check_launch("turbo_quant encode (Lloyd-Max levels)");
+}
+
+int aether_tq_decode_lut(const uint8_t* codes, const float* scales, long long rows, int d, int bits,
+                         const float* diag, const float* levels, void* out, int out_dtype, void* stream) {
+  AETHER_REQUIRE(d == 64 || d == 128, "turbo_quant decode: last dim must be 64 or 128, got %d", d);
+  AETHER_REQUIRE(bits == 4 || bits == 8, "bits must be 4 or 8, got %d", bits);
+  AETHER_REQUIRE(out_dtype >= 0 && out_dtype <= 2, "turbo_quant decode: unsupported dtype code %d", out_dtype);
+  AETHER_REQUIRE(levels != nullptr, "turbo_quant decode: null codebook");
+  if (rows == 0) return 0;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const long long blocks = (rows * 32 + 255) / 256;
+#define AETHER_DEC_LUT(DD, BB)                                                                                   \
+  if (d == DD && bits == BB) {                                                                                   \
+    if (out_dtype == kF32)                                                                                       \
+      tq_decode_lut_kernel<DD, BB, float><<<blocks, 256, 0, st>>>(codes, scales, diag, levels,                 \
+                                                                  static_cast<float*>(out), rows);             \
+    else if (out_dtype == kF16)                                                                                  \
+      tq_decode_lut_kernel<DD, BB, __half><<<blocks, 256, 0, st>>>(codes, scales, diag, levels,                \
+                                                                   static_cast<__half*>(out), rows);           \
+    else                                                                                                         \
+      tq_decode_lut_kernel<DD, BB, __nv_bfloat16><<<blocks, 256, 0, st>>>(codes, scales, diag, levels,         \
+                                                                          static_cast<__nv_bfloat16*>(out), rows); \
+  }
+  AETHER_DEC_LUT(128, 8)
+  AETHER_DEC_LUT(128, 4)
+  AETHER_DEC_LUT(64, 8)
+  AETHER_DEC_LUT(64, 4)
+#undef AETHER_DEC_LUT
+  return check_launch("turbo_quant decode (Lloyd-Max levels)");
 }
 
 int aether_tq_decode(const uint8_t* codes, const float* scales, long long rows, int d, int bits,

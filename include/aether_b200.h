@@ -71,6 +71,18 @@ int aether_compress_emit(const void* c0, const void* z0, const float* bias0, int
 int aether_tq_decode(const uint8_t* codes, const float* scales, long long rows, int d, int bits,
                      const float* diag, void* out, int out_dtype, void* stream);
 
+/* Lloyd-Max level format (alternative to the uniform levels; no reference
+ * counterpart).  Encode: y = WHT(diag * x), scale = max|y| / cmax, code =
+ * number of the 2^bits - 1 ascending fp32 `thresholds` (level midpoints)
+ * strictly below y / scale; codes uint8 [rows, d] (8-bit) or index nibbles
+ * [rows, d/2] (4-bit, even element low).  Decode: x = diag * WHT(levels[code]
+ * * scale).  The codebook is aether_kernels/codebook.py (Lloyd's algorithm for
+ * N(0, 1)). */
+int aether_tq_encode_lut(const void* x, int dtype, long long rows, int d, int bits, const float* diag,
+                         const float* thresholds, float cmax, uint8_t* codes, float* scales, void* stream);
+int aether_tq_decode_lut(const uint8_t* codes, const float* scales, long long rows, int d, int bits,
+                         const float* diag, const float* levels, void* out, int out_dtype, void* stream);
+
 /* Normalised Walsh-Hadamard transform, fp32 (aether_2b/turbo_quant.py:49-76). */
 int aether_wht(const float* x, float* out, long long rows, int d, void* stream);
 

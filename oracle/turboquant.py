@@ -86,3 +86,58 @@ def decode(codes: torch.Tensor, scale: torch.Tensor, bits: int, seed: int = 42,
     rot = unpack_codes(codes, bits) * scale.to(torch.float32)
     d = rot.shape[-1]
     return (wht(rot) * rademacher(d, seed)).to(out_dtype)
+
+
+# ----------------------------------------------------------------------
+# Lloyd-Max level format (the alternative to the uniform levels; the
+# reference has no such path, so this restates the published algorithm).
+
+
+def lloyd_max_levels(levels: int, iters: int = 2000) -> torch.Tensor:
+    """Lloyd's algorithm for N(0, 1) (Lloyd 1982, Max 1960) in float64:
+    thresholds at midpoints, levels at the conditional means
+    (phi(a) - phi(b)) / (Phi(b) - Phi(a)); symmetric."""
+    import math
+
+    c = torch.tensor([-3.0 + 6.0 * (i + 0.5) / levels for i in range(levels)], dtype=torch.float64)
+    n = torch.distributions.Normal(torch.tensor(0.0, dtype=torch.float64), torch.tensor(1.0, dtype=torch.float64))
+    for _ in range(iters):
+        t = (c[:-1] + c[1:]) / 2
+        a = torch.cat([torch.tensor([-math.inf], dtype=torch.float64), t])
+        b = torch.cat([t, torch.tensor([math.inf], dtype=torch.float64)])
+        pdf = lambda x: torch.where(torch.isinf(x), torch.zeros_like(x), torch.exp(-0.5 * x * x) / math.sqrt(2 * math.pi))
+        new = (pdf(a) - pdf(b)) / (n.cdf(b) - n.cdf(a))
+        new = (new - new.flip(0)) / 2
+        if float((new - c).abs().max()) < 1e-12:
+            c = new
+            break
+        c = new
+    return c
+
+
+def encode_lut(x: torch.Tensor, bits: int, levels: torch.Tensor, seed: int = 42):
+    """Codes are the index of the nearest of the fp32 levels (lower index on a
+    midpoint) of y / scale, scale = max|y| / max(level), y = WHT(diag * x)."""
+    lv = levels.to(torch.float32)
+    thr = (lv[:-1] + lv[1:]) * 0.5
+    d = x.shape[-1]
+    y = wht(x.float() * rademacher(d, seed))
+    m = y.abs().amax(dim=-1, keepdim=True).clamp(min=1e-8)
+    scale = m / lv[-1]
+    u = y / scale
+    idx = torch.searchsorted(thr, u.contiguous(), right=False)  # thresholds strictly below u
+    if bits == 8:
+        return idx.to(torch.uint8), scale
+    q = idx.to(torch.int32)
+    return ((q[..., 0::2] & 0xF) | ((q[..., 1::2] & 0xF) << 4)).to(torch.uint8), scale
+
+
+def decode_lut(codes: torch.Tensor, scale: torch.Tensor, bits: int, levels: torch.Tensor, seed: int = 42):
+    lv = levels.to(torch.float32)
+    if bits == 8:
+        idx = codes.to(torch.long)
+    else:
+        c = codes.to(torch.int32)
+        idx = torch.stack([c & 0xF, (c >> 4) & 0xF], dim=-1).reshape(*codes.shape[:-1], codes.shape[-1] * 2).long()
+    rot = lv[idx] * scale.to(torch.float32)
+    return wht(rot) * rademacher(rot.shape[-1], seed)

@@ -382,3 +382,24 @@ def test_csa_decode_host_buffers_match_device_path(ak):
     o, s = bufs.unpack_outputs(hout)
     assert torch.equal(s, ref_s.cpu())
     assert torch.equal(o, ref_o.cpu())
+
+
+@pytest.mark.parametrize("bits", [8, 4])
+@pytest.mark.parametrize("d", [128, 64])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_tq_lloyd_max_bit_exact(ak, bits, d, dtype):
+    """The Lloyd-Max level format: kernel codes, scales and decodes equal the
+    oracle's bit for bit (same fp32 level table)."""
+    from aether_kernels.codebook import codebook
+    from aether_kernels.turbo_quant import PolarQuant
+
+    g = torch.Generator().manual_seed(bits * 1000 + d)
+    x = (torch.randn(300, d, generator=g) * 3).to(dtype)
+    pq = PolarQuant(bits, codebook="lloyd-max")
+    c, s = pq.encode(x.cuda())
+    lv, _ = codebook(bits)
+    oc, osc = otq.encode_lut(x.float() if dtype == torch.float32 else x, bits, lv)
+    assert torch.equal(c.cpu(), oc)
+    assert torch.equal(s.cpu(), osc)
+    dec = pq.decode(c, s, out_dtype=torch.float32)
+    assert torch.equal(dec.cpu(), otq.decode_lut(oc, osc, bits, lv))
