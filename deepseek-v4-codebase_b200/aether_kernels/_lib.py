@@ -107,6 +107,11 @@ SIGNATURES = {
          _p, _p, _c_int, _c_int, _p, _c_int, _c_int,  # req_info, tiles, ntiles, compression, diag, bits, top_k
          _p, _p, _p, _p],                    # cand_keys, cand_ids, err, stream
     ),
+    "aether_csa_decode_paged_rope": (
+        _c_int,
+        [_p, _p, _p, _p, _p, _p, _p, _p, _p, _c_int, _c_int, _p, _c_int, _p, _p,
+         _c_int, _c_int, _c_int, _c_int, _c_int, _c_f, _p, _p, _p, _p, _c_int, _p, _p, _c_int, _p],
+    ),
     "aether_csa_decode_paged_host": (
         _c_int,
         [_p, _p, ctypes.c_size_t, _p, _p, ctypes.c_size_t,  # host_in, dev_in, in_bytes, host_out, dev_out, out_bytes

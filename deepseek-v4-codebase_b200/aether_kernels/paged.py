@@ -189,6 +189,8 @@ def csa_decode_paged(
     scores: Optional[torch.Tensor] = None,
     overlap_prefetch: bool = False,
     workspace: Optional[torch.Tensor] = None,
+    rope_positions: Optional[torch.Tensor] = None,
+    rope_inv_freq: Optional[torch.Tensor] = None,
 ) -> Tuple[torch.Tensor, torch.Tensor]:
     """One fused CSA decode step for a batch of sequences.
 
@@ -212,6 +214,9 @@ def csa_decode_paged(
     ``workspace`` (optional uint8 tensor of ``csa_workspace_bytes(B, max_pages
     * 64)`` bytes) holds the per-block score keys between the two kernels;
     it is allocated per call when not given (contents need no clearing).
+    ``rope_positions`` (int32 [B]) with ``rope_inv_freq`` (fp32 [rope_dim/2])
+    fuse the inverse output RoPE of aether_2b/serving.py:469-472 into the
+    store: the last rope_dim channels are rotated by -position.
     """
     B, H, D = q.shape
     _check(D == HEAD_DIM, f"head_dim must be {HEAD_DIM}")
@@ -244,7 +249,16 @@ def csa_decode_paged(
         workspace = torch.zeros(max(need, 16), dtype=torch.uint8, device=dev)
     _check(workspace.is_cuda and workspace.numel() * workspace.element_size() >= need,
            f"workspace must hold {need} bytes")
-    if scores is None:
+    if rope_inv_freq is not None:
+        _check(scores is None and cluster <= 1, "the fused output RoPE needs cluster 0 and no score output")
+        _cuda(rope_positions, "rope_positions")
+        _cuda(rope_inv_freq, "rope_inv_freq")
+        _check(rope_positions.dtype == torch.int32 and rope_positions.numel() == B, "rope_positions must be int32 [B]")
+        _check(rope_inv_freq.dtype == torch.float32, "rope_inv_freq must be float32")
+        _lib.call("aether_csa_decode_paged_rope", *common, workspace.data_ptr(), _opt_ptr(err),
+                  int(overlap_prefetch), rope_positions.data_ptr(), rope_inv_freq.data_ptr(),
+                  2 * rope_inv_freq.numel(), _stream(dev))
+    elif scores is None:
         _lib.call("aether_csa_decode_paged", *common, workspace.data_ptr(), _opt_ptr(err), int(cluster),
                   int(overlap_prefetch), _stream(dev))
     else:

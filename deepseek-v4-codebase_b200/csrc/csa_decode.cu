@@ -915,7 +915,9 @@ int csa_decode_cta(const void* q, const float* index_q, const float* index_w, co
                    const int32_t* page_table, int table_stride, int num_pages, const int32_t* nblocks,
                    int max_nblocks, const float* diag_idx, const float* diag_kv, int B, int H, int W, int bits,
                    int top_k, float softmax_scale, void* out, int32_t* sel_out, float* score_out, int score_stride,
-                   uint32_t* workspace, int* err, int pdl, void* stream);
+                   uint32_t* workspace, int* err, int pdl, void* stream,
+                   const int32_t* rope_pos = nullptr, const float* rope_inv_freq = nullptr,
+                   int rope_dim = 0);
 
 }  // namespace aether
 
@@ -937,6 +939,24 @@ int aether_csa_decode_paged(const void* q, const float* index_q, const float* in
   return csa_common(false, q, index_q, index_w, sink, window, window_len, idx_pages, kv_pages,
                     page_table, table_stride, num_pages, nblocks, max_nblocks, diag_idx, diag_kv, B, H, W, bits,
                     top_k, softmax_scale, out, sel_out, err, cluster, stream);
+}
+
+// aether_csa_decode_paged (score + select/attend kernels) that also applies
+// the inverse output RoPE: the last rope_dim channels of each head's output
+// are rotated by -rope_pos[b] with rope_inv_freq [rope_dim / 2], as
+// aether_2b/serving.py:469-472 does before the output projection.
+int aether_csa_decode_paged_rope(const void* q, const float* index_q, const float* index_w, const float* sink,
+                                 const void* window, const int32_t* window_len, const uint8_t* idx_pages,
+                                 const uint8_t* kv_pages, const int32_t* page_table, int table_stride, int num_pages,
+                                 const int32_t* nblocks, int max_nblocks, const float* diag_idx, const float* diag_kv,
+                                 int B, int H, int W, int bits, int top_k, float softmax_scale, void* out,
+                                 int32_t* sel_out, uint32_t* workspace, int* err, int pdl, const int32_t* rope_pos,
+                                 const float* rope_inv_freq, int rope_dim, void* stream) {
+  AETHER_REQUIRE(index_q && index_w && idx_pages && diag_idx, "csa_decode_paged: null index input");
+  AETHER_REQUIRE(rope_inv_freq && rope_pos, "csa_decode_paged_rope: null RoPE input");
+  return csa_decode_cta(q, index_q, index_w, sink, window, window_len, idx_pages, kv_pages, page_table, table_stride,
+                        num_pages, nblocks, max_nblocks, diag_idx, diag_kv, B, H, W, bits, top_k, softmax_scale, out,
+                        sel_out, nullptr, 0, workspace, err, pdl, stream, rope_pos, rope_inv_freq, rope_dim);
 }
 
 // aether_csa_decode_paged with host buffers: copies in_bytes of packed

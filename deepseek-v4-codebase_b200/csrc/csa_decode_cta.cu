@@ -161,6 +161,11 @@ struct QParams {
   // (null: row b, rows b * W ..)
   const int32_t* q_row;
   const long long* win_row;
+  // optional inverse output RoPE (aether_2b/serving.py:469-472): rotate the
+  // last rope_dim output channels by -rope_pos[b] with rope_inv_freq
+  const int32_t* rope_pos;
+  const float* rope_inv_freq;
+  int rope_dim;
   long long* dbg;  // per-CTA phase timestamps [grid][16] (profiling aid), or null
   int* err;
   int table_stride, num_pages, H, W, top_k;
@@ -1044,8 +1049,25 @@ __global__ void __launch_bounds__(kQThreads, CS > 1 ? AETHER_ATTEND_MINB : 1) cs
         const float Ms = fmaxf(M, sk);
         const float a = M == -INFINITY ? 0.f : __expf(M - Ms);
         const float inv = a / (L * a + __expf(sk - Ms));
-        __nv_bfloat162 o01 = __floats2bfloat162_rn(o[0] * inv, o[1] * inv);
-        __nv_bfloat162 o23 = __floats2bfloat162_rn(o[2] * inv, o[3] * inv);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) o[k] *= inv;
+        if (p.rope_inv_freq) {
+          const float pos = static_cast<float>(-p.rope_pos[b]);
+          const int first = kHeadDim - p.rope_dim;
+#pragma unroll
+          for (int k = 0; k < 4; k += 2) {
+            const int dd = lane * 4 + k;  // even channel of the pair (dd, dd + 1)
+            if (dd >= first) {
+              const float ang = pos * p.rope_inv_freq[(dd - first) >> 1];
+              const float cs = cosf(ang), sn = sinf(ang);
+              const float x0 = o[k], x1 = o[k + 1];
+              o[k] = x0 * cs - x1 * sn;
+              o[k + 1] = x1 * cs + x0 * sn;
+            }
+          }
+        }
+        __nv_bfloat162 o01 = __floats2bfloat162_rn(o[0], o[1]);
+        __nv_bfloat162 o23 = __floats2bfloat162_rn(o[2], o[3]);
         *reinterpret_cast<uint2*>(p.out + (static_cast<long long>(b) * p.H + h) * kHeadDim + lane * 4) =
             make_uint2(*reinterpret_cast<uint32_t*>(&o01), *reinterpret_cast<uint32_t*>(&o23));
       }
@@ -1229,8 +1251,11 @@ int csa_decode_cta(const void* q, const float* index_q, const float* index_w, co
                    const int32_t* page_table, int table_stride, int num_pages, const int32_t* nblocks,
                    int max_nblocks, const float* diag_idx, const float* diag_kv, int B, int H, int W, int bits,
                    int top_k, float softmax_scale, void* out, int32_t* sel_out, float* score_out, int score_stride,
-                   uint32_t* workspace, int* err, int pdl, void* stream) {
+                   uint32_t* workspace, int* err, int pdl, void* stream, const int32_t* rope_pos,
+                   const float* rope_inv_freq, int rope_dim) {
   int rc = check_common(bits, H, W, top_k, max_nblocks, table_stride, num_pages);
+  AETHER_REQUIRE(!rope_inv_freq || (rope_pos && rope_dim > 0 && rope_dim <= kHeadDim && rope_dim % 4 == 0),
+                 "csa decode: output RoPE needs positions and rope_dim in (0, 128], a multiple of 4");
   if (rc) return rc;
   AETHER_REQUIRE(workspace != nullptr, "csa decode: workspace is required");
   AETHER_REQUIRE(!score_out || max_nblocks <= kMaxKeys, "csa decode: score output is limited to %d blocks", kMaxKeys);
@@ -1241,6 +1266,9 @@ int csa_decode_cta(const void* q, const float* index_q, const float* index_w, co
   p.sel_out = sel_out;
   p.score_out = score_out;
   p.score_stride = score_stride;
+  p.rope_pos = rope_pos;
+  p.rope_inv_freq = rope_inv_freq;
+  p.rope_dim = rope_dim;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   rc = bits == 4 ? run_decode<4>(p, B, max_nblocks, pdl != 0, st, reinterpret_cast<uint8_t*>(workspace))
                  : run_decode<8>(p, B, max_nblocks, pdl != 0, st, reinterpret_cast<uint8_t*>(workspace));

@@ -153,6 +153,19 @@ int aether_csa_decode_paged(const void* q, const float* index_q, const float* in
                             int B, int H, int W, int bits, int top_k, float softmax_scale, void* out,
                             int32_t* sel_out, uint32_t* workspace, int* err, int cluster, int pdl, void* stream);
 
+/* As aether_csa_decode_paged (cluster 0) with the inverse output RoPE fused
+ * into the final store (aether_2b/serving.py:469-472): the last rope_dim
+ * channels (a multiple of 4) of every head's output are rotated in
+ * interleaved pairs by -rope_pos[b] * rope_inv_freq[i] (rope_inv_freq
+ * [rope_dim / 2], e.g. get_rope_freqs of modeling.py:60-99). */
+int aether_csa_decode_paged_rope(const void* q, const float* index_q, const float* index_w, const float* sink,
+                                 const void* window, const int32_t* window_len, const uint8_t* idx_pages,
+                                 const uint8_t* kv_pages, const int32_t* page_table, int table_stride, int num_pages,
+                                 const int32_t* nblocks, int max_nblocks, const float* diag_idx, const float* diag_kv,
+                                 int B, int H, int W, int bits, int top_k, float softmax_scale, void* out,
+                                 int32_t* sel_out, uint32_t* workspace, int* err, int pdl, const int32_t* rope_pos,
+                                 const float* rope_inv_freq, int rope_dim, void* stream);
+
 /* As aether_csa_decode_paged, also writing each visible block's index score
  * to score_out[b * score_stride + block]. */
 int aether_csa_decode_paged_scores(const void* q, const float* index_q, const float* index_w, const float* sink,

@@ -403,3 +403,27 @@ def test_tq_lloyd_max_bit_exact(ak, bits, d, dtype):
     assert torch.equal(s.cpu(), osc)
     dec = pq.decode(c, s, out_dtype=torch.float32)
     assert torch.equal(dec.cpu(), otq.decode_lut(oc, osc, bits, lv))
+
+
+def test_csa_decode_fused_output_rope(ak):
+    """The fused inverse output RoPE equals the oracle's attention output
+    rotated by -position (aether_2b/serving.py:469-472)."""
+    from aether_kernels.paged import csa_decode_paged
+    from aether_kernels.rope import RopeConfig, get_rope_freqs
+    from aether_kernels.synthetic import make_decode_batch
+    from oracle import compress as ocmp
+
+    b = make_decode_batch("csa", 6, 3000, 20000, 4, 4, seed=88, device="cuda")
+    inv = get_rope_freqs(RopeConfig.yarn(4.0))[:32].float()
+    pos = torch.tensor(b.tokens, dtype=torch.int32)
+    out, sel = csa_decode_paged(b.q, b.index_q, b.index_weight, b.sink, b.window, b.window_len, b.cache,
+                                b.page_table, b.nblocks, b.softmax_scale, rope_positions=pos.cuda(),
+                                rope_inv_freq=inv.cuda())
+    torch.cuda.synchronize()
+    ref = _oracle(b)
+    for i in range(6):
+        k = min(256, int(b.nblocks[i]))
+        assert torch.equal(sel[i, :k].cpu().long(), ref.selected[i]) or ref.near_tie[i]
+    rot = torch.stack([ocmp.rope(ref.out[i], (-pos[i:i + 1]).expand(12), inv) for i in range(6)])
+    diff = (out.float().cpu() - rot).abs()
+    assert diff.max() < MAX_ABS and diff.mean() < MEAN_ABS, (float(diff.max()), float(diff.mean()))
