@@ -26,7 +26,15 @@ def _cuda(t: torch.Tensor, name: str) -> None:
     _check(t.is_contiguous(), f"{name} must be contiguous")
 
 
+_RAW_STREAM = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def _stream(dev: torch.device) -> int:
+    """cudaStream_t of the current stream on ``dev`` (the raw accessor when
+    torch has it: the Stream object path costs microseconds per call)."""
+    if _RAW_STREAM is not None:
+        idx = dev.index if dev.index is not None else torch.cuda.current_device()
+        return _RAW_STREAM(idx)
     return torch.cuda.current_stream(dev).cuda_stream
 
 
