@@ -411,7 +411,8 @@ def main():
     def e2e_step(i):
         st = sets[i % len(sets)]
         csa_decode_paged_host(slot_bufs[i & 1], host_ins[i % len(sets)], host_outs[i & 1], st.sink, st.window,
-                              cache, st.page_table, st.softmax_scale, ws_e2e, err, copies=copies, slot=i & 1)
+                              cache, st.page_table, st.softmax_scale, ws_e2e, err, copies=copies, slot=i & 1,
+                              overlap_prefetch=args.pdl)
 
     with torch.cuda.stream(stream):
         for i in range(4):

@@ -119,7 +119,8 @@ SIGNATURES = {
          _p, _p, _p, _c_int, _c_int, _p, _c_int,             # idx_pages, kv_pages, page_table, stride, num_pages, nblocks, max_nb
          _p, _p, _c_int, _c_int, _c_int, _c_int, _c_int, _c_f,  # diag_idx, diag_kv, B, H, W, bits, top_k, scale
          _p, _p, _p, _p, _c_int, _p,                          # out, sel_out, workspace, err, pdl, stream
-         _p, _p, _p, _p, _p],                                 # h2d_stream, d2h_stream, ev_h2d, ev_comp, ev_d2h
+         _p, _p, _p, _p, _p,                                  # h2d_stream, d2h_stream, ev_h2d, ev_comp, ev_d2h
+         _p, ctypes.c_uint32],                                # slot_flags, seq
     ),
     "aether_hca_decode_paged": (
         _c_int,

@@ -291,6 +291,10 @@ class HostDecodeBuffers:
         self.inputs = self._views(self.dev_in, self.in_shapes, self.in_offsets)
         self.out, self.indices = self._views(self.dev_out, self.out_shapes, self.out_offsets)
         self._ws_key, self._ws_need, self._diags = None, 0, (0, 0)
+        # copy-completion words [input copied, output copied] and the step
+        # sequence number written into them (steps with copy streams)
+        self.slot_flags = torch.zeros(2, dtype=torch.int32, device=self.device)
+        self.seq = 0
 
     @staticmethod
     def _layout(shapes):
@@ -355,13 +359,17 @@ def csa_decode_paged_host(bufs: HostDecodeBuffers, host_in: torch.Tensor, host_o
                           sink: torch.Tensor, window: torch.Tensor, cache: TurboQuantPagedCache,
                           page_table: torch.Tensor, softmax_scale: float, workspace: torch.Tensor,
                           err: Optional[torch.Tensor] = None, copies: Optional[CopyStreams] = None,
-                          slot: int = 0) -> None:
+                          slot: int = 0, overlap_prefetch: bool = False) -> None:
     """One CSA decode step with host buffers, enqueued by a single C call: the
     packed inputs are copied from pinned ``host_in`` to the device, the decode
     runs on the current stream, and the packed output and indices are copied
     to pinned ``host_out`` (read them with ``bufs.unpack_outputs`` once the
     copy has completed).  With ``copies`` the transfers run on its streams,
-    ordered by the slot's events; pass a different ``bufs`` per slot."""
+    ordered by the slot's events and by ``bufs``' copy-completion words, which
+    the kernels poll; pass a different ``bufs`` per slot, and the same slot
+    index with the same ``bufs`` every time.  ``overlap_prefetch`` as in
+    ``csa_decode_paged``: only when no kernel before this step on the stream
+    writes the cache pages or the page table."""
     # host buffers from pack_inputs / new_host_output are pinned; others work
     # but their copies are synchronous
     _check(host_in.numel() >= bufs.in_bytes and host_out.numel() >= bufs.out_bytes, "host buffers too small")
@@ -376,15 +384,17 @@ def csa_decode_paged_host(bufs: HostDecodeBuffers, host_in: torch.Tensor, host_o
         bufs._ws_key = key
     _check(workspace.is_cuda and workspace.numel() * workspace.element_size() >= bufs._ws_need,
            f"workspace must hold {bufs._ws_need} bytes")
+    if copies is not None:
+        bufs.seq = (bufs.seq + 1) & 0xFFFFFFFF
     _lib.call("aether_csa_decode_paged_host", host_in.data_ptr(), bufs.dev_in.data_ptr(), bufs.in_bytes,
               host_out.data_ptr(), bufs.dev_out.data_ptr(), bufs.out_bytes, q.data_ptr(), iq.data_ptr(),
               iw.data_ptr(), sink.data_ptr(), window.data_ptr(), wl.data_ptr(), cache.idx_pages.data_ptr(),
               cache.kv_pages.data_ptr(), page_table.data_ptr(), page_table.shape[1], cache.num_pages, nb.data_ptr(),
               page_table.shape[1] * PAGE, bufs._diags[0], bufs._diags[1], bufs.batch, bufs.heads, window.shape[1],
               cache.bits, bufs.top_k, float(softmax_scale), bufs.out.data_ptr(), bufs.indices.data_ptr(),
-              workspace.data_ptr(), _opt_ptr(err), 0, _stream(dev),
-              *((copies.h2d.cuda_stream, copies.d2h.cuda_stream, *[e.cuda_event for e in copies.events[slot]])
-                if copies is not None else (None,) * 5))
+              workspace.data_ptr(), _opt_ptr(err), int(overlap_prefetch), _stream(dev),
+              *((copies.h2d.cuda_stream, copies.d2h.cuda_stream, *[e.cuda_event for e in copies.events[slot]],
+                 bufs.slot_flags.data_ptr(), bufs.seq) if copies is not None else (None,) * 6 + (0,)))
 
 def hca_decode_paged(
     q: torch.Tensor,

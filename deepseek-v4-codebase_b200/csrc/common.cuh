@@ -65,6 +65,22 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
   return false;
 }
 
+// Bounded wait until the sequence word *flag has reached `target` (u32
+// sequence numbers compared with wrap-around).  The word is written by a
+// stream memory operation on a copy stream after that stream's copy, so the
+// wait never depends on another kernel making progress.  Returns false (and
+// flags the error) after ~2^20 polls (about 0.1 s).
+__device__ __forceinline__ bool flag_wait(const uint32_t* flag, uint32_t target, int* err) {
+  for (int it = 0; it < (1 << 20); ++it) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
+    if (static_cast<int32_t>(v - target) >= 0) return true;
+    __nanosleep(100);
+  }
+  report_error(err, kErrWaitTimeout);
+  return false;
+}
+
 // Bulk global->shared copy (TMA engine, no tensor map, no multicast).
 // dst, src 16-byte aligned; bytes a multiple of 16.
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {

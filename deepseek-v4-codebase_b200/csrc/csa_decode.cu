@@ -917,7 +917,7 @@ int csa_decode_cta(const void* q, const float* index_q, const float* index_w, co
                    int top_k, float softmax_scale, void* out, int32_t* sel_out, float* score_out, int score_stride,
                    uint32_t* workspace, int* err, int pdl, void* stream,
                    const int32_t* rope_pos = nullptr, const float* rope_inv_freq = nullptr,
-                   int rope_dim = 0);
+                   int rope_dim = 0, const uint32_t* step_flags = nullptr, uint32_t step_seq = 0);
 
 }  // namespace aether
 
@@ -965,11 +965,43 @@ int aether_csa_decode_paged_rope(const void* q, const float* index_q, const floa
 // enqueued by this one call.  The device pointers (q, index_q, ..., out,
 // sel_out) point into dev_in / dev_out.  With h2d_stream / d2h_stream and the
 // slot's three events (ev_h2d, ev_comp, ev_d2h) given, the input copy runs on
-// h2d_stream after the slot's previous decode, the decode on `stream` after
-// the input copy and the slot's previous output copy, and the output copy on
-// d2h_stream after the decode; alternating two slots (staging buffers and
-// events) lets one step's copies overlap its neighbours' kernels.  With
-// them null everything runs on `stream` in order.
+// h2d_stream after the slot's previous decode, the decode on `stream`, and the
+// output copy on d2h_stream after the decode; alternating two slots (staging
+// buffers and events) lets one step's copies overlap its neighbours' kernels.
+// With them null everything runs on `stream` in order.
+//
+// How the decode waits for its copies: a stream wait on another stream's
+// event in front of the score kernel also ends the programmatic (PDL)
+// overlap with the previous step's attend kernel, which costs ~3.5 us per
+// step.  With slot_flags (two device u32 words per staging slot, zero
+// before the slot's first step) and seq (1, 2, 3, ... per slot, mod 2^32), the copy
+// streams instead write seq into slot_flags[0] after the input copy and into
+// slot_flags[1] after the output copy (stream memory operations), and the
+// kernels poll them with bounded waits: the score kernel for this step's
+// inputs, the attend kernel for the slot's previous output copy before its
+// stores.  Without slot_flags, or where the driver lacks stream memory
+// operations, the decode stream waits on ev_h2d and ev_d2h instead.
+typedef int (*WriteValue32Fn)(cudaStream_t, unsigned long long, unsigned int, unsigned int);
+static WriteValue32Fn write_value32() {
+  static const WriteValue32Fn fn = [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuStreamWriteValue32", &f, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess) {
+      cudaGetLastError();
+      return static_cast<WriteValue32Fn>(nullptr);
+    }
+    return reinterpret_cast<WriteValue32Fn>(f);
+  }();
+  return fn;
+}
+
+static int write_seq(cudaStream_t s, uint32_t* word, uint32_t seq, const char* what) {
+  const int rc = write_value32()(s, reinterpret_cast<unsigned long long>(word), seq, 0u);
+  AETHER_REQUIRE(rc == 0, "csa_decode_paged_host: %s (driver error %d)", what, rc);
+  return 0;
+}
+
 int aether_csa_decode_paged_host(const void* host_in, void* dev_in, size_t in_bytes, void* host_out,
                                  const void* dev_out, size_t out_bytes, const void* q, const float* index_q,
                                  const float* index_w, const float* sink, const void* window,
@@ -978,11 +1010,15 @@ int aether_csa_decode_paged_host(const void* host_in, void* dev_in, size_t in_by
                                  int max_nblocks, const float* diag_idx, const float* diag_kv, int B, int H, int W,
                                  int bits, int top_k, float softmax_scale, void* out, int32_t* sel_out,
                                  uint32_t* workspace, int* err, int pdl, void* stream, void* h2d_stream,
-                                 void* d2h_stream, void* ev_h2d, void* ev_comp, void* ev_d2h) {
+                                 void* d2h_stream, void* ev_h2d, void* ev_comp, void* ev_d2h, uint32_t* slot_flags,
+                                 uint32_t seq) {
   AETHER_REQUIRE(host_in && dev_in && host_out && dev_out, "csa_decode_paged_host: null buffer");
+  AETHER_REQUIRE(index_q && index_w && idx_pages && diag_idx, "csa_decode_paged: null index input");
   const bool split = h2d_stream != nullptr;
   AETHER_REQUIRE(!split || (d2h_stream && ev_h2d && ev_comp && ev_d2h),
                  "csa_decode_paged_host: copy streams need d2h_stream and the slot's three events");
+  AETHER_REQUIRE(!slot_flags || split, "csa_decode_paged_host: slot flags need copy streams");
+  const bool flags = slot_flags != nullptr && write_value32() != nullptr;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   cudaStream_t sin = split ? static_cast<cudaStream_t>(h2d_stream) : st;
   cudaStream_t sout = split ? static_cast<cudaStream_t>(d2h_stream) : st;
@@ -991,15 +1027,17 @@ int aether_csa_decode_paged_host(const void* host_in, void* dev_in, size_t in_by
   if (split) AETHER_CUDA_TRY(cudaStreamWaitEvent(sin, ec, 0), "csa_decode_paged_host: order input copy");
   AETHER_CUDA_TRY(cudaMemcpyAsync(dev_in, host_in, in_bytes, cudaMemcpyHostToDevice, sin),
                   "csa_decode_paged_host: input copy");
-  if (split) {
+  if (flags) {
+    if (int rc = write_seq(sin, slot_flags, seq, "input flag")) return rc;
+  } else if (split) {
     AETHER_CUDA_TRY(cudaEventRecord(eh, sin), "csa_decode_paged_host: record input copy");
     AETHER_CUDA_TRY(cudaStreamWaitEvent(st, eh, 0), "csa_decode_paged_host: wait input copy");
     AETHER_CUDA_TRY(cudaStreamWaitEvent(st, ed, 0), "csa_decode_paged_host: wait output slot");
   }
-  const int rc = aether_csa_decode_paged(q, index_q, index_w, sink, window, window_len, idx_pages, kv_pages,
-                                         page_table, table_stride, num_pages, nblocks, max_nblocks, diag_idx, diag_kv,
-                                         B, H, W, bits, top_k, softmax_scale, out, sel_out, workspace, err, 0, pdl,
-                                         stream);
+  const int rc = csa_decode_cta(q, index_q, index_w, sink, window, window_len, idx_pages, kv_pages, page_table,
+                                table_stride, num_pages, nblocks, max_nblocks, diag_idx, diag_kv, B, H, W, bits,
+                                top_k, softmax_scale, out, sel_out, nullptr, 0, workspace, err, pdl, stream, nullptr,
+                                nullptr, 0, flags ? slot_flags : nullptr, seq);
   if (rc) return rc;
   if (split) {
     AETHER_CUDA_TRY(cudaEventRecord(ec, st), "csa_decode_paged_host: record decode");
@@ -1007,6 +1045,9 @@ int aether_csa_decode_paged_host(const void* host_in, void* dev_in, size_t in_by
   }
   AETHER_CUDA_TRY(cudaMemcpyAsync(host_out, dev_out, out_bytes, cudaMemcpyDeviceToHost, sout),
                   "csa_decode_paged_host: output copy");
+  if (flags) {
+    if (int rc2 = write_seq(sout, slot_flags + 1, seq, "output flag")) return rc2;
+  }
   if (split) AETHER_CUDA_TRY(cudaEventRecord(ed, sout), "csa_decode_paged_host: record output copy");
   return 0;
 }

@@ -166,6 +166,12 @@ struct QParams {
   const int32_t* rope_pos;
   const float* rope_inv_freq;
   int rope_dim;
+  // host-buffer steps on copy streams: step_flags[0] reaches step_seq once
+  // this step's inputs are on the device, step_flags[1] reaches step_seq - 1
+  // once the previous output copy from the same staging slot is done (null:
+  // the stream orders both)
+  const uint32_t* step_flags;
+  uint32_t step_seq;
   long long* dbg;  // per-CTA phase timestamps [grid][16] (profiling aid), or null
   int* err;
   int table_stride, num_pages, H, W, top_k;
@@ -400,6 +406,10 @@ __global__ void __launch_bounds__(kSThreads) csa_score_kernel(QParams p, int spl
     if (dbg && tid == 0) dbg[slot] = clock64();
   };
   stamp(0);
+  if (p.step_flags) {  // this step's inputs are copied on another stream
+    if (tid == 0) flag_wait(p.step_flags, p.step_seq, p.err);
+    __syncthreads();
+  }
   pdl_launch_dependents();
   int nb = p.nblocks[b];
   nb = max(0, min(nb, min(kMaxBlocks, p.table_stride * kPage)));
@@ -626,6 +636,9 @@ __global__ void __launch_bounds__(kQThreads, CS > 1 ? AETHER_ATTEND_MINB : 1) cs
   }
   // the block keys come from the score kernel (or a previous select)
   pdl_wait();
+  // the staging slot's previous output copy must be done before this step's
+  // stores (the __syncthreads below orders the other threads)
+  if (p.step_flags && tid == 0) flag_wait(p.step_flags + 1, p.step_seq - 1u, p.err);
   stamp(2, tid == 0);
   constexpr int PER = kMaxKeys / kQThreads;  // 16 keys per thread, in source order
   const int i0 = tid * PER;
@@ -1252,7 +1265,7 @@ int csa_decode_cta(const void* q, const float* index_q, const float* index_w, co
                    int max_nblocks, const float* diag_idx, const float* diag_kv, int B, int H, int W, int bits,
                    int top_k, float softmax_scale, void* out, int32_t* sel_out, float* score_out, int score_stride,
                    uint32_t* workspace, int* err, int pdl, void* stream, const int32_t* rope_pos,
-                   const float* rope_inv_freq, int rope_dim) {
+                   const float* rope_inv_freq, int rope_dim, const uint32_t* step_flags, uint32_t step_seq) {
   int rc = check_common(bits, H, W, top_k, max_nblocks, table_stride, num_pages);
   AETHER_REQUIRE(!rope_inv_freq || (rope_pos && rope_dim > 0 && rope_dim <= kHeadDim && rope_dim % 4 == 0),
                  "csa decode: output RoPE needs positions and rope_dim in (0, 128], a multiple of 4");
@@ -1269,6 +1282,8 @@ int csa_decode_cta(const void* q, const float* index_q, const float* index_w, co
   p.rope_pos = rope_pos;
   p.rope_inv_freq = rope_inv_freq;
   p.rope_dim = rope_dim;
+  p.step_flags = step_flags;
+  p.step_seq = step_seq;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   rc = bits == 4 ? run_decode<4>(p, B, max_nblocks, pdl != 0, st, reinterpret_cast<uint8_t*>(workspace))
                  : run_decode<8>(p, B, max_nblocks, pdl != 0, st, reinterpret_cast<uint8_t*>(workspace));

@@ -186,7 +186,13 @@ int aether_csa_decode_paged_scores(const void* q, const float* index_q, const fl
  * (cudaEvent_t) are optional (NULL: everything in order on `stream`); with
  * them the input copy waits for the slot's previous decode, the decode for the
  * input copy and the slot's previous output copy, and the output copy for the
- * decode, so callers alternating two slots overlap copies with kernels. */
+ * decode, so callers alternating two slots overlap copies with kernels.
+ * slot_flags (optional, with copy streams): two device u32 words per staging
+ * slot, zero before its first step, and seq = 1, 2, 3, ... per slot.  The
+ * copy streams then publish copy completion by writing seq into the words
+ * (stream memory operations) and the kernels poll them with bounded waits, so
+ * the decode stream carries no cross-stream wait and consecutive steps keep
+ * their programmatic-launch overlap.  A poll that runs out sets bit 1 of *err. */
 int aether_csa_decode_paged_host(const void* host_in, void* dev_in, size_t in_bytes, void* host_out,
                                  const void* dev_out, size_t out_bytes, const void* q, const float* index_q,
                                  const float* index_w, const float* sink, const void* window,
@@ -195,7 +201,8 @@ int aether_csa_decode_paged_host(const void* host_in, void* dev_in, size_t in_by
                                  int max_nblocks, const float* diag_idx, const float* diag_kv, int B, int H, int W,
                                  int bits, int top_k, float softmax_scale, void* out, int32_t* sel_out,
                                  uint32_t* workspace, int* err, int pdl, void* stream, void* h2d_stream,
-                                 void* d2h_stream, void* ev_h2d, void* ev_comp, void* ev_d2h);
+                                 void* d2h_stream, void* ev_h2d, void* ev_comp, void* ev_d2h, uint32_t* slot_flags,
+                                 uint32_t seq);
 
 /* One HCA decode step (replaces aether_2b/serving.py:507-522): attention over
  * every visible compressed block plus the window; nblocks <= 1024. */

@@ -384,6 +384,60 @@ def test_csa_decode_host_buffers_match_device_path(ak):
     assert torch.equal(o, ref_o.cpu())
 
 
+def test_csa_decode_host_buffers_copy_streams(ak):
+    """Host-buffer steps on copy streams, two staging slots, kernels ordered
+    by the slots' copy-completion words: every step's host result equals the
+    device-resident path's, and no bounded wait runs out."""
+    from aether_kernels.paged import (CopyStreams, HostDecodeBuffers, csa_decode_paged, csa_decode_paged_host,
+                                      csa_workspace_bytes)
+    from aether_kernels.synthetic import make_decode_batch
+
+    batches = [make_decode_batch("csa", 8, 3000, 20000, 4, 4, seed=300 + k, device="cuda") for k in range(3)]
+    refs = [csa_decode_paged(b.q, b.index_q, b.index_weight, b.sink, b.window, b.window_len, b.cache, b.page_table,
+                             b.nblocks, b.softmax_scale) for b in batches]
+    bufs = [HostDecodeBuffers(8, 12, 256, "cuda") for _ in range(2)]
+    hins = [bufs[0].pack_inputs(b.q, b.index_q, b.index_weight, b.window_len, b.nblocks) for b in batches]
+    copies = CopyStreams(torch.device("cuda"))
+    ws = torch.zeros(max(csa_workspace_bytes(8, b.page_table.shape[1] * 64) for b in batches), dtype=torch.uint8,
+                     device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    steps = 12
+    houts = [bufs[0].new_host_output() for _ in range(steps)]
+    for i in range(steps):
+        b = batches[i % 3]
+        csa_decode_paged_host(bufs[i & 1], hins[i % 3], houts[i], b.sink, b.window, b.cache, b.page_table,
+                              b.softmax_scale, ws, err, copies=copies, slot=i & 1, overlap_prefetch=True)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    assert bufs[0].seq == steps // 2 and bufs[1].seq == steps // 2
+    for i in range(steps):
+        o, s = bufs[0].unpack_outputs(houts[i])
+        assert torch.equal(s, refs[i % 3][1].cpu()), i
+        assert torch.equal(o, refs[i % 3][0].cpu()), i
+
+
+def test_csa_decode_host_slot_wait_runs_out(ak):
+    """A copy-completion word that never reaches its target: the attend
+    kernel's bounded poll gives up (about 0.1 s), sets the wait-timeout bit and
+    the step still completes; the context stays usable."""
+    from aether_kernels.paged import CopyStreams, HostDecodeBuffers, csa_decode_paged_host, csa_workspace_bytes
+    from aether_kernels.synthetic import make_decode_batch
+
+    b = make_decode_batch("csa", 2, 3000, 20000, 4, 4, seed=91, device="cuda")
+    bufs = HostDecodeBuffers(2, 12, 256, "cuda")
+    hin = bufs.pack_inputs(b.q, b.index_q, b.index_weight, b.window_len, b.nblocks)
+    hout = bufs.new_host_output()
+    ws = torch.zeros(csa_workspace_bytes(2, b.page_table.shape[1] * 64), dtype=torch.uint8, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    bufs.seq = 1000  # the output word holds 0, the step waits for 1000
+    csa_decode_paged_host(bufs, hin, hout, b.sink, b.window, b.cache, b.page_table, b.softmax_scale, ws, err,
+                          copies=CopyStreams(torch.device("cuda")), slot=0)
+    torch.cuda.synchronize()
+    assert int(err.item()) & 1
+    assert bufs.slot_flags.tolist() == [1001, 1001]
+    torch.ones(4, device="cuda").sum().item()  # the context still works
+
+
 @pytest.mark.parametrize("bits", [8, 4])
 @pytest.mark.parametrize("d", [128, 64])
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
