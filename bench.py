@@ -10,7 +10,7 @@ A *query* is one sequence x one step x one layer.
   value      queries/s over all ranks, inputs resident in HBM; steps replayed
              from a CUDA graph; every step reads a different cache set, and
              the sets together are > 4x L2 so every step reads cold HBM
-  e2e        queries/s through the public Python API (``csa_decode_paged``)
+  e2e        queries/s through the public host-buffer API (``CsaDecodeHostPlan``)
              with the step's inputs copied from pinned host memory and the
              outputs copied back inside the timed region
   roofline   algorithmic bytes per launch / CUDA-event launch time, against
@@ -390,50 +390,46 @@ def main():
     achieved = bytes_launch / (ms_step / 1e3) / 1e9
     peak, peak_src = read_peak()
 
-    # ---- e2e through the public C-ABI call with host buffers: every step is
-    # one aether_csa_decode_paged_host call (csa_decode_paged_host), which
+    # ---- e2e through the public C-ABI with host buffers: every step is one
+    # aether_csa_decode_host_plan_step call (CsaDecodeHostPlan.step), which
     # enqueues the copy of that step's packed inputs (q, index q, head
     # weights, window lengths, block counts of the step's cache set) from
     # pinned host memory, the decode, and the copy of the packed output and
     # selected indices back to pinned host memory.
-    from aether_kernels.paged import CopyStreams, HostDecodeBuffers, csa_decode_paged_host
+    from aether_kernels.paged import CsaDecodeHostPlan
 
-    # two staging slots on copy streams: a step's copies overlap its
-    # neighbours' kernels
-    slot_bufs = [HostDecodeBuffers(B, CFG["heads"], CFG["top_k"], dev) for _ in range(2)]
-    bufs = slot_bufs[0]
-    copies = CopyStreams(dev)
-    host_ins = [bufs.pack_inputs(st.q, st.index_q, st.index_weight, st.window_len, st.nblocks) for st in sets]
-    host_outs = [bufs.new_host_output() for _ in range(2)]
-    ws_e2e = torch.zeros(max_ws_bytes(B), dtype=torch.uint8, device=dev)
-    h2d, d2h = bufs.in_bytes, bufs.out_bytes
+    # a prepared plan: two staging slots on copy streams, so a step's copies
+    # overlap its neighbours' kernels, and one short C call per step
+    plan = CsaDecodeHostPlan(cache, B, max(st.page_table.shape[1] for st in sets), CFG["heads"], CFG["top_k"],
+                             window=sets[0].window.shape[1], err=err, overlap_prefetch=args.pdl, device=dev)
+    host_ins = [plan.pack_inputs(st.q, st.index_q, st.index_weight, st.window_len, st.nblocks) for st in sets]
+    host_outs = [plan.new_host_output() for _ in range(2)]
+    h2d, d2h = plan.in_bytes, plan.out_bytes
 
     def e2e_step(i):
         st = sets[i % len(sets)]
-        csa_decode_paged_host(slot_bufs[i & 1], host_ins[i % len(sets)], host_outs[i & 1], st.sink, st.window,
-                              cache, st.page_table, st.softmax_scale, ws_e2e, err, copies=copies, slot=i & 1,
-                              overlap_prefetch=args.pdl)
+        plan.step(host_ins[i % len(sets)], host_outs[i & 1], st.page_table, st.sink, st.window, st.softmax_scale)
 
     with torch.cuda.stream(stream):
         for i in range(4):
             e2e_step(i)
+        plan.fence(wait_for_copies=True)
         stream.synchronize()
         # the host copy of a result matches the device-resident path
         ref_o, ref_s = csa_decode_paged(sets[3].q, sets[3].index_q, sets[3].index_weight, sets[3].sink,
                                         sets[3].window, sets[3].window_len, cache, sets[3].page_table,
                                         sets[3].nblocks, sets[3].softmax_scale, top_k=sets[3].top_k)
         torch.cuda.synchronize(dev)
-        ho, hs = bufs.unpack_outputs(host_outs[1])
+        ho, hs = plan.unpack_outputs(host_outs[1])
         assert torch.equal(hs, ref_s.cpu()) and torch.equal(ho, ref_o.cpu()), "host-buffer decode differs"
         if world > 1:
             torch.distributed.barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
-        copies.h2d.wait_stream(stream)  # the first input copy starts inside the timed region
+        plan.fence(wait_for_copies=False)  # the first input copy starts inside the timed region
         for i in range(args.e2e_steps):
             e2e_step(i)
-        for sl in range(2):
-            stream.wait_event(copies.last_output(sl))
+        plan.fence(wait_for_copies=True)
         e1.record(stream)
     e1.synchronize()
     assert int(err.item()) == 0, f"kernel error flag {int(err.item())}"

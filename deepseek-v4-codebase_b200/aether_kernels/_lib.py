@@ -122,6 +122,15 @@ SIGNATURES = {
          _p, _p, _p, _p, _p,                                  # h2d_stream, d2h_stream, ev_h2d, ev_comp, ev_d2h
          _p, ctypes.c_uint32],                                # slot_flags, seq
     ),
+    "aether_csa_decode_host_plan_create": (
+        _c_int,
+        [_p, _p, ctypes.c_size_t, _p, _p, _p, ctypes.c_size_t, _p,  # dev_in0/1, in_bytes, in_offsets, dev_out0/1, ...
+         _p, _p, _p, _c_int, _c_int, _c_int, _p, _p,              # slot_flags, idx/kv pages, stride, num_pages, max_nb, diags
+         _c_int, _c_int, _c_int, _c_int, _c_int, _p, _p, _c_int, _p],  # B, H, W, bits, top_k, workspace, err, pdl, plan_out
+    ),
+    "aether_csa_decode_host_plan_step": (_c_int, [_p, _p, _p, _p, _c_int, _p, _p, _c_f, _p]),
+    "aether_csa_decode_host_plan_fence": (_c_int, [_p, _p, _c_int]),
+    "aether_csa_decode_host_plan_destroy": (None, [_p]),
     "aether_hca_decode_paged": (
         _c_int,
         [

@@ -396,6 +396,87 @@ def csa_decode_paged_host(bufs: HostDecodeBuffers, host_in: torch.Tensor, host_o
               *((copies.h2d.cuda_stream, copies.d2h.cuda_stream, *[e.cuda_event for e in copies.events[slot]],
                  bufs.slot_flags.data_ptr(), bufs.seq) if copies is not None else (None,) * 6 + (0,)))
 
+class CsaDecodeHostPlan:
+    """A prepared host-buffer CSA decode (``aether_csa_decode_host_plan_*``):
+    two staging slots, copy streams, the cache and the launch shape are bound
+    once; each ``step`` enqueues one step's input copy from pinned host
+    memory, the decode and the output copy to pinned host memory with one
+    short C call, alternating the staging slots so a step's copies overlap its
+    neighbours' kernels.  Same results as ``csa_decode_paged_host``.
+    ``max_pages`` is the widest page table a step may pass.
+
+    ``overlap_prefetch`` as in ``csa_decode_paged``: only when no kernel
+    before a step on the stream writes the cache pages or the page table."""
+
+    def __init__(self, cache: TurboQuantPagedCache, batch: int, max_pages: int, heads: int = 12,
+                 top_k: int = 256, window: int = 128, err: Optional[torch.Tensor] = None,
+                 overlap_prefetch: bool = False, device="cuda"):
+        import ctypes
+        _check(cache.idx_pages is not None, "CSA decode needs a cache with an indexer stream")
+        self.device = torch.device(device)
+        self.slots = [HostDecodeBuffers(batch, heads, top_k, self.device) for _ in range(2)]
+        self.in_bytes, self.out_bytes = self.slots[0].in_bytes, self.slots[0].out_bytes
+        self.table_stride, self.window = max_pages, window
+        self._flags = torch.zeros(4, dtype=torch.int32, device=self.device)
+        self._ws = torch.zeros(csa_workspace_bytes(batch, max_pages * PAGE), dtype=torch.uint8, device=self.device)
+        self._diags = (rademacher_diag(INDEX_DIM, cache.seed, self.device),
+                       rademacher_diag(HEAD_DIM, cache.seed, self.device))
+        self._cache, self._err = cache, err
+        in_off = (ctypes.c_size_t * 5)(*self.slots[0].in_offsets)
+        out_off = (ctypes.c_size_t * 2)(*self.slots[0].out_offsets)
+        handle = ctypes.c_void_p()
+        a, b = self.slots
+        _lib.call("aether_csa_decode_host_plan_create", a.dev_in.data_ptr(), b.dev_in.data_ptr(), self.in_bytes,
+                  in_off, a.dev_out.data_ptr(), b.dev_out.data_ptr(), self.out_bytes, out_off,
+                  self._flags.data_ptr(), cache.idx_pages.data_ptr(), cache.kv_pages.data_ptr(), max_pages,
+                  cache.num_pages, max_pages * PAGE, self._diags[0].data_ptr(), self._diags[1].data_ptr(), batch,
+                  heads, window, cache.bits, top_k, self._ws.data_ptr(),
+                  _opt_ptr(err), int(overlap_prefetch), ctypes.byref(handle))
+        self._h = handle.value
+        lib = _lib.load()
+        self._step, self._fence, self._destroy = (lib.aether_csa_decode_host_plan_step,
+                                                  lib.aether_csa_decode_host_plan_fence,
+                                                  lib.aether_csa_decode_host_plan_destroy)
+
+    def pack_inputs(self, q, index_q, index_weight, window_len, nblocks) -> torch.Tensor:
+        """Pinned host buffer holding one step's inputs in the packed layout."""
+        return self.slots[0].pack_inputs(q, index_q, index_weight, window_len, nblocks)
+
+    def new_host_output(self) -> torch.Tensor:
+        return self.slots[0].new_host_output()
+
+    def unpack_outputs(self, host_out: torch.Tensor):
+        """(out [B, H, 128] bf16, indices [B, top_k] int32) views of a host result buffer."""
+        return self.slots[0].unpack_outputs(host_out)
+
+    def step(self, host_in: torch.Tensor, host_out: torch.Tensor, page_table: torch.Tensor, sink: torch.Tensor,
+             window: torch.Tensor, softmax_scale: float) -> None:
+        """Enqueue one step on the current stream: pinned ``host_in`` (from
+        ``pack_inputs``) in, results to pinned ``host_out`` once the plan's
+        copies are done (``fence(wait_for_copies=True)`` then synchronise)."""
+        _check(self._h is not None, "plan is closed")
+        _check(window.shape[:2] == (self.slots[0].batch, self.window), "window shape differs from the plan")
+        rc = self._step(self._h, host_in.data_ptr(), host_out.data_ptr(), page_table.data_ptr(), page_table.shape[1],
+                        sink.data_ptr(), window.data_ptr(), softmax_scale, _stream(self.device))
+        if rc != 0:
+            raise _lib.AetherKernelError(f"aether_csa_decode_host_plan_step failed ({rc}): {_lib.last_error()}")
+
+    def fence(self, wait_for_copies: bool) -> None:
+        """Order the plan's copy streams against the current stream (see the C entry)."""
+        _lib.call("aether_csa_decode_host_plan_fence", self._h, _stream(self.device), int(wait_for_copies))
+
+    def close(self) -> None:
+        if self._h is not None:
+            self._destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 def hca_decode_paged(
     q: torch.Tensor,
     sink: torch.Tensor,

@@ -1052,6 +1052,151 @@ int aether_csa_decode_paged_host(const void* host_in, void* dev_in, size_t in_by
   return 0;
 }
 
+// A prepared host-buffer decode: the staging slots, copy streams, events,
+// cache and launch shape bound once, so a step passes only what changes
+// between steps (its host buffers, the layer's page table, sink and window).
+// Steps alternate between the two staging slots.
+struct CsaHostPlan {
+  uint8_t* dev_in[2];
+  uint8_t* dev_out[2];
+  uint32_t* flags[2];
+  uint32_t seq[2];
+  cudaEvent_t ev[2][3];
+  cudaEvent_t fence;
+  cudaStream_t h2d, d2h;
+  size_t in_bytes, out_bytes, in_off[5], out_off[2];
+  const uint8_t* idx_pages;
+  const uint8_t* kv_pages;
+  int table_stride, num_pages;  // table_stride: the widest page table a step may pass
+  const float* diag_idx;
+  const float* diag_kv;
+  int B, H, W, bits, top_k, pdl, next;
+  uint32_t* workspace;
+  int* err;
+};
+
+static void destroy_host_plan(CsaHostPlan* p) {
+  if (!p) return;
+  if (p->h2d) cudaStreamSynchronize(p->h2d);
+  if (p->d2h) cudaStreamSynchronize(p->d2h);
+  for (auto& slot : p->ev)
+    for (cudaEvent_t e : slot)
+      if (e) cudaEventDestroy(e);
+  if (p->fence) cudaEventDestroy(p->fence);
+  if (p->h2d) cudaStreamDestroy(p->h2d);
+  if (p->d2h) cudaStreamDestroy(p->d2h);
+  delete p;
+}
+
+int aether_csa_decode_host_plan_create(void* dev_in0, void* dev_in1, size_t in_bytes, const size_t* in_offsets,
+                                       void* dev_out0, void* dev_out1, size_t out_bytes, const size_t* out_offsets,
+                                       uint32_t* slot_flags, const uint8_t* idx_pages, const uint8_t* kv_pages,
+                                       int table_stride, int num_pages, int max_nblocks, const float* diag_idx,
+                                       const float* diag_kv, int B, int H, int W, int bits, int top_k,
+                                       uint32_t* workspace, int* err, int pdl, void** plan_out) {
+  AETHER_REQUIRE(plan_out, "csa_decode_host_plan_create: null plan_out");
+  *plan_out = nullptr;
+  AETHER_REQUIRE(dev_in0 && dev_in1 && dev_out0 && dev_out1 && slot_flags && in_offsets && out_offsets,
+                 "csa_decode_host_plan_create: null staging buffer");
+  AETHER_REQUIRE(idx_pages && kv_pages && diag_idx && diag_kv && workspace,
+                 "csa_decode_host_plan_create: null cache, diagonal or workspace");
+  AETHER_REQUIRE(table_stride > 0 && max_nblocks == table_stride * kPage,
+                 "csa_decode_host_plan_create: max_nblocks must be table_stride * %d", kPage);
+  for (int i = 0; i < 5; ++i)
+    AETHER_REQUIRE(in_offsets[i] < in_bytes && in_offsets[i] % 16 == 0,
+                   "csa_decode_host_plan_create: input field %d offset out of range or unaligned", i);
+  for (int i = 0; i < 2; ++i)
+    AETHER_REQUIRE(out_offsets[i] < out_bytes && out_offsets[i] % 16 == 0,
+                   "csa_decode_host_plan_create: output field %d offset out of range or unaligned", i);
+  CsaHostPlan* p = new CsaHostPlan{};
+  p->dev_in[0] = static_cast<uint8_t*>(dev_in0);
+  p->dev_in[1] = static_cast<uint8_t*>(dev_in1);
+  p->dev_out[0] = static_cast<uint8_t*>(dev_out0);
+  p->dev_out[1] = static_cast<uint8_t*>(dev_out1);
+  p->flags[0] = slot_flags;
+  p->flags[1] = slot_flags + 2;
+  p->in_bytes = in_bytes;
+  p->out_bytes = out_bytes;
+  for (int i = 0; i < 5; ++i) p->in_off[i] = in_offsets[i];
+  for (int i = 0; i < 2; ++i) p->out_off[i] = out_offsets[i];
+  p->idx_pages = idx_pages;
+  p->kv_pages = kv_pages;
+  p->table_stride = table_stride;
+  p->num_pages = num_pages;
+  p->diag_idx = diag_idx;
+  p->diag_kv = diag_kv;
+  p->B = B;
+  p->H = H;
+  p->W = W;
+  p->bits = bits;
+  p->top_k = top_k;
+  p->workspace = workspace;
+  p->err = err;
+  p->pdl = pdl;
+  cudaError_t e = cudaStreamCreateWithFlags(&p->h2d, cudaStreamNonBlocking);
+  if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&p->d2h, cudaStreamNonBlocking);
+  for (auto& slot : p->ev)
+    for (cudaEvent_t& ev : slot)
+      if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&p->fence, cudaEventDisableTiming);
+  if (e != cudaSuccess) {
+    destroy_host_plan(p);
+    AETHER_CUDA_TRY(e, "csa_decode_host_plan_create: streams and events");
+  }
+  *plan_out = p;
+  return 0;
+}
+
+// One step of a prepared host-buffer decode (aether_csa_decode_paged_host
+// on the plan's next staging slot).  After a failed step the plan's slot
+// sequence is out of step with its flags: destroy the plan.
+int aether_csa_decode_host_plan_step(void* plan, const void* host_in, void* host_out, const int32_t* page_table,
+                                     int table_stride, const float* sink, const void* window, float softmax_scale,
+                                     void* stream) {
+  CsaHostPlan* p = static_cast<CsaHostPlan*>(plan);
+  AETHER_REQUIRE(p && host_in && host_out && page_table && sink && window,
+                 "csa_decode_host_plan_step: null argument");
+  AETHER_REQUIRE(table_stride > 0 && table_stride <= p->table_stride,
+                 "csa_decode_host_plan_step: page-table width %d outside (0, %d]", table_stride, p->table_stride);
+  const int s = p->next;
+  p->next ^= 1;
+  const uint32_t seq = ++p->seq[s];
+  uint8_t* in = p->dev_in[s];
+  uint8_t* out = p->dev_out[s];
+  return aether_csa_decode_paged_host(
+      host_in, in, p->in_bytes, host_out, out, p->out_bytes, in + p->in_off[0],
+      reinterpret_cast<const float*>(in + p->in_off[1]), reinterpret_cast<const float*>(in + p->in_off[2]), sink,
+      window, reinterpret_cast<const int32_t*>(in + p->in_off[3]), p->idx_pages, p->kv_pages, page_table,
+      table_stride, p->num_pages, reinterpret_cast<const int32_t*>(in + p->in_off[4]), table_stride * 64,
+      p->diag_idx, p->diag_kv, p->B, p->H, p->W, p->bits, p->top_k, softmax_scale, out + p->out_off[0],
+      reinterpret_cast<int32_t*>(out + p->out_off[1]), p->workspace, p->err, p->pdl, stream, p->h2d, p->d2h,
+      p->ev[s][0], p->ev[s][1], p->ev[s][2], p->flags[s], seq);
+}
+
+// Orders the plan's copy streams against `stream`: with wait_for_copies 0,
+// later copies start after the work enqueued on `stream` so far; with 1,
+// later work on `stream` starts after every copy enqueued by the plan so far.
+int aether_csa_decode_host_plan_fence(void* plan, void* stream, int wait_for_copies) {
+  CsaHostPlan* p = static_cast<CsaHostPlan*>(plan);
+  AETHER_REQUIRE(p, "csa_decode_host_plan_fence: null plan");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (wait_for_copies) {
+    AETHER_CUDA_TRY(cudaEventRecord(p->fence, p->h2d), "csa_decode_host_plan_fence: record");
+    AETHER_CUDA_TRY(cudaStreamWaitEvent(st, p->fence, 0), "csa_decode_host_plan_fence: wait");
+    AETHER_CUDA_TRY(cudaEventRecord(p->fence, p->d2h), "csa_decode_host_plan_fence: record");
+    AETHER_CUDA_TRY(cudaStreamWaitEvent(st, p->fence, 0), "csa_decode_host_plan_fence: wait");
+  } else {
+    AETHER_CUDA_TRY(cudaEventRecord(p->fence, st), "csa_decode_host_plan_fence: record");
+    AETHER_CUDA_TRY(cudaStreamWaitEvent(p->h2d, p->fence, 0), "csa_decode_host_plan_fence: wait");
+    AETHER_CUDA_TRY(cudaStreamWaitEvent(p->d2h, p->fence, 0), "csa_decode_host_plan_fence: wait");
+  }
+  return 0;
+}
+
+// Waits for the plan's copies and frees its streams and events (not the
+// caller's buffers).
+void aether_csa_decode_host_plan_destroy(void* plan) { destroy_host_plan(static_cast<CsaHostPlan*>(plan)); }
+
 int aether_hca_decode_paged(const void* q, const float* sink, const void* window, const int32_t* window_len,
                             const uint8_t* kv_pages, const int32_t* page_table,
                             int table_stride, int num_pages, const int32_t* nblocks, int max_nblocks,

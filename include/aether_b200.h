@@ -204,6 +204,35 @@ int aether_csa_decode_paged_host(const void* host_in, void* dev_in, size_t in_by
                                  void* d2h_stream, void* ev_h2d, void* ev_comp, void* ev_d2h, uint32_t* slot_flags,
                                  uint32_t seq);
 
+/* A prepared host-buffer CSA decode.  create binds what stays fixed across
+ * steps: two staging slots (dev_in0/1 and dev_out0/1, packed as
+ * aether_csa_decode_paged_host expects, with the device offsets of
+ * q / index_q / index_w / window_len / nblocks in in_offsets[5] and of
+ * out / sel_out in out_offsets[2]), four zeroed device u32 copy-completion
+ * words (slot_flags), the cache, the launch shape, the workspace (sized for
+ * table_stride pages, the widest page table a step may pass) and the error
+ * word.  The plan owns two copy streams and six events.  Each step
+ * passes only its pinned host buffers, the layer's page table, sink and
+ * window, the scale and the decode stream, and uses the next staging slot
+ * (alternating), so a step's copies overlap its neighbours' kernels.  The
+ * per-step host cost is one short call instead of the 45-argument entry.
+ * destroy waits for the plan's copies.  After a failed step, destroy the
+ * plan. */
+int aether_csa_decode_host_plan_create(void* dev_in0, void* dev_in1, size_t in_bytes, const size_t* in_offsets,
+                                       void* dev_out0, void* dev_out1, size_t out_bytes, const size_t* out_offsets,
+                                       uint32_t* slot_flags, const uint8_t* idx_pages, const uint8_t* kv_pages,
+                                       int table_stride, int num_pages, int max_nblocks, const float* diag_idx,
+                                       const float* diag_kv, int B, int H, int W, int bits, int top_k,
+                                       uint32_t* workspace, int* err, int pdl, void** plan_out);
+int aether_csa_decode_host_plan_step(void* plan, const void* host_in, void* host_out, const int32_t* page_table,
+                                     int table_stride, const float* sink, const void* window, float softmax_scale,
+                                     void* stream);
+/* Orders the plan's copy streams against `stream`: wait_for_copies 0 makes
+ * later copies start after the work enqueued on `stream` so far, 1 makes later
+ * work on `stream` start after every copy the plan has enqueued so far. */
+int aether_csa_decode_host_plan_fence(void* plan, void* stream, int wait_for_copies);
+void aether_csa_decode_host_plan_destroy(void* plan);
+
 /* One HCA decode step (replaces aether_2b/serving.py:507-522): attention over
  * every visible compressed block plus the window; nblocks <= 1024. */
 int aether_hca_decode_paged(const void* q, const float* sink, const void* window, const int32_t* window_len,

@@ -416,6 +416,38 @@ def test_csa_decode_host_buffers_copy_streams(ak):
         assert torch.equal(o, refs[i % 3][0].cpu()), i
 
 
+def test_csa_decode_host_plan(ak):
+    """The prepared host-buffer plan (one short C call per step, alternating
+    staging slots): every step's host result equals the device-resident
+    path's; fences order the copies; no bounded wait runs out."""
+    from aether_kernels.paged import CsaDecodeHostPlan, csa_decode_paged
+    from aether_kernels.synthetic import make_decode_batch
+
+    batches = [make_decode_batch("csa", 8, 3000, 20000, 4, 4, seed=400 + k, device="cuda") for k in range(3)]
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    for overlap in (False, True):
+        for b in batches:
+            ref = csa_decode_paged(b.q, b.index_q, b.index_weight, b.sink, b.window, b.window_len, b.cache,
+                                   b.page_table, b.nblocks, b.softmax_scale)
+            plan = CsaDecodeHostPlan(b.cache, 8, b.page_table.shape[1], window=b.window.shape[1], err=err,
+                                     overlap_prefetch=overlap)
+            hin = plan.pack_inputs(b.q, b.index_q, b.index_weight, b.window_len, b.nblocks)
+            houts = [plan.new_host_output() for _ in range(5)]
+            plan.fence(wait_for_copies=False)
+            for i in range(5):
+                plan.step(hin, houts[i], b.page_table, b.sink, b.window, b.softmax_scale)
+            plan.fence(wait_for_copies=True)
+            torch.cuda.synchronize()
+            for i in range(5):
+                o, s = plan.unpack_outputs(houts[i])
+                assert torch.equal(s, ref[1].cpu()), (overlap, i)
+                assert torch.equal(o, ref[0].cpu()), (overlap, i)
+            plan.close()
+    assert int(err.item()) == 0
+    with pytest.raises(RuntimeError):
+        plan.step(hin, houts[0], batches[0].page_table, batches[0].sink, batches[0].window, 1.0)
+
+
 def test_csa_decode_host_slot_wait_runs_out(ak):
     """A copy-completion word that never reaches its target: the attend
     kernel's bounded poll gives up (about 0.1 s), sets the wait-timeout bit and
