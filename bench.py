@@ -622,7 +622,7 @@ def run_hca(args):
     def step(i):
         s = sets[i % nsets]
         hca_decode_paged(s.q, s.sink, s.window, s.window_len, cache, s.page_table, s.nblocks, s.softmax_scale,
-                         out=outs[i % nsets], err=err)
+                         out=outs[i % nsets], err=err, overlap_prefetch=args.pdl)
 
     stream = torch.cuda.Stream(dev)
     with torch.cuda.stream(stream):

@@ -139,7 +139,7 @@ SIGNATURES = {
             _p, _c_int, _c_int, _p, _c_int,    # page_table, stride, num_pages, nblocks, max_nblocks
             _p,                                # diag_kv
             _c_int, _c_int, _c_int, _c_int, _c_f,  # B, H, W, bits, scale
-            _p, _p, _c_int, _p,                # out, err, cluster, stream
+            _p, _p, _c_int, _c_int, _p,        # out, err, cluster, pdl, stream
         ],
     ),
 }

@@ -489,9 +489,17 @@ def hca_decode_paged(
     out: Optional[torch.Tensor] = None,
     err: Optional[torch.Tensor] = None,
     cluster: int = 0,
+    overlap_prefetch: bool = False,
 ) -> torch.Tensor:
     """One fused HCA decode step: attention over every visible compressed
-    block plus the sliding window (aether_2b/serving.py:507-522)."""
+    block plus the sliding window (aether_2b/serving.py:507-522).
+
+    ``cluster`` 0 (default) runs a 4-CTA cluster per sequence; 4 or 8 the
+    older single-kernel cluster path.  ``overlap_prefetch=True`` (cluster 0)
+    launches with programmatic dependent launch: before waiting for the
+    previous kernel on the stream the kernel reads ``page_table``,
+    ``nblocks``, ``window_len``, the cache pages and every window row except
+    the newest; use it only when that kernel writes none of those."""
     B, H, D = q.shape
     _check(D == HEAD_DIM, f"head_dim must be {HEAD_DIM}")
     for t, nm in ((q, "q"), (sink, "sink"), (window, "window"), (window_len, "window_len"),
@@ -508,6 +516,6 @@ def hca_decode_paged(
         page_table.data_ptr(), page_table.shape[1], cache.num_pages, nblocks.data_ptr(),
         page_table.shape[1] * PAGE, rademacher_diag(HEAD_DIM, cache.seed, dev).data_ptr(),
         B, H, window.shape[1], cache.bits, float(softmax_scale), out.data_ptr(), _opt_ptr(err), int(cluster),
-        _stream(dev),
+        int(overlap_prefetch), _stream(dev),
     )
     return out

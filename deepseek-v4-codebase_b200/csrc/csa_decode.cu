@@ -49,6 +49,10 @@ namespace cg = cooperative_groups;
 
 namespace aether {
 
+// profiling aid: the phase-timestamp buffer set by
+// aether_csa_decode_set_debug_timer (null when off)
+long long* cta_debug_buffer();
+
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
 constexpr int kRowH = kHeadDim + 8;  // fp16 row stride (halves) of MMA operand tiles: 272 B, conflict-free ldmatrix
@@ -116,6 +120,7 @@ struct CsaParams {
   int32_t* sel_out;             // [B, top_k] or null
   float* score_out;             // [B, score_stride] index scores, or null
   int score_stride;
+  long long* dbg;  // per-CTA phase timestamps [grid][16] (profiling aid), or null
   int* err;
   int table_stride, num_pages, H, W, top_k;
   float softmax_scale;
@@ -162,6 +167,10 @@ __global__ void __launch_bounds__(kThreads) csa_decode_kernel(CsaParams p) {
   const int b = blockIdx.x / CS;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, t = lane & 3;
+  auto stamp = [&](int slot) {  // SM clock cycles (phase durations)
+    if (p.dbg && tid == 0) p.dbg[blockIdx.x * 16 + slot] = clock64();
+  };
+  stamp(0);
 
   uint32_t* scores = reinterpret_cast<uint32_t*>(smem + C::OFF_SCORES);
   __nv_bfloat16* winraw = reinterpret_cast<__nv_bfloat16*>(smem + C::OFF_WIN);
@@ -541,6 +550,7 @@ __global__ void __launch_bounds__(kThreads) csa_decode_kernel(CsaParams p) {
     for (int i = tid; i < own_cnt; i += kThreads) sel[i] = r * selp + i;
     cl.sync();  // all CTAs running before remote stores in the merge
   }
+  stamp(1);
 
   // =============================================== attention (this slice)
   __half* Kc = reinterpret_cast<__half*>(smem + C::A_KC);
@@ -609,6 +619,7 @@ __global__ void __launch_bounds__(kThreads) csa_decode_kernel(CsaParams p) {
     *reinterpret_cast<uint2*>(qr) =
         make_uint2(pack_half2(v[0] * cn, v[1] * cn), pack_half2(v[2] * cn, v[3] * cn));
   }
+  stamp(2);
   // window rows -> fp16 tiles (rows beyond wcnt zero-filled to the tile edge)
   const int ntw = (wcnt + 15) / 16;
   if (wcnt > 0) mbar_wait(&bars[C::STAGES], 0, p.err);
@@ -627,6 +638,7 @@ __global__ void __launch_bounds__(kThreads) csa_decode_kernel(CsaParams p) {
   }
   cp_async_commit_wait_all();
   __syncthreads();
+  stamp(3);
   // codes -> exact fp16 integers
   const int ntc = (own_cnt + 15) / 16;
   for (int i = tid; i < ntc * 16 * (kHeadDim / 8); i += kThreads) {
@@ -658,6 +670,7 @@ __global__ void __launch_bounds__(kThreads) csa_decode_kernel(CsaParams p) {
   }
   __syncthreads();
 
+  stamp(4);
   // ---- S = Q K^T per 16-source tile (compressed tiles first, then window)
   const int ncols_c = ntc * 16;
   const int ncols = ncols_c + ntw * 16;
@@ -694,6 +707,7 @@ __global__ void __launch_bounds__(kThreads) csa_decode_kernel(CsaParams p) {
   }
   __syncthreads();
 
+  stamp(5);
   // ---- per-head max / exp / sum over this CTA's sources
   for (int h = warp; h < kMaxHeads; h += kWarps) {
     float m = -INFINITY;
@@ -736,6 +750,7 @@ __global__ void __launch_bounds__(kThreads) csa_decode_kernel(CsaParams p) {
     }
   }
 
+  stamp(6);
   // ---- push partials to the owner CTA of each head
   const int hpc = (p.H + CS - 1) / CS;
 #pragma unroll
@@ -757,6 +772,7 @@ __global__ void __launch_bounds__(kThreads) csa_decode_kernel(CsaParams p) {
     }
   }
   cl.sync();
+  stamp(7);
 
   // ---- owner: log-sum-exp merge with the sink, inverse WHT, bf16 store
   for (int lh = warp; lh < hpc; lh += kWarps) {
@@ -810,6 +826,7 @@ __global__ void __launch_bounds__(kThreads) csa_decode_kernel(CsaParams p) {
     *reinterpret_cast<uint2*>(dst) =
         make_uint2(*reinterpret_cast<uint32_t*>(&o01), *reinterpret_cast<uint32_t*>(&o23));
   }
+  stamp(8);
 }
 
 template <int BITS, int CS, bool HCA>
@@ -903,6 +920,7 @@ static int csa_common(bool hca, const void* q, const float* index_q, const float
   p.H = H;
   p.W = W;
   p.top_k = hca ? 0 : top_k;
+  p.dbg = cta_debug_buffer();
   p.softmax_scale = softmax_scale;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   int rc = hca ? dispatch_csa<true>(p, B, bits, cs, st) : dispatch_csa<false>(p, B, bits, cs, st);
@@ -910,6 +928,10 @@ static int csa_common(bool hca, const void* q, const float* index_q, const float
   return check_launch(hca ? "hca_decode_paged" : "csa_decode_paged");
 }
 
+int hca_decode_cta(const void* q, const float* sink, const void* window, const int32_t* window_len,
+                   const uint8_t* kv_pages, const int32_t* page_table, int table_stride, int num_pages,
+                   const int32_t* nblocks, int max_nblocks, const float* diag_kv, int B, int H, int W, int bits,
+                   float softmax_scale, void* out, int* err, int pdl, void* stream);
 int csa_decode_cta(const void* q, const float* index_q, const float* index_w, const float* sink, const void* window,
                    const int32_t* window_len, const uint8_t* idx_pages, const uint8_t* kv_pages,
                    const int32_t* page_table, int table_stride, int num_pages, const int32_t* nblocks,
@@ -1201,7 +1223,10 @@ int aether_hca_decode_paged(const void* q, const float* sink, const void* window
                             const uint8_t* kv_pages, const int32_t* page_table,
                             int table_stride, int num_pages, const int32_t* nblocks, int max_nblocks,
                             const float* diag_kv, int B, int H, int W, int bits, float softmax_scale, void* out,
-                            int* err, int cluster, void* stream) {
+                            int* err, int cluster, int pdl, void* stream) {
+  if (cluster <= 0)
+    return hca_decode_cta(q, sink, window, window_len, kv_pages, page_table, table_stride, num_pages, nblocks,
+                          max_nblocks, diag_kv, B, H, W, bits, softmax_scale, out, err, pdl, stream);
   return csa_common(true, q, nullptr, nullptr, sink, window, window_len, nullptr, kv_pages,
                     page_table, table_stride, num_pages, nblocks, max_nblocks, nullptr, diag_kv, B, H, W, bits, 0,
                     softmax_scale, out, nullptr, err, cluster, stream);

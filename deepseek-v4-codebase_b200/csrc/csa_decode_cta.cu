@@ -1089,6 +1089,348 @@ __global__ void __launch_bounds__(kQThreads, CS > 1 ? AETHER_ATTEND_MINB : 1) cs
   stamp(10, tid == 0);
 }
 
+// ======================================================================
+// HCA decode (modeling.py:384-410, serving.py:507-522): every visible
+// compressed block plus the sliding window, no selection.  A 4-CTA cluster
+// per sequence; CTA r attends blocks [256 r, 256 r + 256) (four whole pages)
+// and window rows [w0, w0 + 32).  Everything that is cache state -- the page
+// table, the pages (one bulk copy each), their fp16 expansion and every
+// window row but the newest -- is staged before griddepcontrol.wait, so under
+// programmatic dependent launch it overlaps the previous kernel; after the
+// wait only the query-dependent work runs: rotated query, S = Q K^T, softmax,
+// O = P V, and the DSMEM merge of the four partials with the sink.
+constexpr int kHcaCS = 4;
+constexpr int kHcaRows = 256;                   // compressed rows per CTA
+constexpr int kHcaPages = kHcaRows / kPage;     // 4
+constexpr int kHcaMaxBlocks = kHcaCS * kHcaRows;  // 1024 (131072 tokens at compression 128)
+
+template <int BITS>
+struct HCfg {
+  static constexpr int RB_KV = kHeadDim * BITS / 8;
+  static constexpr int PB_KV = page_bytes(RB_KV);
+  static constexpr int KROW = kHeadDim + 8;                 // fp16 operand row stride (halves)
+  static constexpr int WSL = kWinMax / kHcaCS;              // window rows per CTA (max)
+  static constexpr int LST = kHcaRows + WSL;                // logit row stride (floats)
+  static constexpr int PST = kHcaRows + WSL + 8;            // P row stride (halves)
+  static constexpr int HPC = kMaxHeads / kHcaCS;            // heads finalised per CTA (max)
+  static constexpr int SLOT = 4 + 2 * kHeadDim;             // merge slot: m, l, pad, pad, O_rot, O_win
+  static constexpr int A_KC = 0;                            // f16 [256][KROW] expanded codes
+  static constexpr int A_KS = A_KC + kHcaRows * KROW * 2;   // fp32 [256] row scales
+  static constexpr int A_QR = A_KS + kHcaRows * 4;          // f16 [16][KROW] rotated q
+  static constexpr int A_QW = A_QR + 16 * KROW * 2;         // bf16 [16][KROW] plain q
+  // the staged pages are dead once expanded: logits and P reuse their space
+  static constexpr int A_RAW = A_QW + 16 * KROW * 2;        // [4] pages
+  static constexpr int A_LOG = A_RAW;                       // fp32 [16][LST]
+  static constexpr int A_P = A_LOG + 16 * LST * 4;          // f16 [16][PST]
+  static constexpr int RAW_END = A_RAW + kHcaPages * PB_KV;
+  static constexpr int P_END = A_P + 16 * PST * 2;
+  static constexpr int OFF_WIN = ((RAW_END > P_END ? RAW_END : P_END) + 127) & ~127;  // bf16 [WSL][kWRow]
+  static constexpr int OFF_MERGE = OFF_WIN + WSL * kWRow;   // fp32 [CS][HPC][SLOT]
+  static constexpr int OFF_MISC = OFF_MERGE + kHcaCS * HPC * SLOT * 4;  // m_h[16], l_h[16]
+  static constexpr int OFF_LUT = OFF_MISC + 2 * kMaxHeads * 4;          // u32 [256]: code byte -> half2
+  static constexpr int OFF_BAR = OFF_LUT + 256 * 4;
+  static constexpr int SMEM = OFF_BAR + 16;
+  static_assert(A_RAW % 128 == 0 && PB_KV % 16 == 0, "bulk-copy destinations are 16-byte aligned");
+  static_assert(SMEM <= 227 * 1024, "fits one CTA per SM");
+};
+
+struct HcaParams {
+  const __nv_bfloat16* q;       // [B, H, 128]
+  const float* sink;            // [H]
+  const __nv_bfloat16* window;  // [B, W, 128]
+  const int32_t* window_len;    // [B]
+  const uint8_t* kv_pages;      // [P][64 x 128*bits/8 codes | 64 x fp32 scales]
+  const int32_t* page_table;    // [B, table_stride]
+  const int32_t* nblocks;       // [B]
+  const float* diag_kv;         // [128] +-1
+  __nv_bfloat16* out;           // [B, H, 128]
+  long long* dbg;
+  int* err;
+  int table_stride, num_pages, H, W;
+  float softmax_scale;
+};
+
+template <int BITS>
+__global__ void __launch_bounds__(kQThreads, 1) hca_attend_kernel(HcaParams p) {
+  using C = HCfg<BITS>;
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int r = blockIdx.x % kHcaCS, b = blockIdx.x / kHcaCS;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int g = lane >> 2, t = lane & 3;
+  auto stamp = [&](int slot) {  // SM clock cycles (phase durations)
+    if (p.dbg && tid == 0) p.dbg[blockIdx.x * 16 + slot] = clock64();
+  };
+  stamp(0);
+  pdl_launch_dependents();
+  // announce this CTA is running; the wait comes before the first remote store
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+
+  __half* Kc = reinterpret_cast<__half*>(smem + C::A_KC);
+  float* ks = reinterpret_cast<float*>(smem + C::A_KS);
+  __half* Qr = reinterpret_cast<__half*>(smem + C::A_QR);
+  __nv_bfloat16* Qw = reinterpret_cast<__nv_bfloat16*>(smem + C::A_QW);
+  uint8_t* raw = smem + C::A_RAW;
+  float* logit = reinterpret_cast<float*>(smem + C::A_LOG);
+  __half* P = reinterpret_cast<__half*>(smem + C::A_P);
+  uint8_t* winb = smem + C::OFF_WIN;
+  float* merge = reinterpret_cast<float*>(smem + C::OFF_MERGE);
+  float* m_h = reinterpret_cast<float*>(smem + C::OFF_MISC);
+  float* l_h = m_h + kMaxHeads;
+  uint32_t* lut = reinterpret_cast<uint32_t*>(smem + C::OFF_LUT);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+
+  // ------------------------------------------- prologue: cache state only
+  int nb = p.nblocks[b];
+  if (nb > kHcaMaxBlocks || nb > p.table_stride * kPage) {
+    if (tid == 0) report_error(p.err, kErrBadShape);
+    nb = min(kHcaMaxBlocks, p.table_stride * kPage);
+  }
+  nb = max(nb, 0);
+  const int kc = max(0, min(nb - r * kHcaRows, kHcaRows));  // this CTA's compressed rows
+  const int npg = (kc + kPage - 1) / kPage;
+  const int W = p.W;
+  const int wl = max(0, min(p.window_len[b], W));
+  const int wsl = (W + kHcaCS - 1) / kHcaCS;
+  const int w0 = r * wsl;
+  const int wn = max(0, min(wl - w0, wsl));  // this CTA's window rows
+  const int ntc = (kc + 15) / 16, ntw = (wn + 15) / 16;
+  if (tid == 0) {
+    mbar_init(bar, 1);
+    fence_mbar_init();
+  }
+  if (BITS == 4 && tid < 256) lut[tid] = nib_byte_to_h2(static_cast<uint32_t>(tid));
+  __syncthreads();
+  if (warp == 0 && npg > 0) {
+    if (lane == 0) mbar_expect_tx(bar, npg * C::PB_KV);
+    __syncwarp();
+    if (lane < npg) {
+      int phys = p.page_table[static_cast<long long>(b) * p.table_stride + r * kHcaPages + lane];
+      if (phys < 0 || phys >= p.num_pages) {
+        report_error(p.err, kErrBadPage);
+        phys = 0;
+      }
+      bulk_g2s(raw + lane * C::PB_KV, p.kv_pages + static_cast<long long>(phys) * C::PB_KV, C::PB_KV, bar);
+    }
+  }
+  // window rows other than the newest are cache state
+  const long long wbase = static_cast<long long>(b) * W;
+  {
+    const int pre = max(0, min(wn, wl - 1 - w0));
+    const __nv_bfloat16* wsrc = p.window + (wbase + w0) * kHeadDim;
+    for (int i = tid; i < pre * 16; i += kQThreads)
+      cp_async16(winb + (i >> 4) * kWRow + (i & 15) * 16, wsrc + (i >> 4) * kHeadDim + (i & 15) * 8);
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  }
+  // zero window rows past wn up to the tile edge
+  for (int i = tid; i < (ntw * 16 - wn) * 16; i += kQThreads)
+    *reinterpret_cast<uint4*>(winb + (wn + (i >> 4)) * kWRow + (i & 15) * 16) = make_uint4(0, 0, 0, 0);
+  stamp(1);
+  if (npg > 0) mbar_wait(bar, 0, p.err);
+  // codes -> exact fp16 rows, scales -> ks (rows past kc zero to the tile edge)
+  for (int i = tid; i < ntc * 16 * 16; i += kQThreads) {
+    const int row = i >> 4, c8 = (i & 15) * 8;
+    uint4 o = make_uint4(0, 0, 0, 0);
+    const uint8_t* pg = raw + (row >> 6) * C::PB_KV;
+    if (row < kc) {
+      if (BITS == 4) {
+        const uint32_t w = *reinterpret_cast<const uint32_t*>(pg + (row & 63) * C::RB_KV + c8 / 2);
+        o = make_uint4(lut[w & 0xFFu], lut[(w >> 8) & 0xFFu], lut[(w >> 16) & 0xFFu], lut[w >> 24]);
+      } else {
+        const uint2 w = *reinterpret_cast<const uint2*>(pg + (row & 63) * C::RB_KV + c8);
+        o = make_uint4(s8pair_to_h2(w.x & 0xFFFFu), s8pair_to_h2(w.x >> 16), s8pair_to_h2(w.y & 0xFFFFu),
+                       s8pair_to_h2(w.y >> 16));
+      }
+    }
+    if ((i & 15) == 0)
+      ks[row] = row < kc ? *reinterpret_cast<const float*>(pg + kPage * C::RB_KV + (row & 63) * 4) : 0.f;
+    *reinterpret_cast<uint4*>(Kc + row * C::KROW + c8) = o;
+  }
+  stamp(2);
+
+  // ------------------------------------------- query-dependent work
+  pdl_wait();
+  stamp(3);
+  {
+    const int h = warp;  // 16 warps, 16 padded heads
+    float v[4];
+    if (h < p.H) {
+      const uint2 r4 = *reinterpret_cast<const uint2*>(p.q + (static_cast<long long>(b) * p.H + h) * kHeadDim + lane * 4);
+      *reinterpret_cast<uint2*>(Qw + h * C::KROW + lane * 4) = r4;
+      const __nv_bfloat162* bb = reinterpret_cast<const __nv_bfloat162*>(&r4);
+      const float2 f0 = __bfloat1622float2(bb[0]), f1 = __bfloat1622float2(bb[1]);
+      v[0] = f0.x; v[1] = f0.y; v[2] = f1.x; v[3] = f1.y;
+    } else {
+      *reinterpret_cast<uint2*>(Qw + h * C::KROW + lane * 4) = make_uint2(0, 0);
+      v[0] = v[1] = v[2] = v[3] = 0.f;
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) v[k] *= p.diag_kv[lane * 4 + k];
+    warp_wht128(v, lane);
+    const float cn = 0.0883883461356163f;
+    *reinterpret_cast<uint2*>(Qr + h * C::KROW + lane * 4) =
+        make_uint2(pack_half2(v[0] * cn, v[1] * cn), pack_half2(v[2] * cn, v[3] * cn));
+  }
+  // the newest window row (written by the previous kernel)
+  if (wl > 0 && wl - 1 >= w0 && wl - 1 < w0 + wn && tid < 16)
+    cp_async16(winb + (wl - 1 - w0) * kWRow + tid * 16, p.window + (wbase + wl - 1) * kHeadDim + tid * 8);
+  cp_async_commit_wait_all();
+  __syncthreads();
+  stamp(4);
+
+  // ---- S = Q K^T, one 16-source tile per warp iteration
+  for (int tile = warp; tile < ntc + ntw; tile += kQWarps) {
+    const bool comp = tile < ntc;
+    float acc[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
+    float acc2[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
+    if (comp) {
+      const __half* Kt = Kc + tile * 16 * C::KROW;
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        uint32_t a[4], b0, b1, b2, b3;
+        ldsm_x4(a[0], a[1], a[2], a[3], Qr + (lane & 15) * C::KROW + kk * 16 + (lane >> 4) * 8);
+        ldsm_x4(b0, b1, b2, b3, Kt + ((lane & 7) + ((lane >> 4) << 3)) * C::KROW + kk * 16 + ((lane >> 3) & 1) * 8);
+        mma_f16((kk & 1) ? acc2[0] : acc[0], a, b0, b1);
+        mma_f16((kk & 1) ? acc2[1] : acc[1], a, b2, b3);
+      }
+    } else {
+      const uint8_t* wt = winb + (tile - ntc) * 16 * kWRow;
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        uint32_t a[4], b0, b1, b2, b3;
+        ldsm_x4(a[0], a[1], a[2], a[3], Qw + (lane & 15) * C::KROW + kk * 16 + (lane >> 4) * 8);
+        ldsm_x4(b0, b1, b2, b3, wt + ((lane & 7) + ((lane >> 4) << 3)) * kWRow + (kk * 16 + ((lane >> 3) & 1) * 8) * 2);
+        mma_bf16((kk & 1) ? acc2[0] : acc[0], a, b0, b1);
+        mma_bf16((kk & 1) ? acc2[1] : acc[1], a, b2, b3);
+      }
+    }
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; e += 2) {
+        const int h = g + (e >> 1) * 8;
+        const int src = tile * 16 + nt * 8 + 2 * t;
+        float z0 = acc[nt][e] + acc2[nt][e], z1 = acc[nt][e + 1] + acc2[nt][e + 1];
+        if (comp) {
+          z0 = src < kc ? z0 * ks[src] * p.softmax_scale : -INFINITY;
+          z1 = src + 1 < kc ? z1 * ks[src + 1] * p.softmax_scale : -INFINITY;
+        } else {
+          z0 = (src - ntc * 16) < wn ? z0 * p.softmax_scale : -INFINITY;
+          z1 = (src + 1 - ntc * 16) < wn ? z1 * p.softmax_scale : -INFINITY;
+        }
+        *reinterpret_cast<float2*>(logit + h * C::LST + src) = make_float2(z0, z1);
+      }
+  }
+  __syncthreads();
+  stamp(5);
+  // ---- softmax statistics, one warp per head, 4 columns per lane step
+  const int ncols = (ntc + ntw) * 16, ncc = ntc * 16;
+  if (warp >= p.H) {
+    for (int c = lane * 4; c < ncols; c += 128) *reinterpret_cast<uint2*>(P + warp * C::PST + c) = make_uint2(0, 0);
+  } else {
+    const int h = warp;
+    float m = -INFINITY;
+    for (int c = lane * 4; c < ncols; c += 128) {
+      const float4 z = *reinterpret_cast<const float4*>(logit + h * C::LST + c);
+      m = fmaxf(m, fmaxf(fmaxf(z.x, z.y), fmaxf(z.z, z.w)));
+    }
+    m = warp_max(m);
+    const float mu = m == -INFINITY ? 0.f : m;
+    float l = 0.f;
+    for (int c = lane * 4; c < ncols; c += 128) {
+      const float4 z = *reinterpret_cast<const float4*>(logit + h * C::LST + c);
+      const float e0 = __expf(z.x - mu), e1 = __expf(z.y - mu), e2 = __expf(z.z - mu), e3 = __expf(z.w - mu);
+      l += (e0 + e1) + (e2 + e3);
+      float4 w = make_float4(e0, e1, e2, e3);
+      if (c < ncc) {  // compressed columns carry the per-entry scale into P
+        const float4 s4 = *reinterpret_cast<const float4*>(ks + c);
+        w = make_float4(e0 * s4.x, e1 * s4.y, e2 * s4.z, e3 * s4.w);
+      }
+      *reinterpret_cast<uint2*>(P + h * C::PST + c) = make_uint2(pack_half2(w.x, w.y), pack_half2(w.z, w.w));
+    }
+    l = warp_sum(l);
+    if (lane == 0) {
+      m_h[h] = m;
+      l_h[h] = l;
+    }
+  }
+  __syncthreads();
+  stamp(6);
+  // ---- O = P V; warp w owns output dims [8w, 8w+8); partials go to the
+  // head's owner CTA, which merges them
+  const int hpc = (p.H + kHcaCS - 1) / kHcaCS;
+  {
+    float orot[4] = {0, 0, 0, 0}, owin[4] = {0, 0, 0, 0};
+    for (int kt = 0; kt < ntc; ++kt) {
+      uint32_t a[4], b0, b1;
+      ldsm_x4(a[0], a[1], a[2], a[3], P + (lane & 15) * C::PST + kt * 16 + (lane >> 4) * 8);
+      asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0,%1}, [%2];"
+                   : "=r"(b0), "=r"(b1)
+                   : "r"(smem_u32(Kc + (kt * 16 + (lane & 7) + ((lane >> 3) & 1) * 8) * C::KROW + warp * 8)));
+      mma_f16(orot, a, b0, b1);
+    }
+    for (int kt = ntc; kt < ntc + ntw; ++kt) {
+      uint32_t a[4], b0, b1;
+      ldsm_x4(a[0], a[1], a[2], a[3], P + (lane & 15) * C::PST + kt * 16 + (lane >> 4) * 8);
+      const uint8_t* wt = winb + (kt - ntc) * 16 * kWRow;
+      asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0,%1}, [%2];"
+                   : "=r"(b0), "=r"(b1)
+                   : "r"(smem_u32(wt + ((lane & 7) + ((lane >> 3) & 1) * 8) * kWRow + warp * 16)));
+      mma_f16(owin, a, bf2_to_h2(b0), bf2_to_h2(b1));
+    }
+    asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
+#pragma unroll
+    for (int e = 0; e < 4; e += 2) {
+      const int h = g + (e >> 1) * 8;
+      if (h < p.H) {
+        const int owner = h / hpc, lh = h % hpc;
+        float* slot = cg::this_cluster().map_shared_rank(merge + (r * C::HPC + lh) * C::SLOT, owner);
+        const int dd = warp * 8 + 2 * t;
+        *reinterpret_cast<float2*>(slot + 4 + dd) = make_float2(orot[e], orot[e + 1]);
+        *reinterpret_cast<float2*>(slot + 4 + kHeadDim + dd) = make_float2(owin[e], owin[e + 1]);
+      }
+    }
+  }
+  if (warp == 0 && lane < p.H) {
+    const int h = lane, owner = h / hpc, lh = h % hpc;
+    float* slot = cg::this_cluster().map_shared_rank(merge + (r * C::HPC + lh) * C::SLOT, owner);
+    slot[0] = m_h[h];
+    slot[1] = l_h[h];
+  }
+  cg::this_cluster().sync();
+  stamp(7);
+  // ---- owner: merge the four partials of its heads with the sink, inverse
+  // rotation of the compressed part, bf16 store
+  for (int lh = warp; lh < hpc; lh += kQWarps) {
+    const int h = r * hpc + lh;
+    if (h >= p.H) break;
+    const float sk = p.sink[h];
+    float M = sk;
+#pragma unroll
+    for (int rr = 0; rr < kHcaCS; ++rr) M = fmaxf(M, merge[(rr * C::HPC + lh) * C::SLOT]);
+    float L = __expf(sk - M), vr[4] = {0, 0, 0, 0}, vw[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int rr = 0; rr < kHcaCS; ++rr) {
+      const float* slot = merge + (rr * C::HPC + lh) * C::SLOT;
+      const float m = slot[0];
+      const float a = m == -INFINITY ? 0.f : __expf(m - M);
+      L += a * slot[1];
+      const float4 o1 = *reinterpret_cast<const float4*>(slot + 4 + lane * 4);
+      const float4 o2 = *reinterpret_cast<const float4*>(slot + 4 + kHeadDim + lane * 4);
+      vr[0] += a * o1.x; vr[1] += a * o1.y; vr[2] += a * o1.z; vr[3] += a * o1.w;
+      vw[0] += a * o2.x; vw[1] += a * o2.y; vw[2] += a * o2.z; vw[3] += a * o2.w;
+    }
+    warp_wht128(vr, lane);
+    const float inv = 1.f / L;
+    float o[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) o[k] = (vr[k] * 0.0883883461356163f * p.diag_kv[lane * 4 + k] + vw[k]) * inv;
+    __nv_bfloat162 o01 = __floats2bfloat162_rn(o[0], o[1]), o23 = __floats2bfloat162_rn(o[2], o[3]);
+    *reinterpret_cast<uint2*>(p.out + (static_cast<long long>(b) * p.H + h) * kHeadDim + lane * 4) =
+        make_uint2(*reinterpret_cast<uint32_t*>(&o01), *reinterpret_cast<uint32_t*>(&o23));
+  }
+  stamp(8);
+}
+
 #ifndef AETHER_ATTEND_CLUSTER
 #define AETHER_ATTEND_CLUSTER 2
 #endif
@@ -1167,6 +1509,7 @@ static int launch_attend(const QParams& p, int B, bool pdl, cudaStream_t st) {
 }
 
 static long long* g_cta_debug = nullptr;
+long long* cta_debug_buffer() { return g_cta_debug; }
 
 // workspace layout: u32 keys [B][ws_stride], then candidate keys / ids
 // [B][chunks * kMaxTopK] each (only for sequences longer than 8192 blocks)
@@ -1257,6 +1600,65 @@ static int run_decode(QParams p, int B, int max_nblocks, bool pdl, cudaStream_t 
   pa.cand_stride = chunks * ps.sel_stride;
   pa.score_out = nullptr;
   return launch_attend<BITS>(pa, B, true, st);
+}
+
+// HCA decode with the 4-CTA cluster kernel; pdl: programmatic dependent launch.
+int hca_decode_cta(const void* q, const float* sink, const void* window, const int32_t* window_len,
+                   const uint8_t* kv_pages, const int32_t* page_table, int table_stride, int num_pages,
+                   const int32_t* nblocks, int max_nblocks, const float* diag_kv, int B, int H, int W, int bits,
+                   float softmax_scale, void* out, int* err, int pdl, void* stream) {
+  AETHER_REQUIRE(bits == 4 || bits == 8, "bits must be 4 or 8, got %d", bits);
+  AETHER_REQUIRE(H >= 1 && H <= kMaxHeads, "num_heads must be in [1, %d], got %d", kMaxHeads, H);
+  AETHER_REQUIRE(W >= 0 && W <= kWinMax, "window capacity must be in [0, %d], got %d", kWinMax, W);
+  AETHER_REQUIRE(B >= 0, "batch must be non-negative");
+  AETHER_REQUIRE(table_stride >= 1 && num_pages >= 1, "page table / pool must be non-empty");
+  AETHER_REQUIRE(max_nblocks <= kHcaMaxBlocks, "hca decode: %d visible blocks exceed the limit %d", max_nblocks,
+                 kHcaMaxBlocks);
+  AETHER_REQUIRE(q && sink && window && window_len && kv_pages && page_table && nblocks && diag_kv && out,
+                 "hca decode: null argument");
+  if (B == 0) return 0;
+  HcaParams p{};
+  p.q = static_cast<const __nv_bfloat16*>(q);
+  p.sink = sink;
+  p.window = static_cast<const __nv_bfloat16*>(window);
+  p.window_len = window_len;
+  p.kv_pages = kv_pages;
+  p.page_table = page_table;
+  p.nblocks = nblocks;
+  p.diag_kv = diag_kv;
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.dbg = g_cta_debug;
+  p.err = err;
+  p.table_stride = table_stride;
+  p.num_pages = num_pages;
+  p.H = H;
+  p.W = W;
+  p.softmax_scale = softmax_scale;
+  const int smem = bits == 4 ? HCfg<4>::SMEM : HCfg<8>::SMEM;
+  auto kern = bits == 4 ? hca_attend_kernel<4> : hca_attend_kernel<8>;
+  static bool attr4 = false, attr8 = false;
+  bool& attr = bits == 4 ? attr4 : attr8;
+  if (!attr) {
+    AETHER_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
+                    "hca decode: set shared memory size");
+    attr = true;
+  }
+  cudaLaunchAttribute at[2];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = kHcaCS;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[1].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t c = {};
+  c.gridDim = dim3(B * kHcaCS);
+  c.blockDim = dim3(kQThreads);
+  c.dynamicSmemBytes = smem;
+  c.stream = static_cast<cudaStream_t>(stream);
+  c.attrs = at;
+  c.numAttrs = pdl ? 2 : 1;
+  AETHER_CUDA_TRY(cudaLaunchKernelEx(&c, kern, p), "hca decode: launch");
+  return check_launch("hca_decode_paged");
 }
 
 int csa_decode_cta(const void* q, const float* index_q, const float* index_w, const float* sink, const void* window,

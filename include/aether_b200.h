@@ -234,11 +234,17 @@ int aether_csa_decode_host_plan_fence(void* plan, void* stream, int wait_for_cop
 void aether_csa_decode_host_plan_destroy(void* plan);
 
 /* One HCA decode step (replaces aether_2b/serving.py:507-522): attention over
- * every visible compressed block plus the window; nblocks <= 1024. */
+ * every visible compressed block plus the window; nblocks <= 1024.
+ * cluster 0: a 4-CTA cluster per sequence that stages the pages, their fp16
+ * expansion and all window rows but the newest before waiting on the previous
+ * kernel when pdl is set (programmatic dependent launch: only when that
+ * kernel writes none of them); 4 or 8: the older one-kernel cluster path
+ * (pdl ignored). */
 int aether_hca_decode_paged(const void* q, const float* sink, const void* window, const int32_t* window_len,
                             const uint8_t* kv_pages, const int32_t* page_table, int table_stride, int num_pages,
                             const int32_t* nblocks, int max_nblocks, const float* diag_kv, int B, int H, int W,
-                            int bits, float softmax_scale, void* out, int* err, int cluster, void* stream);
+                            int bits, float softmax_scale, void* out, int* err, int cluster, int pdl,
+                            void* stream);
 
 /* ------------------------------------------ context-parallel decode
  * New design (the reference has no multi-GPU attention): a

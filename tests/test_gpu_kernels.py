@@ -263,15 +263,50 @@ def test_csa_decode_exact_ties(ak):
 
 
 @pytest.mark.parametrize("bits", [4, 8])
-def test_hca_decode(ak, bits):
-    """BASELINE config 2 shapes (HCA, 131072 tokens -> 1024 blocks, YaRN 4) at batch 6."""
+@pytest.mark.parametrize("cluster", [0, 8])
+def test_hca_decode(ak, bits, cluster):
+    """BASELINE config 2 shapes (HCA, 131072 tokens -> 1024 blocks, YaRN 4) at
+    batch 6: the 4-CTA cluster kernel (cluster 0) and the older 8-CTA one."""
     from aether_kernels.rope import RopeConfig
     from aether_kernels.synthetic import make_decode_batch
 
     batch = make_decode_batch("hca", 6, 60000, 131072, bits, 128, seed=5, device="cuda",
                               rope=RopeConfig.yarn(4.0))
+    out, _ = _run_decode(ak, batch, cluster=cluster)
+    _check_decode(batch, out, None)
+
+
+@pytest.mark.parametrize("bits", [4, 8])
+@pytest.mark.parametrize("window", [128, 20])
+def test_hca_decode_ragged(ak, bits, window):
+    """Ragged contexts from empty to the 1024-block maximum, a block count
+    that is not a page multiple, short and empty windows."""
+    from aether_kernels.synthetic import make_decode_batch
+
+    batch = make_decode_batch("hca", 9, 0, 131072, bits, 128, window=window, seed=21 + bits + window,
+                              device="cuda")
+    batch.nblocks[2] = 0
+    batch.nblocks[3] = 1024 if batch.page_table.shape[1] * 64 >= 1024 else batch.nblocks[3]
+    batch.nblocks[4] = min(int(batch.nblocks[4]), 1000)
+    batch.window_len[5] = 0
+    batch.window_len[6] = 1
     out, _ = _run_decode(ak, batch)
     _check_decode(batch, out, None)
+
+
+def test_hca_decode_overlap_prefetch(ak):
+    """Back-to-back HCA launches with programmatic dependent launch give the
+    same bits as plain launches."""
+    from aether_kernels.paged import hca_decode_paged
+    from aether_kernels.synthetic import make_decode_batch
+
+    bs = [make_decode_batch("hca", 8, 20000, 131072, 4, 128, seed=60 + i, device="cuda") for i in range(3)]
+    plain = [_run_decode(ak, b)[0] for b in bs]
+    outs = [hca_decode_paged(b.q, b.sink, b.window, b.window_len, b.cache, b.page_table, b.nblocks,
+                             b.softmax_scale, overlap_prefetch=True) for b in bs for _ in range(2)]
+    torch.cuda.synchronize()
+    for i, o in enumerate(outs):
+        assert torch.equal(o, plain[i // 2])
 
 
 def test_csa_decode_overlap_prefetch(ak):
