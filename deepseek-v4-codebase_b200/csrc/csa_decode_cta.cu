@@ -1128,8 +1128,8 @@ struct HCfg {
   static constexpr int OFF_MERGE = OFF_WIN + WSL * kWRow;   // fp32 [CS][HPC][SLOT]
   static constexpr int OFF_MISC = OFF_MERGE + kHcaCS * HPC * SLOT * 4;  // m_h[16], l_h[16]
   static constexpr int OFF_LUT = OFF_MISC + 2 * kMaxHeads * 4;          // u32 [256]: code byte -> half2
-  static constexpr int OFF_BAR = OFF_LUT + 256 * 4;
-  static constexpr int SMEM = OFF_BAR + 16;
+  static constexpr int OFF_BAR = OFF_LUT + 256 * 4;        // u64 [4]: one per staged page
+  static constexpr int SMEM = OFF_BAR + 8 * kHcaPages;
   static_assert(A_RAW % 128 == 0 && PB_KV % 16 == 0, "bulk-copy destinations are 16-byte aligned");
   static_assert(SMEM <= 227 * 1024, "fits one CTA per SM");
 };
@@ -1180,7 +1180,13 @@ __global__ void __launch_bounds__(kQThreads, 1) hca_attend_kernel(HcaParams p) {
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
 
   // ------------------------------------------- prologue: cache state only
+  // independent loads first: block count, window length, this CTA's four
+  // page-table entries
+  const int32_t* ptab = p.page_table + static_cast<long long>(b) * p.table_stride + r * kHcaPages;
+  int phys = 0;
+  if (warp == 0 && lane < kHcaPages && r * kHcaPages + lane < p.table_stride) phys = ptab[lane];
   int nb = p.nblocks[b];
+  const int wl_raw = p.window_len[b];
   if (nb > kHcaMaxBlocks || nb > p.table_stride * kPage) {
     if (tid == 0) report_error(p.err, kErrBadShape);
     nb = min(kHcaMaxBlocks, p.table_stride * kPage);
@@ -1189,29 +1195,26 @@ __global__ void __launch_bounds__(kQThreads, 1) hca_attend_kernel(HcaParams p) {
   const int kc = max(0, min(nb - r * kHcaRows, kHcaRows));  // this CTA's compressed rows
   const int npg = (kc + kPage - 1) / kPage;
   const int W = p.W;
-  const int wl = max(0, min(p.window_len[b], W));
+  const int wl = max(0, min(wl_raw, W));
   const int wsl = (W + kHcaCS - 1) / kHcaCS;
   const int w0 = r * wsl;
   const int wn = max(0, min(wl - w0, wsl));  // this CTA's window rows
   const int ntc = (kc + 15) / 16, ntw = (wn + 15) / 16;
-  if (tid == 0) {
-    mbar_init(bar, 1);
+  // one mbarrier per page, initialised and armed by the issuing warp
+  if (warp == 0) {
+    if (lane < kHcaPages) mbar_init(bar + lane, 1);
     fence_mbar_init();
-  }
-  if (BITS == 4 && tid < 256) lut[tid] = nib_byte_to_h2(static_cast<uint32_t>(tid));
-  __syncthreads();
-  if (warp == 0 && npg > 0) {
-    if (lane == 0) mbar_expect_tx(bar, npg * C::PB_KV);
     __syncwarp();
     if (lane < npg) {
-      int phys = p.page_table[static_cast<long long>(b) * p.table_stride + r * kHcaPages + lane];
       if (phys < 0 || phys >= p.num_pages) {
         report_error(p.err, kErrBadPage);
         phys = 0;
       }
-      bulk_g2s(raw + lane * C::PB_KV, p.kv_pages + static_cast<long long>(phys) * C::PB_KV, C::PB_KV, bar);
+      mbar_expect_tx(bar + lane, C::PB_KV);
+      bulk_g2s(raw + lane * C::PB_KV, p.kv_pages + static_cast<long long>(phys) * C::PB_KV, C::PB_KV, bar + lane);
     }
   }
+  if (BITS == 4 && tid < 256) lut[tid] = nib_byte_to_h2(static_cast<uint32_t>(tid));
   // window rows other than the newest are cache state
   const long long wbase = static_cast<long long>(b) * W;
   {
@@ -1224,26 +1227,31 @@ __global__ void __launch_bounds__(kQThreads, 1) hca_attend_kernel(HcaParams p) {
   // zero window rows past wn up to the tile edge
   for (int i = tid; i < (ntw * 16 - wn) * 16; i += kQThreads)
     *reinterpret_cast<uint4*>(winb + (wn + (i >> 4)) * kWRow + (i & 15) * 16) = make_uint4(0, 0, 0, 0);
+  __syncthreads();  // barriers initialised, LUT written
   stamp(1);
-  if (npg > 0) mbar_wait(bar, 0, p.err);
-  // codes -> exact fp16 rows, scales -> ks (rows past kc zero to the tile edge)
-  for (int i = tid; i < ntc * 16 * 16; i += kQThreads) {
-    const int row = i >> 4, c8 = (i & 15) * 8;
-    uint4 o = make_uint4(0, 0, 0, 0);
-    const uint8_t* pg = raw + (row >> 6) * C::PB_KV;
-    if (row < kc) {
-      if (BITS == 4) {
-        const uint32_t w = *reinterpret_cast<const uint32_t*>(pg + (row & 63) * C::RB_KV + c8 / 2);
-        o = make_uint4(lut[w & 0xFFu], lut[(w >> 8) & 0xFFu], lut[(w >> 16) & 0xFFu], lut[w >> 24]);
-      } else {
-        const uint2 w = *reinterpret_cast<const uint2*>(pg + (row & 63) * C::RB_KV + c8);
-        o = make_uint4(s8pair_to_h2(w.x & 0xFFFFu), s8pair_to_h2(w.x >> 16), s8pair_to_h2(w.y & 0xFFFFu),
-                       s8pair_to_h2(w.y >> 16));
+  // codes -> exact fp16 rows, scales -> ks, page by page as each lands (rows
+  // past kc zero to the tile edge)
+  for (int pg = 0; pg * kPage < ntc * 16; ++pg) {
+    if (pg < npg) mbar_wait(bar + pg, 0, p.err);
+    const uint8_t* src = raw + pg * C::PB_KV;
+    for (int i = tid; i < kPage * 16; i += kQThreads) {
+      const int prow = i >> 4, row = pg * kPage + prow, c8 = (i & 15) * 8;
+      if (row >= ntc * 16) break;
+      uint4 o = make_uint4(0, 0, 0, 0);
+      if (row < kc) {
+        if (BITS == 4) {
+          const uint32_t w = *reinterpret_cast<const uint32_t*>(src + prow * C::RB_KV + c8 / 2);
+          o = make_uint4(lut[w & 0xFFu], lut[(w >> 8) & 0xFFu], lut[(w >> 16) & 0xFFu], lut[w >> 24]);
+        } else {
+          const uint2 w = *reinterpret_cast<const uint2*>(src + prow * C::RB_KV + c8);
+          o = make_uint4(s8pair_to_h2(w.x & 0xFFFFu), s8pair_to_h2(w.x >> 16), s8pair_to_h2(w.y & 0xFFFFu),
+                         s8pair_to_h2(w.y >> 16));
+        }
       }
+      if ((i & 15) == 0)
+        ks[row] = row < kc ? *reinterpret_cast<const float*>(src + kPage * C::RB_KV + prow * 4) : 0.f;
+      *reinterpret_cast<uint4*>(Kc + row * C::KROW + c8) = o;
     }
-    if ((i & 15) == 0)
-      ks[row] = row < kc ? *reinterpret_cast<const float*>(pg + kPage * C::RB_KV + (row & 63) * 4) : 0.f;
-    *reinterpret_cast<uint4*>(Kc + row * C::KROW + c8) = o;
   }
   stamp(2);
 
@@ -1277,7 +1285,12 @@ __global__ void __launch_bounds__(kQThreads, 1) hca_attend_kernel(HcaParams p) {
   __syncthreads();
   stamp(4);
 
-  // ---- S = Q K^T, one 16-source tile per warp iteration
+  // ---- S = Q K^T, one 16-source tile per warp iteration; the rotated
+  // query's A fragments stay in registers
+  uint32_t qa[8][4];
+#pragma unroll
+  for (int kk = 0; kk < 8; ++kk)
+    ldsm_x4(qa[kk][0], qa[kk][1], qa[kk][2], qa[kk][3], Qr + (lane & 15) * C::KROW + kk * 16 + (lane >> 4) * 8);
   for (int tile = warp; tile < ntc + ntw; tile += kQWarps) {
     const bool comp = tile < ntc;
     float acc[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
@@ -1286,11 +1299,10 @@ __global__ void __launch_bounds__(kQThreads, 1) hca_attend_kernel(HcaParams p) {
       const __half* Kt = Kc + tile * 16 * C::KROW;
 #pragma unroll
       for (int kk = 0; kk < 8; ++kk) {
-        uint32_t a[4], b0, b1, b2, b3;
-        ldsm_x4(a[0], a[1], a[2], a[3], Qr + (lane & 15) * C::KROW + kk * 16 + (lane >> 4) * 8);
+        uint32_t b0, b1, b2, b3;
         ldsm_x4(b0, b1, b2, b3, Kt + ((lane & 7) + ((lane >> 4) << 3)) * C::KROW + kk * 16 + ((lane >> 3) & 1) * 8);
-        mma_f16((kk & 1) ? acc2[0] : acc[0], a, b0, b1);
-        mma_f16((kk & 1) ? acc2[1] : acc[1], a, b2, b3);
+        mma_f16((kk & 1) ? acc2[0] : acc[0], qa[kk], b0, b1);
+        mma_f16((kk & 1) ? acc2[1] : acc[1], qa[kk], b2, b3);
       }
     } else {
       const uint8_t* wt = winb + (tile - ntc) * 16 * kWRow;
@@ -1359,15 +1371,18 @@ __global__ void __launch_bounds__(kQThreads, 1) hca_attend_kernel(HcaParams p) {
   // head's owner CTA, which merges them
   const int hpc = (p.H + kHcaCS - 1) / kHcaCS;
   {
-    float orot[4] = {0, 0, 0, 0}, owin[4] = {0, 0, 0, 0};
+    // two accumulator chains over the compressed tiles
+    float orot[4] = {0, 0, 0, 0}, orot2[4] = {0, 0, 0, 0}, owin[4] = {0, 0, 0, 0};
     for (int kt = 0; kt < ntc; ++kt) {
       uint32_t a[4], b0, b1;
       ldsm_x4(a[0], a[1], a[2], a[3], P + (lane & 15) * C::PST + kt * 16 + (lane >> 4) * 8);
       asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0,%1}, [%2];"
                    : "=r"(b0), "=r"(b1)
                    : "r"(smem_u32(Kc + (kt * 16 + (lane & 7) + ((lane >> 3) & 1) * 8) * C::KROW + warp * 8)));
-      mma_f16(orot, a, b0, b1);
+      mma_f16((kt & 1) ? orot2 : orot, a, b0, b1);
     }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) orot[e] += orot2[e];
     for (int kt = ntc; kt < ntc + ntw; ++kt) {
       uint32_t a[4], b0, b1;
       ldsm_x4(a[0], a[1], a[2], a[3], P + (lane & 15) * C::PST + kt * 16 + (lane >> 4) * 8);
