@@ -72,12 +72,13 @@ def read_peak():
     return FALLBACK_HBM_GBS, "fallback"
 
 
-def read_traffic():
-    """Per-launch DRAM bytes of the decode kernel from the committed ncu
-    summary (line 'traffic_bytes_per_launch: N'), or None."""
-    if not NCU_SUMMARY.exists():
+def read_traffic(summary=None):
+    """Per-launch DRAM bytes of a kernel from its committed ncu summary (line
+    'traffic_bytes_per_launch: N'; default: the CSA decode one), or None."""
+    summary = NCU_SUMMARY if summary is None else summary
+    if not summary.exists():
         return None
-    for line in NCU_SUMMARY.read_text().splitlines():
+    for line in summary.read_text().splitlines():
         if line.strip().startswith("traffic_bytes_per_launch:"):
             try:
                 return int(line.split(":", 1)[1].strip())
@@ -672,7 +673,8 @@ def run_hca(args):
                        "timing": "CUDA graph replay, CUDA events"},
             "gpu_launches": steps,
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(achieved / peak, 4), "peak_source": src, "traffic": None,
+                         "frac": round(achieved / peak, 4), "peak_source": src,
+                         "traffic": read_traffic(NCU_SUMMARY.parent / "hca_decode_4bit_b32_ncu.md"),
                          "algorithmic_bytes_per_launch": B * per_q},
             "clocks": clocks,
         }), flush=True)
