@@ -62,7 +62,9 @@ struct QCfg {
   static constexpr int KROW = kHeadDim + 8;                  // fp16 operand row stride (halves)
   static constexpr int SL = kMaxTopK / CS;                   // selected rows attended per CTA (max)
   static constexpr int WSL = kWinMax / CS;                   // window rows per CTA (max)
-  static constexpr int LST = SL + WSL;                       // logit row stride (floats)
+  // logit row stride (floats), = 8 mod 32: the per-head float2 stores of an
+  // MMA tile hit distinct banks
+  static constexpr int LST = SL + WSL + 8;
   static constexpr int PST = SL + WSL + 8;                   // P row stride (halves)
   static constexpr int HPC = (kMaxHeads + CS - 1) / CS;      // heads finalised per CTA (max)
   static constexpr int SLOT = 4 + 2 * kHeadDim;              // merge slot: m, l, pad, pad, O_rot, O_win
@@ -76,8 +78,7 @@ struct QCfg {
   static constexpr int A_QW = A_QR + 16 * KROW * 2;          // bf16 [16][KROW] plain q
   static constexpr int A_LOG = A_QW + 16 * KROW * 2;         // fp32 [16][LST]
   static constexpr int A_P = A_LOG + 16 * LST * 4;           // f16 [16][PST]
-  static constexpr int A_O = (A_P + 16 * PST * 2 + 15) & ~15;  // fp32 [2][16][128]
-  static constexpr int A_END = A_O + 2 * 16 * kHeadDim * 4;
+  static constexpr int A_END = A_P + 16 * PST * 2;
   // gathered code rows [SL][RAWS] share the logits / P / O area (dead by then)
   static constexpr int A_RAW = A_LOG;
   static_assert(A_RAW + SL * RAWS <= A_END, "raw rows fit the shared area");
@@ -85,8 +86,9 @@ struct QCfg {
 
   static constexpr int OFF_WIN = REGION;                     // bf16 [WSL][kWRow] this CTA's window rows
   static constexpr int OFF_MERGE = OFF_WIN + WSL * kWRow;    // fp32 [CS][HPC][SLOT]
-  static constexpr int OFF_PT = OFF_MERGE + CS * HPC * SLOT * 4;  // i32 [kMaxPagesLocal]
-  static constexpr int OFF_SEL = OFF_PT + kMaxPagesLocal * 4;  // i32 [256] positions
+  // page-table entries of this CTA's 8192-block chunk (implicit sources)
+  static constexpr int OFF_PT = OFF_MERGE + CS * HPC * SLOT * 4;  // i32 [kMaxKeys / kPage]
+  static constexpr int OFF_SEL = OFF_PT + kMaxKeys / kPage * 4;  // i32 [256] positions
   static constexpr int OFF_OWN = OFF_SEL + kMaxTopK * 4;     // i32 [256] local block ids attended
   static constexpr int OFF_SCAN = OFF_OWN + kMaxTopK * 4;    // u32 [64]
   static constexpr int OFF_MISC = OFF_SCAN + 64 * 4;
@@ -603,10 +605,13 @@ __global__ void __launch_bounds__(kQThreads, CS > 1 ? AETHER_ATTEND_MINB : 1) cs
   const int wsl = (W + CS - 1) / CS;               // window rows per CTA
   const int w0 = r * wsl;                           // this CTA's first window row
   const int wn = max(0, min(wl - w0, wsl));         // its valid window rows
-  if (!select_only) {
-    const int32_t* ptab = p.page_table + static_cast<long long>(p.q_row ? p.q_row[b] : b) * p.table_stride;
-    for (int i = tid; i < npages; i += kQThreads) {
-      int v = ptab[i];
+  // implicit sources lie in this CTA's chunk: stage its page-table entries;
+  // explicit candidate lists may name any block, read at the gather
+  const int32_t* ptab = p.page_table + static_cast<long long>(p.q_row ? p.q_row[b] : b) * p.table_stride;
+  const int pt0 = chunk * (kMaxKeys / kPage);
+  if (!select_only && !explicit_list) {
+    for (int i = tid; i < min(npages - pt0, kMaxKeys / kPage); i += kQThreads) {
+      int v = ptab[pt0 + i];
       if (v < 0 || v >= p.num_pages) {
         report_error(p.err, kErrBadPage);
         v = 0;
@@ -837,14 +842,23 @@ __global__ void __launch_bounds__(kQThreads, CS > 1 ? AETHER_ATTEND_MINB : 1) cs
   __nv_bfloat16* Qw = reinterpret_cast<__nv_bfloat16*>(smem + C::A_QW);
   float* logit = reinterpret_cast<float*>(smem + C::A_LOG);
   __half* P = reinterpret_cast<__half*>(smem + C::A_P);
-  float* Obuf = reinterpret_cast<float*>(smem + C::A_O);
   const int ntc = (kc + 15) / 16, ntw = (wn + 15) / 16;
   {
     constexpr int CPR = C::RB_KV / 16;
     for (int i = tid; i < kc * CPR; i += kQThreads) {
       const int row = i / CPR, ch = i % CPR;
       const int blk = min(max(own[s0 + row], 0), max(nb - 1, 0));
-      const uint8_t* pg = p.kv_pages + static_cast<long long>(pt[blk >> 6]) * C::PB_KV;
+      int phys;
+      if (explicit_list) {
+        phys = __ldg(ptab + (blk >> 6));
+        if (phys < 0 || phys >= p.num_pages) {
+          report_error(p.err, kErrBadPage);
+          phys = 0;
+        }
+      } else {
+        phys = pt[min(max((blk >> 6) - pt0, 0), kMaxKeys / kPage - 1)];
+      }
+      const uint8_t* pg = p.kv_pages + static_cast<long long>(phys) * C::PB_KV;
       cp_async16(raw + row * C::RAWS + ch * 16, pg + (blk & 63) * C::RB_KV + ch * 16);
       if (ch == 0) cp_async4(ks + row, pg + kPage * C::RB_KV + (blk & 63) * 4);
     }
@@ -1110,7 +1124,7 @@ struct HCfg {
   static constexpr int PB_KV = page_bytes(RB_KV);
   static constexpr int KROW = kHeadDim + 8;                 // fp16 operand row stride (halves)
   static constexpr int WSL = kWinMax / kHcaCS;              // window rows per CTA (max)
-  static constexpr int LST = kHcaRows + WSL;                // logit row stride (floats)
+  static constexpr int LST = kHcaRows + WSL + 8;            // logit row stride (floats), = 8 mod 32
   static constexpr int PST = kHcaRows + WSL + 8;            // P row stride (halves)
   static constexpr int HPC = kMaxHeads / kHcaCS;            // heads finalised per CTA (max)
   static constexpr int SLOT = 4 + 2 * kHeadDim;             // merge slot: m, l, pad, pad, O_rot, O_win
@@ -1451,6 +1465,25 @@ __global__ void __launch_bounds__(kQThreads, 1) hca_attend_kernel(HcaParams p) {
 #endif
 constexpr int kAttendCluster = AETHER_ATTEND_CLUSTER;  // CTAs per sequence in the attention phase
 
+// Dynamic shared memory that keeps a second attend CTA off an SM.  The
+// attend CTA needs ~99 KB, so two fit on one SM; when a launch's CTAs fit the
+// GPU one per SM (decode batches), requesting this much spreads them over all
+// SMs instead of pairing them on half of them, which halves each CTA's
+// latency-bound phases.  Larger launches (prefill) use the compact size.
+constexpr int kSpreadSmem = 116 * 1024;
+
+static int sm_count() {
+  static const int n = [] {
+    int dev = 0, v = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+      cudaGetLastError();
+      return 148;
+    }
+    return v;
+  }();
+  return n;
+}
+
 template <int BITS>
 static int set_smem_attrs() {
   static bool done = false;
@@ -1462,7 +1495,10 @@ static int set_smem_attrs() {
                                          QCfg<BITS, 1>::SMEM),
                     "csa_decode: set shared memory size (select)");
     AETHER_CUDA_TRY(cudaFuncSetAttribute(csa_attend_kernel<BITS, kAttendCluster>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, QCfg<BITS, kAttendCluster>::SMEM),
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         QCfg<BITS, kAttendCluster>::SMEM > kSpreadSmem
+                                             ? QCfg<BITS, kAttendCluster>::SMEM
+                                             : kSpreadSmem),
                     "csa_decode: set shared memory size (attend)");
     done = true;
   }
@@ -1517,7 +1553,10 @@ static int launch_attend(const QParams& p, int B, bool pdl, cudaStream_t st) {
     c.dynamicSmemBytes = QCfg<BITS, 1>::SMEM;
     AETHER_CUDA_TRY(cudaLaunchKernelEx(&c, csa_attend_kernel<BITS, 1>, p), "csa_decode: launch (select)");
   } else {
-    c.dynamicSmemBytes = QCfg<BITS, kAttendCluster>::SMEM;
+    const int grid = B * p.chunks * cs;
+    c.dynamicSmemBytes = grid <= sm_count() && QCfg<BITS, kAttendCluster>::SMEM < kSpreadSmem
+                             ? kSpreadSmem
+                             : QCfg<BITS, kAttendCluster>::SMEM;
     AETHER_CUDA_TRY(cudaLaunchKernelEx(&c, csa_attend_kernel<BITS, kAttendCluster>, p), "csa_decode: launch (attend)");
   }
   return 0;
