@@ -619,7 +619,11 @@ __global__ void __launch_bounds__(kQThreads, CS > 1 ? AETHER_ATTEND_MINB : 1) cs
       pt[i] = v;
     }
   }
-  for (int i = tid; i < kL1Bins / 4; i += kQThreads) reinterpret_cast<uint4*>(hist)[i] = make_uint4(0, 0, 0, 0);
+  // with at most top_k candidate positions every valid key is taken: no
+  // histogram (prefill's explicit top-k lists, short contexts)
+  const bool need_select = n > p.top_k;
+  if (need_select)
+    for (int i = tid; i < kL1Bins / 4; i += kQThreads) reinterpret_cast<uint4*>(hist)[i] = make_uint4(0, 0, 0, 0);
   if (tid < kMaxTopK) sel[tid] = 0;  // every slot holds a valid position
   if (tid == 0) {
     misc->thr = 0;
@@ -667,7 +671,7 @@ __global__ void __launch_bounds__(kQThreads, CS > 1 ? AETHER_ATTEND_MINB : 1) cs
     for (int j = 0; j < PER; ++j) {
       kr[j] = i0 + j < n ? kr[j] : 0u;  // key 0 = no block
       if (kr[j]) {
-        atomicAdd(&hist[kr[j] >> 19], 1u);
+        if (need_select) atomicAdd(&hist[kr[j] >> 19], 1u);
         ++cnt;
       }
     }
