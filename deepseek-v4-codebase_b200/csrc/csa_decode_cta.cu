@@ -816,20 +816,28 @@ __global__ void __launch_bounds__(kQThreads, CS > 1 ? AETHER_ATTEND_MINB : 1) cs
   // the selected blocks held on this device, as local ids (order kept)
   if (direct_own) {
     if (tid == 0) misc->nown = K;
-  } else if (warp == 0) {
-    uint32_t base = 0;
-    for (int r0 = 0; r0 < K; r0 += 32) {
-      const int i = r0 + lane;
-      int loc = -1;
-      if (i < K) {
-        const int gidv = gid_of(sel[i]);
-        if (gidv >= p.id_base && gidv < p.id_base + nb) loc = gidv - p.id_base;
-      }
-      const uint32_t bal = __ballot_sync(0xffffffffu, loc >= 0);
-      if (loc >= 0) own[base + __popc(bal & ((1u << lane) - 1))] = loc;
-      base += __popc(bal);
+  } else {
+    // thread i < K looks up winner i (all id loads in flight together); a
+    // ballot per warp and the per-warp counts keep the winners' order
+    int loc = -1;
+    if (tid < K) {
+      const int gidv = gid_of(sel[tid]);
+      if (gidv >= p.id_base && gidv < p.id_base + nb) loc = gidv - p.id_base;
     }
-    if (lane == 0) misc->nown = base;
+    const uint32_t bal = __ballot_sync(0xffffffffu, loc >= 0);
+    constexpr int kSelWarps = kMaxTopK / 32;
+    if (lane == 0 && warp < kSelWarps) wtot[warp] = __popc(bal);
+    __syncthreads();
+    if (warp < kSelWarps) {
+      uint32_t base = 0;
+      for (int w = 0; w < warp; ++w) base += wtot[w];
+      if (loc >= 0) own[base + __popc(bal & ((1u << lane) - 1))] = loc;
+      if (tid == 0) {
+        uint32_t tot = 0;
+        for (int w = 0; w < kSelWarps; ++w) tot += wtot[w];
+        misc->nown = tot;
+      }
+    }
   }
   __syncthreads();
   const int KO = static_cast<int>(misc->nown);
