@@ -649,193 +649,230 @@ __global__ void __launch_bounds__(kQThreads, CS > 1 ? AETHER_ATTEND_MINB : 1) cs
   // stores (the __syncthreads below orders the other threads)
   if (p.step_flags && tid == 0) flag_wait(p.step_flags + 1, p.step_seq - 1u, p.err);
   stamp(2, tid == 0);
-  constexpr int PER = kMaxKeys / kQThreads;  // 16 keys per thread, in source order
-  const int i0 = tid * PER;
-  uint32_t kr[PER];
-  {
-    const uint32_t* src = explicit_list ? p.cand_keys + static_cast<long long>(b) * p.cand_stride + i0
-                                        : p.ws + static_cast<long long>(b) * p.ws_stride + chunk * kMaxKeys + i0;
-#pragma unroll
-    for (int v = 0; v < PER / 4; ++v) {
-      uint4 x = make_uint4(0, 0, 0, 0);
-      if (i0 + 4 * v < n) x = __ldcg(reinterpret_cast<const uint4*>(src) + v);
-      kr[4 * v] = x.x; kr[4 * v + 1] = x.y; kr[4 * v + 2] = x.z; kr[4 * v + 3] = x.w;
+  // a short explicit list that needs no selection (prefill's top-k lists):
+  // one candidate per thread; the winners are the valid keys in list order
+  const bool few = explicit_list && !select_only && n <= kQThreads && n <= p.top_k;
+  if (few) {
+    const uint32_t* ck = p.cand_keys + static_cast<long long>(b) * p.cand_stride;
+    const int32_t* ci = p.cand_ids + static_cast<long long>(b) * p.cand_stride;
+    const uint32_t key = tid < n ? __ldcg(ck + tid) : 0u;
+    const int gid = tid < n ? __ldcg(ci + tid) : -1;
+    const bool valid = key != 0u;
+    const int loc = valid && gid >= p.id_base && gid < p.id_base + nb ? gid - p.id_base : -1;
+    const uint32_t bv = __ballot_sync(0xffffffffu, valid), bo = __ballot_sync(0xffffffffu, loc >= 0);
+    if (lane == 0) {
+      wtot[warp] = __popc(bv);
+      wtot[32 + warp] = __popc(bo);
     }
-  }
-  // the prologue's zero-fill of the histogram and of misc happens-before
-  // any update (the key loads above are already in flight)
-  __syncthreads();
-  {
-    uint32_t cnt = 0;
-#pragma unroll
-    for (int j = 0; j < PER; ++j) {
-      kr[j] = i0 + j < n ? kr[j] : 0u;  // key 0 = no block
-      if (kr[j]) {
-        if (need_select) atomicAdd(&hist[kr[j] >> 19], 1u);
-        ++cnt;
+    __syncthreads();
+    uint32_t pv = 0, po = 0, tv = 0, to = 0;
+    for (int w = 0; w < kQWarps; ++w) {
+      const uint32_t cv = wtot[w], co = wtot[32 + w];
+      if (w < warp) {
+        pv += cv;
+        po += co;
+      }
+      tv += cv;
+      to += co;
+    }
+    const uint32_t lt = (1u << lane) - 1u;
+    if (loc >= 0) own[po + __popc(bo & lt)] = loc;
+    if (p.sel_out && r == 0) {
+      int32_t* so = p.sel_out + static_cast<long long>(b) * p.top_k;
+      if (valid) so[pv + __popc(bv & lt)] = gid;
+      for (int i = static_cast<int>(tv) + tid; i < p.top_k; i += kQThreads) so[i] = -1;
+    }
+    if (tid == 0) misc->nown = to;
+    stamp(5, tid == 0);
+  } else {
+    constexpr int PER = kMaxKeys / kQThreads;  // 16 keys per thread, in source order
+    const int i0 = tid * PER;
+    uint32_t kr[PER];
+    {
+      const uint32_t* src = explicit_list ? p.cand_keys + static_cast<long long>(b) * p.cand_stride + i0
+                                          : p.ws + static_cast<long long>(b) * p.ws_stride + chunk * kMaxKeys + i0;
+  #pragma unroll
+      for (int v = 0; v < PER / 4; ++v) {
+        uint4 x = make_uint4(0, 0, 0, 0);
+        if (i0 + 4 * v < n) x = __ldcg(reinterpret_cast<const uint4*>(src) + v);
+        kr[4 * v] = x.x; kr[4 * v + 1] = x.y; kr[4 * v + 2] = x.z; kr[4 * v + 3] = x.w;
       }
     }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) cnt += __shfl_xor_sync(0xffffffffu, cnt, o);
-    if (lane == 0 && cnt) atomicAdd(&misc->nvalid, cnt);
-  }
-  __syncthreads();
-  stamp(3, tid == 0);
-  const int nvalid = static_cast<int>(misc->nvalid);
-  const int K = min(p.top_k, nvalid);
-  if (p.score_out && !explicit_list && r == 0) {
-    float* so = p.score_out + static_cast<long long>(b) * p.score_stride + chunk * kMaxKeys + i0;
-#pragma unroll
-    for (int j = 0; j < PER; ++j)
-      if (i0 + j < n) so[j] = __uint_as_float(kr[j] - 1u);
-  }
+    // the prologue's zero-fill of the histogram and of misc happens-before
+    // any update (the key loads above are already in flight)
+    __syncthreads();
+    {
+      uint32_t cnt = 0;
+  #pragma unroll
+      for (int j = 0; j < PER; ++j) {
+        kr[j] = i0 + j < n ? kr[j] : 0u;  // key 0 = no block
+        if (kr[j]) {
+          if (need_select) atomicAdd(&hist[kr[j] >> 19], 1u);
+          ++cnt;
+        }
+      }
+  #pragma unroll
+      for (int o = 16; o > 0; o >>= 1) cnt += __shfl_xor_sync(0xffffffffu, cnt, o);
+      if (lane == 0 && cnt) atomicAdd(&misc->nvalid, cnt);
+    }
+    __syncthreads();
+    stamp(3, tid == 0);
+    const int nvalid = static_cast<int>(misc->nvalid);
+    const int K = min(p.top_k, nvalid);
+    if (p.score_out && !explicit_list && r == 0) {
+      float* so = p.score_out + static_cast<long long>(b) * p.score_stride + chunk * kMaxKeys + i0;
+  #pragma unroll
+      for (int j = 0; j < PER; ++j)
+        if (i0 + j < n) so[j] = __uint_as_float(kr[j] - 1u);
+    }
 
-  // ------------------------------------------------------------- select
-  // Result: every key > thr is taken, and the take_eq lowest-position keys
-  // == thr.  Keys are >= 1 for real blocks, so thr = 0 takes all of them.
-  // After the bin b1 of the K-th largest key (bins of key >> 19) is known,
-  // later steps walk `wmask`, the bit set of this thread's keys in bins >= b1.
-  uint32_t wmask = 0;
-#pragma unroll
-  for (int j = 0; j < PER; ++j) wmask |= static_cast<uint32_t>(kr[j] != 0u) << j;
-  if (nvalid > K) {
-    find_bin(hist, kL1Bins, static_cast<uint32_t>(K), wtot, misc, tid, lane, warp);
-    const uint32_t b1 = misc->bin, ccnt = misc->cnt;
-    const uint32_t R = static_cast<uint32_t>(K) - misc->above;  // keys still to take from bin b1
-    wmask = 0;
-#pragma unroll
-    for (int j = 0; j < PER; ++j) wmask |= static_cast<uint32_t>(kr[j] != 0u && (kr[j] >> 19) >= b1) << j;
-    if (ccnt == R) {
-      if (tid == 0) misc->thr = b1 << 19;  // lowest key of bin b1: the whole bin is taken
-    } else if (ccnt <= static_cast<uint32_t>(kBoundMax)) {
-      // rank the keys of bin b1 exactly: (key desc, position asc)
-      uint2* cand = reinterpret_cast<uint2*>(hist + kL1Bins);
-      for (uint32_t m = wmask; m; m &= m - 1u) {
-        const int j = __ffs(m) - 1;
-        const uint32_t kj = pick16(kr, j);
-        if ((kj >> 19) == b1) cand[atomicAdd(&misc->ncand, 1u)] = make_uint2(kj, i0 + j);
-      }
-      __syncthreads();
-      for (int i = tid; i < static_cast<int>(ccnt); i += kQThreads) {
-        const uint2 me = cand[i];
-        uint32_t rank = 0, eq_before = 0;
-        for (int k2 = 0; k2 < static_cast<int>(ccnt); ++k2) {
-          const uint2 o = cand[k2];
-          rank += o.x > me.x || (o.x == me.x && o.y < me.y);
-          eq_before += o.x == me.x && o.y < me.y;
+    // ------------------------------------------------------------- select
+    // Result: every key > thr is taken, and the take_eq lowest-position keys
+    // == thr.  Keys are >= 1 for real blocks, so thr = 0 takes all of them.
+    // After the bin b1 of the K-th largest key (bins of key >> 19) is known,
+    // later steps walk `wmask`, the bit set of this thread's keys in bins >= b1.
+    uint32_t wmask = 0;
+  #pragma unroll
+    for (int j = 0; j < PER; ++j) wmask |= static_cast<uint32_t>(kr[j] != 0u) << j;
+    if (nvalid > K) {
+      find_bin(hist, kL1Bins, static_cast<uint32_t>(K), wtot, misc, tid, lane, warp);
+      const uint32_t b1 = misc->bin, ccnt = misc->cnt;
+      const uint32_t R = static_cast<uint32_t>(K) - misc->above;  // keys still to take from bin b1
+      wmask = 0;
+  #pragma unroll
+      for (int j = 0; j < PER; ++j) wmask |= static_cast<uint32_t>(kr[j] != 0u && (kr[j] >> 19) >= b1) << j;
+      if (ccnt == R) {
+        if (tid == 0) misc->thr = b1 << 19;  // lowest key of bin b1: the whole bin is taken
+      } else if (ccnt <= static_cast<uint32_t>(kBoundMax)) {
+        // rank the keys of bin b1 exactly: (key desc, position asc)
+        uint2* cand = reinterpret_cast<uint2*>(hist + kL1Bins);
+        for (uint32_t m = wmask; m; m &= m - 1u) {
+          const int j = __ffs(m) - 1;
+          const uint32_t kj = pick16(kr, j);
+          if ((kj >> 19) == b1) cand[atomicAdd(&misc->ncand, 1u)] = make_uint2(kj, i0 + j);
         }
-        if (rank == R - 1) {  // the last key taken
-          misc->thr = me.x;
-          misc->take_eq = eq_before + 1;
+        __syncthreads();
+        for (int i = tid; i < static_cast<int>(ccnt); i += kQThreads) {
+          const uint2 me = cand[i];
+          uint32_t rank = 0, eq_before = 0;
+          for (int k2 = 0; k2 < static_cast<int>(ccnt); ++k2) {
+            const uint2 o = cand[k2];
+            rank += o.x > me.x || (o.x == me.x && o.y < me.y);
+            eq_before += o.x == me.x && o.y < me.y;
+          }
+          if (rank == R - 1) {  // the last key taken
+            misc->thr = me.x;
+            misc->take_eq = eq_before + 1;
+          }
         }
-      }
-    } else {
-      // many keys share bin b1: two more radix levels over those keys
-      uint32_t R2 = R;
-      for (int i = tid; i < 2048; i += kQThreads) hist[i] = 0;
-      __syncthreads();
-      for (uint32_t m = wmask; m; m &= m - 1u) {
-        const uint32_t kj = pick16(kr, __ffs(m) - 1);
-        if ((kj >> 19) == b1) atomicAdd(&hist[(kj >> 8) & 2047u], 1u);
-      }
-      __syncthreads();
-      find_bin(hist, 2048, R2, wtot, misc, tid, lane, warp);
-      const uint32_t b2 = misc->bin;
-      R2 -= misc->above;
-      const uint32_t pfx = (b1 << 11) | b2;  // key >> 8
-      if (misc->cnt == R2) {
-        if (tid == 0) misc->thr = pfx << 8;  // the whole sub-bin is taken
       } else {
-        for (int i = tid; i < kQThreads; i += kQThreads) hist[i] = 0;
+        // many keys share bin b1: two more radix levels over those keys
+        uint32_t R2 = R;
+        for (int i = tid; i < 2048; i += kQThreads) hist[i] = 0;
         __syncthreads();
         for (uint32_t m = wmask; m; m &= m - 1u) {
           const uint32_t kj = pick16(kr, __ffs(m) - 1);
-          if ((kj >> 8) == pfx) atomicAdd(&hist[kj & 255u], 1u);
+          if ((kj >> 19) == b1) atomicAdd(&hist[(kj >> 8) & 2047u], 1u);
         }
         __syncthreads();
-        find_bin(hist, kQThreads, R2, wtot, misc, tid, lane, warp);  // 256 used bins of 512
+        find_bin(hist, 2048, R2, wtot, misc, tid, lane, warp);
+        const uint32_t b2 = misc->bin;
         R2 -= misc->above;
-        if (tid == 0) {
-          misc->thr = (pfx << 8) | static_cast<uint32_t>(misc->bin);
-          misc->take_eq = R2;  // keys equal to thr: the lowest-position R2 of them
+        const uint32_t pfx = (b1 << 11) | b2;  // key >> 8
+        if (misc->cnt == R2) {
+          if (tid == 0) misc->thr = pfx << 8;  // the whole sub-bin is taken
+        } else {
+          for (int i = tid; i < kQThreads; i += kQThreads) hist[i] = 0;
+          __syncthreads();
+          for (uint32_t m = wmask; m; m &= m - 1u) {
+            const uint32_t kj = pick16(kr, __ffs(m) - 1);
+            if ((kj >> 8) == pfx) atomicAdd(&hist[kj & 255u], 1u);
+          }
+          __syncthreads();
+          find_bin(hist, kQThreads, R2, wtot, misc, tid, lane, warp);  // 256 used bins of 512
+          R2 -= misc->above;
+          if (tid == 0) {
+            misc->thr = (pfx << 8) | static_cast<uint32_t>(misc->bin);
+            misc->take_eq = R2;  // keys equal to thr: the lowest-position R2 of them
+          }
         }
       }
     }
-  }
-  __syncthreads();
-  stamp(4, tid == 0);
-  // ordered compaction over wmask: thread order is source order.  On the
-  // implicit (single-device, in-order) source every winner is held here, so
-  // the attended list `own` is written directly.
-  const bool direct_own = !explicit_list && p.id_base == 0 && !select_only;
-  {
-    const uint32_t thr = misc->thr, take_eq = misc->take_eq;
-    uint32_t cs = 0, ce = 0;
-    for (uint32_t m = wmask; m; m &= m - 1u) {
-      const uint32_t kj = pick16(kr, __ffs(m) - 1);
-      cs += kj > thr;
-      ce += kj == thr;
-    }
-    const uint32_t packed = cs | (ce << 16);
-    const uint32_t exc = block_scan_incl(packed, wtot, lane, warp) - packed;
-    uint32_t sb = exc & 0xFFFFu, eb = exc >> 16;  // 16-bit fields: at most 8192 keys
-    for (uint32_t m = (cs | ce) ? wmask : 0u; m; m &= m - 1u) {
-      const int j = __ffs(m) - 1;
-      const uint32_t kj = pick16(kr, j);
-      const bool st = kj > thr, eq = kj == thr;
-      const uint32_t pos = st ? sb + min(eb, take_eq) : sb + eb;
-      if ((st || (eq && eb < take_eq)) && pos < static_cast<uint32_t>(K)) {
-        sel[pos] = i0 + j;
-        if (direct_own) own[pos] = chunk * kMaxKeys + i0 + j;
-      }
-      sb += st;
-      eb += eq;
-    }
-  }
-  __syncthreads();
-  stamp(5, tid == 0);
-  // global block id of a source position
-  const int32_t* cids = explicit_list ? p.cand_ids + static_cast<long long>(b) * p.cand_stride : nullptr;
-  auto gid_of = [&](int pos) -> int { return explicit_list ? cids[pos] : p.id_base + chunk * kMaxKeys + pos; };
-  if (select_only) {
-    if (r == 0) {
-      const uint32_t* kk = explicit_list ? p.cand_keys + static_cast<long long>(b) * p.cand_stride
-                                         : p.ws + static_cast<long long>(b) * p.ws_stride + chunk * kMaxKeys;
-      const long long o = static_cast<long long>(bc) * p.sel_stride;
-      for (int i = tid; i < p.sel_stride; i += kQThreads) {
-        p.sel_keys_out[o + i] = i < K ? __ldcg(kk + sel[i]) : 0u;
-        p.sel_ids_out[o + i] = i < K ? gid_of(sel[i]) : -1;
-      }
-    }
-    return;
-  }
-  if (p.sel_out && r == 0) {
-    int32_t* so = p.sel_out + static_cast<long long>(b) * p.top_k;
-    for (int i = tid; i < p.top_k; i += kQThreads) so[i] = i < K ? gid_of(sel[i]) : -1;
-  }
-  // the selected blocks held on this device, as local ids (order kept)
-  if (direct_own) {
-    if (tid == 0) misc->nown = K;
-  } else {
-    // thread i < K looks up winner i (all id loads in flight together); a
-    // ballot per warp and the per-warp counts keep the winners' order
-    int loc = -1;
-    if (tid < K) {
-      const int gidv = gid_of(sel[tid]);
-      if (gidv >= p.id_base && gidv < p.id_base + nb) loc = gidv - p.id_base;
-    }
-    const uint32_t bal = __ballot_sync(0xffffffffu, loc >= 0);
-    constexpr int kSelWarps = kMaxTopK / 32;
-    if (lane == 0 && warp < kSelWarps) wtot[warp] = __popc(bal);
     __syncthreads();
-    if (warp < kSelWarps) {
-      uint32_t base = 0;
-      for (int w = 0; w < warp; ++w) base += wtot[w];
-      if (loc >= 0) own[base + __popc(bal & ((1u << lane) - 1))] = loc;
-      if (tid == 0) {
-        uint32_t tot = 0;
-        for (int w = 0; w < kSelWarps; ++w) tot += wtot[w];
-        misc->nown = tot;
+    stamp(4, tid == 0);
+    // ordered compaction over wmask: thread order is source order.  On the
+    // implicit (single-device, in-order) source every winner is held here, so
+    // the attended list `own` is written directly.
+    const bool direct_own = !explicit_list && p.id_base == 0 && !select_only;
+    {
+      const uint32_t thr = misc->thr, take_eq = misc->take_eq;
+      uint32_t cs = 0, ce = 0;
+      for (uint32_t m = wmask; m; m &= m - 1u) {
+        const uint32_t kj = pick16(kr, __ffs(m) - 1);
+        cs += kj > thr;
+        ce += kj == thr;
+      }
+      const uint32_t packed = cs | (ce << 16);
+      const uint32_t exc = block_scan_incl(packed, wtot, lane, warp) - packed;
+      uint32_t sb = exc & 0xFFFFu, eb = exc >> 16;  // 16-bit fields: at most 8192 keys
+      for (uint32_t m = (cs | ce) ? wmask : 0u; m; m &= m - 1u) {
+        const int j = __ffs(m) - 1;
+        const uint32_t kj = pick16(kr, j);
+        const bool st = kj > thr, eq = kj == thr;
+        const uint32_t pos = st ? sb + min(eb, take_eq) : sb + eb;
+        if ((st || (eq && eb < take_eq)) && pos < static_cast<uint32_t>(K)) {
+          sel[pos] = i0 + j;
+          if (direct_own) own[pos] = chunk * kMaxKeys + i0 + j;
+        }
+        sb += st;
+        eb += eq;
+      }
+    }
+    __syncthreads();
+    stamp(5, tid == 0);
+    // global block id of a source position
+    const int32_t* cids = explicit_list ? p.cand_ids + static_cast<long long>(b) * p.cand_stride : nullptr;
+    auto gid_of = [&](int pos) -> int { return explicit_list ? cids[pos] : p.id_base + chunk * kMaxKeys + pos; };
+    if (select_only) {
+      if (r == 0) {
+        const uint32_t* kk = explicit_list ? p.cand_keys + static_cast<long long>(b) * p.cand_stride
+                                           : p.ws + static_cast<long long>(b) * p.ws_stride + chunk * kMaxKeys;
+        const long long o = static_cast<long long>(bc) * p.sel_stride;
+        for (int i = tid; i < p.sel_stride; i += kQThreads) {
+          p.sel_keys_out[o + i] = i < K ? __ldcg(kk + sel[i]) : 0u;
+          p.sel_ids_out[o + i] = i < K ? gid_of(sel[i]) : -1;
+        }
+      }
+      return;
+    }
+    if (p.sel_out && r == 0) {
+      int32_t* so = p.sel_out + static_cast<long long>(b) * p.top_k;
+      for (int i = tid; i < p.top_k; i += kQThreads) so[i] = i < K ? gid_of(sel[i]) : -1;
+    }
+    // the selected blocks held on this device, as local ids (order kept)
+    if (direct_own) {
+      if (tid == 0) misc->nown = K;
+    } else {
+      // thread i < K looks up winner i (all id loads in flight together); a
+      // ballot per warp and the per-warp counts keep the winners' order
+      int loc = -1;
+      if (tid < K) {
+        const int gidv = gid_of(sel[tid]);
+        if (gidv >= p.id_base && gidv < p.id_base + nb) loc = gidv - p.id_base;
+      }
+      const uint32_t bal = __ballot_sync(0xffffffffu, loc >= 0);
+      constexpr int kSelWarps = kMaxTopK / 32;
+      if (lane == 0 && warp < kSelWarps) wtot[warp] = __popc(bal);
+      __syncthreads();
+      if (warp < kSelWarps) {
+        uint32_t base = 0;
+        for (int w = 0; w < warp; ++w) base += wtot[w];
+        if (loc >= 0) own[base + __popc(bal & ((1u << lane) - 1))] = loc;
+        if (tid == 0) {
+          uint32_t tot = 0;
+          for (int w = 0; w < kSelWarps; ++w) tot += wtot[w];
+          misc->nown = tot;
+        }
       }
     }
   }

@@ -144,6 +144,7 @@ def test_prefill_chunk_attention_matches_oracle(lib, bits):
             k = sels[row].numel()
             got = ids[row, :k].long()
             assert ties[row] or torch.equal(got, sels[row]), f"row {row}: selection"
+            assert (ids[row, k:] == -1).all(), f"row {row}: unused index slots hold -1"
             wl = min(128, t + 1)
             w0 = first[ri] + i + (128 - wl)
             src = torch.cat([main[got], window[w0: w0 + wl].float()], dim=0)
