@@ -13,6 +13,7 @@ from typing import List, Optional
 
 PKG = Path(__file__).resolve().parent
 CSRC = PKG.parent / "csrc"
+INCLUDE = PKG.parent.parent / "include"  # aether_b200.h: the sources include it, so drift fails to compile
 SOURCES = ["capi.cu", "tq.cu", "compat.cu", "csa_decode.cu", "csa_decode_cta.cu", "csa_prefill.cu"]
 OUT = PKG / "libaether_b200.so"
 
@@ -49,7 +50,7 @@ def build(force: bool = False, verbose: bool = False, extra: Optional[List[str]]
     if nvcc is None:
         raise RuntimeError("nvcc was not found; cannot build the Aether sm_100a kernels")
     tmp = OUT.with_suffix(".so.tmp")
-    cmd = [nvcc, *NVCC_FLAGS, *(extra or []), "-o", str(tmp), *[str(CSRC / s) for s in SOURCES]]
+    cmd = [nvcc, *NVCC_FLAGS, "-I", str(INCLUDE), *(extra or []), "-o", str(tmp), *[str(CSRC / s) for s in SOURCES]]
     if verbose:
         print(" ".join(cmd))
     res = subprocess.run(cmd, capture_output=True, text=True)

@@ -1,6 +1,7 @@
 // Library-level C-ABI entry points: version, last error message, build info.
 #include <string.h>
 
+#include "aether_b200.h"
 #include "capi_util.cuh"
 
 namespace aether {

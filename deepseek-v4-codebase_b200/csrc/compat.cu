@@ -14,6 +14,7 @@
 // reference adds it once per source token), and the indexer uses the
 // canonical softplus/ReLU score with an exact, (score desc, index asc)
 // ordered top-k instead of a raw weighted dot with an unordered serial pick.
+#include "aether_b200.h"
 #include "capi_util.cuh"
 #include "common.cuh"
 

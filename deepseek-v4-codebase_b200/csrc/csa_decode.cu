@@ -42,6 +42,7 @@
 // and attends every visible block.
 #include <cooperative_groups.h>
 
+#include "aether_b200.h"
 #include "capi_util.cuh"
 #include "common.cuh"
 

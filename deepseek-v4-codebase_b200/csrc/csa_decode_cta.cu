@@ -36,6 +36,7 @@
 #include <cooperative_groups.h>
 #include <stdlib.h>
 
+#include "aether_b200.h"
 #include "capi_util.cuh"
 #include "common.cuh"
 

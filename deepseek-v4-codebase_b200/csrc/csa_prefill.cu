@@ -35,6 +35,7 @@
 // and raises T to that key; later keys equal to T lose the tie (they have
 // higher block indices).  At the end the exact top-k of the buffer is
 // written in ascending block order.
+#include "aether_b200.h"
 #include "capi_util.cuh"
 #include "common.cuh"
 

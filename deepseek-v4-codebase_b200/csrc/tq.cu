@@ -13,6 +13,7 @@
 // floating-point step uses the explicitly rounded intrinsics in the reference
 // op order (no contraction, IEEE division), so codes and scales are
 // bit-identical to the reference's fp32 torch path.
+#include "aether_b200.h"
 #include "capi_util.cuh"
 #include "common.cuh"
 

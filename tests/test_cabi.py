@@ -50,3 +50,33 @@ def test_invalid_argument_reports_error():
     rc = lib.aether_tq_encode(None, 0, 4, 96, 8, None, None, None, None, None)
     assert rc == 1
     assert "64 or 128" in _lib.last_error()
+
+
+def _prototypes():
+    """name -> (return type, parameter count) of every function the header declares."""
+    text = re.sub(r"/\*.*?\*/", " ", HEADER.read_text(), flags=re.S)
+    text = re.sub(r"//[^\n]*", " ", text)
+    out = {}
+    for ret, name, params in re.findall(r"([A-Za-z_][\w\s\*]*?)\s*\b(aether_\w+)\s*\(([^;{]*?)\)\s*;", text, flags=re.S):
+        params = " ".join(params.split())
+        n = 0 if params in ("", "void") else params.count(",") + 1
+        out[name] = (" ".join(ret.split()).split()[-1].rstrip("*") or ret, n)
+    return out
+
+
+def test_ctypes_table_matches_header_prototypes():
+    """Every ctypes signature has the header prototype's parameter count and
+    a void return exactly where the header returns void (the sources include
+    the header, so the definitions match it at compile time)."""
+    from aether_kernels import _lib
+
+    protos = _prototypes()
+    assert len(protos) == len(declared_functions())
+    bad = []
+    for name, (ret, n) in protos.items():
+        restype, argtypes = _lib.SIGNATURES[name]
+        if len(argtypes) != n:
+            bad.append(f"{name}: header {n} parameters, ctypes {len(argtypes)}")
+        if (ret == "void") != (restype is None):
+            bad.append(f"{name}: header returns {ret}, ctypes {restype}")
+    assert not bad, bad
