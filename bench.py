@@ -250,6 +250,9 @@ def cpu_baseline(steps: int, warmup: int, budget_s: float, full_line: bool = Fal
 
 # ------------------------------------------------------------------- main
 def main():
+    # rank 0's stdout carries exactly one JSON line: NCCL's own banner and
+    # debug lines (NCCL_DEBUG) go to stderr
+    os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=102400)
