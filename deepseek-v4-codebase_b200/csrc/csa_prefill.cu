@@ -42,6 +42,32 @@
 namespace aether {
 namespace prefill {
 
+// Tuning variant, off by default: pair two queries per packed fp32 FMA in
+// the epilogue (B rows ordered so a pair's columns are adjacent in TMEM).
+#ifndef AETHER_PF_PAIRED
+#define AETHER_PF_PAIRED 0
+#endif
+
+// packed fp32x2 helpers (sm_100 fma.rn.f32x2: per-lane IEEE fma)
+__device__ __forceinline__ uint64_t pack_f2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ uint64_t pack_u2(uint32_t lo, uint32_t hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(lo), "r"(hi));
+  return r;
+}
+__device__ __forceinline__ void unpack_f2(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t fma_f2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+
 constexpr int kThreads = 512;
 constexpr int kQ = 32;                  // query tokens per CTA
 constexpr int kTileKeys = 128;          // keys per MMA tile (M)
@@ -316,9 +342,15 @@ __global__ void __launch_bounds__(kThreads, 1) csa_prefill_index_kernel(Params p
       const int qint = valid ? __float2int_rn(__fdiv_rn(k ? x1 : x0, s)) : 0;
       const int a = (qint + 1024) >> 11, b = qint - a * 2048;
       const int d = 2 * lane + k;
-      const int n0 = (qi * kIdxHeads + h) * 2;
+#if AETHER_PF_PAIRED
+      // B row (query pair, head, limb, query & 1): the two queries of a pair
+      // sit in adjacent accumulator columns
+      const int n0 = ((qi >> 1) * kIdxHeads + h) * 4 + (qi & 1), nb = n0 + 2;
+#else
+      const int n0 = (qi * kIdxHeads + h) * 2, nb = n0 + 1;
+#endif
       *reinterpret_cast<__half*>(smem + C::OFF_B + canon(n0, d)) = __int2half_rn(a);
-      *reinterpret_cast<__half*>(smem + C::OFF_B + canon(n0 + 1, d)) = __int2half_rn(b);
+      *reinterpret_cast<__half*>(smem + C::OFF_B + canon(nb, d)) = __int2half_rn(b);
     }
     if (lane == 0) m->alpha[qi][h] = valid ? softplus_f(w) * s : 0.f;
   }
@@ -475,6 +507,30 @@ __global__ void __launch_bounds__(kThreads, 1) csa_prefill_index_kernel(Params p
               "=r"(v[57]), "=r"(v[58]), "=r"(v[59]), "=r"(v[60]), "=r"(v[61]), "=r"(v[62]), "=r"(v[63])
             : "r"(ta));
         asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#if AETHER_PF_PAIRED
+        // two queries per packed fp32 FMA; each lane rounds exactly as the
+        // scalar sequence below, so the keys are bit-identical
+#pragma unroll
+        for (int pp = 0; pp < 4; ++pp) {
+          const int qa = half * 16 + c2 * 8 + 2 * pp;
+          const float4 a0 = *reinterpret_cast<const float4*>(m->alpha[qa]);
+          const float4 a1 = *reinterpret_cast<const float4*>(m->alpha[qa + 1]);
+          const float al0[4] = {a0.x, a0.y, a0.z, a0.w}, al1[4] = {a1.x, a1.y, a1.z, a1.w};
+          uint64_t sc2 = pack_f2(0.f, 0.f);
+#pragma unroll
+          for (int h = 0; h < 4; ++h) {
+            const uint32_t* vv = v + pp * 16 + h * 4;
+            const uint64_t dot2 = fma_f2(pack_f2(2048.f, 2048.f), pack_u2(vv[0], vv[1]), pack_u2(vv[2], vv[3]));
+            float d0, d1;
+            unpack_f2(dot2, d0, d1);
+            sc2 = fma_f2(pack_f2(al0[h], al1[h]), pack_f2(fmaxf(d0, 0.f), fmaxf(d1, 0.f)), sc2);
+          }
+          float s0, s1;
+          unpack_f2(sc2, s0, s1);
+          xo[qa * kTileKeys + r] = __float_as_uint(__fmul_rn(s0, kscale)) + 1u;
+          xo[(qa + 1) * kTileKeys + r] = __float_as_uint(__fmul_rn(s1, kscale)) + 1u;
+        }
+#else
 #pragma unroll
         for (int qq = 0; qq < 8; ++qq) {
           const int qi = half * 16 + c2 * 8 + qq;
@@ -488,6 +544,7 @@ __global__ void __launch_bounds__(kThreads, 1) csa_prefill_index_kernel(Params p
           }
           xo[qi * kTileKeys + r] = __float_as_uint(__fmul_rn(sc, kscale)) + 1u;
         }
+#endif
       }
       // this warp's TMEM reads are done: the accumulator may be overwritten
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
