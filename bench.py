@@ -87,6 +87,21 @@ def read_traffic(summary=None):
     return None
 
 
+def init_nccl(dist, dev):
+    """init_process_group over NCCL with the communicator created eagerly; fd
+    1 points at stderr meanwhile, so a banner NCCL prints at init (NCCL_DEBUG)
+    stays out of rank 0's stdout, which carries only the JSON line."""
+    sys.stdout.flush()
+    saved = os.dup(1)
+    os.dup2(2, 1)
+    try:
+        dist.init_process_group("nccl", device_id=dev)
+    finally:
+        sys.stdout.flush()
+        os.dup2(saved, 1)
+        os.close(saved)
+
+
 class ClockSampler:
     """nvidia-smi clocks / throttle reasons sampled during the timed region."""
 
@@ -250,9 +265,6 @@ def cpu_baseline(steps: int, warmup: int, budget_s: float, full_line: bool = Fal
 
 # ------------------------------------------------------------------- main
 def main():
-    # rank 0's stdout carries exactly one JSON line: NCCL's own banner and
-    # debug lines (NCCL_DEBUG) go to stderr
-    os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=102400)
@@ -299,7 +311,7 @@ def main():
     if world > 1:
         import torch.distributed as dist
 
-        dist.init_process_group("nccl", device_id=dev)
+        init_nccl(dist, dev)
     from aether_kernels.paged import csa_decode_paged
 
     cache, sets = build_sets(args.sets, dev, rank)
@@ -497,7 +509,7 @@ def run_long(args):
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
-        dist.init_process_group("nccl", device_id=dev)
+        init_nccl(dist, dev)
     NB, bits = 65536, 8
     assert NB % (world * PAGE) == 0
     per = NB // world
@@ -614,7 +626,7 @@ def run_hca(args):
     if world > 1:
         import torch.distributed as dist
 
-        dist.init_process_group("nccl", device_id=dev)
+        init_nccl(dist, dev)
     B, bits, nsets = 32, 4, 240
     pages_per_set = B * (1024 // PAGE)
     cache = TurboQuantPagedCache(nsets * pages_per_set, bits, dev, with_index=False)
@@ -706,7 +718,7 @@ def run_prefill(args):
     if world > 1:
         import torch.distributed as dist
 
-        dist.init_process_group("nccl", device_id=dev)
+        init_nccl(dist, dev)
     R, NQ, CACHED, H, bits = args.prefill_requests, args.prefill_queries, args.prefill_cached, 12, 4
     nblk = (CACHED + NQ) // 4
     pages = (nblk + 63) // 64
