@@ -247,7 +247,7 @@ int aether_hca_decode_paged(const void* q, const float* sink, const void* window
                             void* stream);
 
 /* ------------------------------------------ context-parallel decode
- * New design (the reference has no multi-GPU attention; SURVEY 8(e)): a
+ * New design (the reference has no multi-GPU attention): a
  * sequence's compressed blocks are split into contiguous ranges, one per
  * device; this device holds blocks [id_base, id_base + nblocks[b]).
  *

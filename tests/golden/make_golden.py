@@ -1,8 +1,8 @@
 """Writes tests/golden/reference_vectors.npz from the reference implementation.
 
-Run in a container that has the reference checkout (the path is the first
-argument, default /root/reference); the fixtures it writes are committed so
-that the tests never need the reference at run time.  Every array below is
+Run where the reference checkout is available: its path is the first
+argument, or the AETHER_REFERENCE environment variable.  The fixtures it
+writes are committed, so the tests never need the reference at run time.  Every array below is
 produced by the reference's own code:
 
   aether_2b/turbo_quant.py         PolarQuant.encode / decode, _wht, _diag
@@ -20,7 +20,12 @@ from pathlib import Path
 import numpy as np
 import torch
 
-REF = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+import os  # noqa: E402
+
+_ref = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("AETHER_REFERENCE")
+if not _ref:
+    sys.exit("usage: make_golden.py <reference checkout>  (or set AETHER_REFERENCE)")
+REF = Path(_ref)
 sys.path.insert(0, str(REF))
 
 from aether_2b.configuration import Aether2BConfig  # noqa: E402
