@@ -39,7 +39,7 @@ def needs_build() -> bool:
     if not OUT.exists():
         return True
     mtime = OUT.stat().st_mtime
-    deps = [CSRC / s for s in SOURCES] + list(CSRC.glob("*.cuh"))
+    deps = [CSRC / s for s in SOURCES] + list(CSRC.glob("*.cuh")) + list(INCLUDE.glob("*.h"))
     return any(p.stat().st_mtime > mtime for p in deps)
 
 

@@ -1,6 +1,10 @@
 // Library-level C-ABI entry points: version, last error message, build info.
 #include <string.h>
 
+#include <map>
+#include <mutex>
+#include <utility>
+
 #include "aether_b200.h"
 #include "capi_util.cuh"
 
@@ -21,6 +25,28 @@ int check_launch(const char* what) {
     set_last_error("%s: launch failed: %s", what, cudaGetErrorString(e));
     return 2;
   }
+  return 0;
+}
+
+int ensure_smem_attr(const void* fn, int bytes, const char* what) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) {
+    set_last_error("%s: cudaGetDevice: %s", what, cudaGetErrorString(e));
+    return 2;
+  }
+  static std::mutex mu;
+  static std::map<std::pair<const void*, int>, int> done;  // (kernel, device) -> bytes set
+  std::lock_guard<std::mutex> lock(mu);
+  const auto key = std::make_pair(fn, dev);
+  const auto it = done.find(key);
+  if (it != done.end() && it->second >= bytes) return 0;
+  e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess) {
+    set_last_error("%s: set shared memory size: %s", what, cudaGetErrorString(e));
+    return 2;
+  }
+  done[key] = bytes;
   return 0;
 }
 

@@ -14,6 +14,13 @@ void set_last_error(const char* fmt, ...);
 // launch, translating a pending launch error into status 2.
 int check_launch(const char* what);
 
+// Raises the dynamic shared-memory limit of kernel `fn` to `bytes` on the
+// current device.  The attribute belongs to each device's context, so it is
+// set once per (kernel, device) pair; the record is guarded by a mutex, so
+// several host threads (or several devices driven by one process) are safe.
+// Returns 0, or 2 with the last-error message set.
+int ensure_smem_attr(const void* fn, int bytes, const char* what);
+
 }  // namespace aether
 
 #define AETHER_REQUIRE(cond, ...)          \

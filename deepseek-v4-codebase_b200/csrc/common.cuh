@@ -47,19 +47,38 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
                : "memory");
 }
-// Bounded wait on phase `parity`.  Returns false (and flags the error) if the
-// phase did not complete within ~2^22 polls (milliseconds), so a lost copy can
-// never hang the GPU.
+// Nanoseconds of the GPU's global timer (%globaltimer): bounds waits by
+// elapsed time rather than by a count of polls, whose duration varies.
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+// Every bounded wait in these kernels gives up after this long.  A wait that
+// runs out means a copy or a producer was lost; the status word then carries
+// kErrWaitTimeout and that launch's outputs are undefined.
+constexpr uint64_t kWaitLimitNs = 200ull * 1000 * 1000;  // 0.2 s
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t addr, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(done)
+      : "r"(addr), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+// Bounded wait on phase `parity` of an mbarrier.  Returns false (and sets
+// kErrWaitTimeout) if the phase has not completed within kWaitLimitNs.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
-  uint32_t addr = smem_u32(bar);
-  for (int it = 0; it < (1 << 22); ++it) {
-    uint32_t done;
-    asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
-        : "=r"(done)
-        : "r"(addr), "r"(parity)
-        : "memory");
-    if (done) return true;
+  const uint32_t addr = smem_u32(bar);
+  if (mbar_try_wait(addr, parity)) return true;
+  const uint64_t t0 = global_ns();
+  for (;;) {
+    for (int it = 0; it < 64; ++it)
+      if (mbar_try_wait(addr, parity)) return true;
+    if (global_ns() - t0 > kWaitLimitNs) break;
   }
   report_error(err, kErrWaitTimeout);
   return false;
@@ -69,12 +88,18 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
 // sequence numbers compared with wrap-around).  The word is written by a
 // stream memory operation on a copy stream after that stream's copy, so the
 // wait never depends on another kernel making progress.  Returns false (and
-// flags the error) after ~2^20 polls (about 0.1 s).
+// sets kErrWaitTimeout) after kWaitLimitNs.
 __device__ __forceinline__ bool flag_wait(const uint32_t* flag, uint32_t target, int* err) {
-  for (int it = 0; it < (1 << 20); ++it) {
+  uint64_t t0 = 0;
+  for (int it = 0;; ++it) {
     uint32_t v;
     asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
     if (static_cast<int32_t>(v - target) >= 0) return true;
+    if (it == 0) {
+      t0 = global_ns();
+    } else if (global_ns() - t0 > kWaitLimitNs) {
+      break;
+    }
     __nanosleep(100);
   }
   report_error(err, kErrWaitTimeout);

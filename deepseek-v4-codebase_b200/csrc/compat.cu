@@ -348,6 +348,7 @@ int aether_csa_indexer_topk(const float* index_q, const float* index_kv, const f
   AETHER_REQUIRE(k <= S, "k (%d) must not exceed the number of sources (%d)", k, S);
   AETHER_REQUIRE(k <= kTopkMax, "k must be <= %d, got %d", kTopkMax, k);
   AETHER_REQUIRE(S < 65536, "csa_indexer_topk: at most 65535 sources per row, got %d", S);
+  AETHER_REQUIRE(B >= 0, "csa_indexer_topk: batch must be non-negative, got %d", B);
   AETHER_REQUIRE(scratch != nullptr, "csa_indexer_topk: scratch buffer is required");
   if (B == 0) return 0;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -398,7 +399,9 @@ int aether_hca_compress(const void* buffer_c, const void* buffer_z, void* out, i
 // GPU that loads the library holds that array until the process exits.
 // The first call on a device, with that device current, looks up the array's
 // device address (cudaGetSymbolAddress) and caches it; make that first call
-// before any stream capture.  All calls share the one array: every call
+// before any stream capture.  The cached address belongs to the device's
+// current context: after cudaDeviceReset on a device, unload and reload the
+// library before calling this entry point there again.  All calls share the one array: every call
 // overwrites the scores it reads, so nothing has to be cleared, but two calls
 // whose kernels overlap on the GPU (different streams, no ordering) race on it.
 #include <mutex>

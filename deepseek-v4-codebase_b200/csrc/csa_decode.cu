@@ -834,12 +834,7 @@ template <int BITS, int CS, bool HCA>
 static int launch_csa(const CsaParams& p, int B, cudaStream_t st) {
   using C = CsaCfg<BITS, CS, HCA>;
   auto kern = csa_decode_kernel<BITS, CS, HCA>;
-  static bool attr_set = false;  // per template instance, per process
-  if (!attr_set) {
-    AETHER_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM),
-                    "csa_decode: set smem");
-    attr_set = true;
-  }
+  if (int rc = ensure_smem_attr(reinterpret_cast<const void*>(kern), C::SMEM, "csa_decode")) return rc;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(B * CS);
   cfg.blockDim = dim3(kThreads);

@@ -39,10 +39,12 @@
 #include "aether_b200.h"
 #include "capi_util.cuh"
 #include "common.cuh"
+#include "decode_common.cuh"
 
 namespace cg = cooperative_groups;
 
 namespace aether {
+
 
 constexpr int kQThreads = 512;
 constexpr int kQWarps = kQThreads / 32;
@@ -100,23 +102,14 @@ struct QCfg {
 };
 
 // Score kernel: a CTA stages PPC index pages and scores them.
-#ifndef AETHER_SCORE_THREADS
-#define AETHER_SCORE_THREADS 256
-#endif
-constexpr int kSThreads = AETHER_SCORE_THREADS;
+constexpr int kSThreads = 256;
 constexpr int kSWarps = kSThreads / 32;
-#ifndef AETHER_SCORE_UNROLL
-#define AETHER_SCORE_UNROLL 4
-#endif
-constexpr int kSU = AETHER_SCORE_UNROLL;  // 16-key tiles a warp scores per loop iteration
+constexpr int kSU = 4;  // 16-key tiles a warp scores per loop iteration
 template <int BITS>
 struct SCfg {
   static constexpr int RB_IDX = kIdxDim * BITS / 8;
   static constexpr int PB_IDX = page_bytes(RB_IDX);
-#ifndef AETHER_SCORE_PPC4
-#define AETHER_SCORE_PPC4 16
-#endif
-  static constexpr int PPC = BITS == 4 ? AETHER_SCORE_PPC4 : 8;  // pages per CTA (36 / 34 KB at 16 / 8)
+  static constexpr int PPC = BITS == 4 ? 16 : 8;  // pages per CTA (36 / 34 KB at 16 / 8)
   static constexpr int OFF_LIMB = PPC * PB_IDX;              // s8 [4 heads][3 limbs][64]
   static constexpr int OFF_MISC = OFF_LIMB + kIdxHeads * 3 * kIdxDim;
   static constexpr int OFF_BAR = OFF_MISC + 128;
@@ -200,12 +193,6 @@ struct QMisc {
   float l_h[kMaxHeads];
 };
 
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;"); }
-
 // kr[j] for a run-time j < 16 without local memory (binary select tree)
 __device__ __forceinline__ uint32_t pick16(const uint32_t (&kr)[16], int j) {
   uint32_t a[8];
@@ -282,120 +269,6 @@ __device__ __forceinline__ void hist_add(uint32_t* hist, int bin) {
   if (bin >= 0) atomicAdd(&hist[bin], 1u);
 }
 
-// nibble pair of one byte -> half2(lo, hi), exact signed values
-__device__ __forceinline__ uint32_t nib_byte_to_h2(uint32_t byte) {
-  uint32_t y = (byte & 0xFu) | ((byte & 0xF0u) << 12);
-  y = (y ^ 0x00080008u) | 0x64006400u;
-  __half2 h = *reinterpret_cast<__half2*>(&y);
-  h = __hsub2(h, __halves2half2(__ushort_as_half(0x6408), __ushort_as_half(0x6408)));  // 1032
-  return *reinterpret_cast<uint32_t*>(&h);
-}
-// two int8 codes (low 16 bits of w) -> half2
-__device__ __forceinline__ uint32_t s8pair_to_h2(uint32_t w) {
-  uint32_t y = __byte_perm(w ^ 0x8080u, 0x64646464u, 0x5140);  // [b0^80, 0x64, b1^80, 0x64]
-  __half2 h = *reinterpret_cast<__half2*>(&y);
-  h = __hsub2(h, __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480)));  // 1152
-  return *reinterpret_cast<uint32_t*>(&h);
-}
-// selected nibble (shift sh) of two bytes -> half2
-__device__ __forceinline__ uint32_t two_nib_to_h2(uint32_t b0, uint32_t b1, int sh) {
-  uint32_t y = ((b0 >> sh) & 0xFu) | (((b1 >> sh) & 0xFu) << 16);
-  y = (y ^ 0x00080008u) | 0x64006400u;
-  __half2 h = *reinterpret_cast<__half2*>(&y);
-  h = __hsub2(h, __halves2half2(__ushort_as_half(0x6408), __ushort_as_half(0x6408)));
-  return *reinterpret_cast<uint32_t*>(&h);
-}
-__device__ __forceinline__ uint32_t two_s8_to_h2(uint32_t b0, uint32_t b1) {
-  return s8pair_to_h2((b0 & 0xFFu) | ((b1 & 0xFFu) << 8));
-}
-__device__ __forceinline__ uint32_t bf2_to_h2(uint32_t v) {
-  const __nv_bfloat162 b = *reinterpret_cast<__nv_bfloat162*>(&v);
-  const float2 f = __bfloat1622float2(b);
-  return pack_half2(f.x, f.y);
-}
-__device__ __forceinline__ void mma_bf16(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};"
-      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-
-// In-warp normalised 128-point WHT of 4 consecutive values per lane (unscaled).
-__device__ __forceinline__ void warp_wht128(float (&v)[4], int lane) {
-  {
-    const float a0 = v[0] + v[1], a1 = v[0] - v[1], a2 = v[2] + v[3], a3 = v[2] - v[3];
-    v[0] = a0 + a2;
-    v[2] = a0 - a2;
-    v[1] = a1 + a3;
-    v[3] = a1 - a3;
-  }
-#pragma unroll
-  for (int ld = 1; ld < 32; ld <<= 1) {
-    const bool up = (lane & ld) != 0;
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const float o = __shfl_xor_sync(0xffffffffu, v[k], ld);
-      v[k] = up ? o - v[k] : v[k] + o;
-    }
-  }
-}
-
-
-// Rotated index query of head `warp` (warps 0-3): 24-bit limbs into `limb`,
-// their per-limb sums and alpha_h = softplus(w_h) * scale_h into misc.
-__device__ __forceinline__ void index_query_limbs(const QParams& p, int b, int warp, int lane, int8_t* limb,
-                                                  float* alpha, int (*lsum)[3]) {
-  const int h = warp;
-  const float* src = p.index_q + (static_cast<long long>(b) * kIdxHeads + h) * kIdxDim;
-  float v0 = src[lane * 2] * p.diag_idx[lane * 2];
-  float v1 = src[lane * 2 + 1] * p.diag_idx[lane * 2 + 1];
-  {
-    const float a = v0, c2 = v1;
-    v0 = a + c2;
-    v1 = a - c2;
-  }
-#pragma unroll
-  for (int ld = 1; ld < 32; ld <<= 1) {
-    const bool up = (lane & ld) != 0;
-    const float o0 = __shfl_xor_sync(0xffffffffu, v0, ld);
-    const float o1 = __shfl_xor_sync(0xffffffffu, v1, ld);
-    v0 = up ? o0 - v0 : v0 + o0;
-    v1 = up ? o1 - v1 : v1 + o1;
-  }
-  v0 *= 0.125f;
-  v1 *= 0.125f;
-  const float am = warp_max(fmaxf(fabsf(v0), fabsf(v1)));
-  const float s = am > 0.f ? am / 8355000.0f : 1.0f;
-  int ls[3] = {0, 0, 0};
-#pragma unroll
-  for (int k = 0; k < 2; ++k) {
-    const int v = __float2int_rn(__fdiv_rn(k ? v1 : v0, s));
-    const int l0 = ((v + 128) & 255) - 128;
-    const int w1 = (v - l0) >> 8;
-    const int l1 = ((w1 + 128) & 255) - 128;
-    const int l2 = (w1 - l1) >> 8;
-    const int d = lane * 2 + k;
-    limb[(h * 3 + 0) * kIdxDim + d] = static_cast<int8_t>(l0);
-    limb[(h * 3 + 1) * kIdxDim + d] = static_cast<int8_t>(l1);
-    limb[(h * 3 + 2) * kIdxDim + d] = static_cast<int8_t>(l2);
-    ls[0] += l0;
-    ls[1] += l1;
-    ls[2] += l2;
-  }
-#pragma unroll
-  for (int l = 0; l < 3; ++l) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) ls[l] += __shfl_xor_sync(0xffffffffu, ls[l], o);
-  }
-  if (lane == 0) {
-    alpha[h] = softplus_f(p.index_w[b * kIdxHeads + h]) * s;
-    lsum[h][0] = ls[0];
-    lsum[h][1] = ls[1];
-    lsum[h][2] = ls[2];
-  }
-}
-
 template <int BITS>
 __global__ void __launch_bounds__(kSThreads) csa_score_kernel(QParams p, int splits) {
   using C = SCfg<BITS>;
@@ -444,34 +317,12 @@ __global__ void __launch_bounds__(kSThreads) csa_score_kernel(QParams p, int spl
   }
   stamp(1);
   pdl_wait();
-  if (warp < kIdxHeads) index_query_limbs(p, b, warp, lane, limb, alpha, lsum);
+  if (warp < kIdxHeads) index_query_limbs(p.index_q, p.index_w, p.diag_idx, b, warp, lane, limb, alpha, lsum);
   __syncthreads();
-  // B fragments: column n = g of n-tile 0 is (head g/2, limb g%2), of
-  // n-tile 1 (head g/2, limb 2) for even g and zero for odd g.
   uint32_t bq[2][2][2];
-  {
-    const int hq = g >> 1;
-#pragma unroll
-    for (int j = 0; j < 2; ++j)
-#pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        uint32_t w0 = 0, w1 = 0;
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int d = BITS == 4 ? 16 * t + 8 * j + 2 * e + hh : 16 * t + 8 * j + 4 * hh + e;
-          const int lA = limb[(hq * 3 + (g & 1)) * kIdxDim + d];
-          const int lB = (g & 1) ? 0 : limb[(hq * 3 + 2) * kIdxDim + d];
-          w0 |= (static_cast<uint32_t>(lA) & 0xFFu) << (8 * e);
-          w1 |= (static_cast<uint32_t>(lB) & 0xFFu) << (8 * e);
-        }
-        bq[0][j][hh] = w0;
-        bq[1][j][hh] = w1;
-      }
-  }
+  int c0i, c1i, c2i;
+  limb_fragments<BITS>(limb, lsum, g, t, bq, c0i, c1i, c2i);
   const float alpha_t = alpha[t];
-  const int c0i = BITS == 4 ? -8 * lsum[t][0] : 0;
-  const int c1i = BITS == 4 ? -8 * lsum[t][1] : 0;
-  const int c2i = BITS == 4 ? -8 * lsum[t][2] : 0;
   stamp(2);
   mbar_wait(bar, 0, p.err);
   stamp(3);
@@ -556,10 +407,7 @@ __global__ void __launch_bounds__(kSThreads) csa_score_kernel(QParams p, int spl
 }
 
 template <int BITS, int CS>
-#ifndef AETHER_ATTEND_MINB
-#define AETHER_ATTEND_MINB 2
-#endif
-__global__ void __launch_bounds__(kQThreads, CS > 1 ? AETHER_ATTEND_MINB : 1) csa_attend_kernel(QParams p) {
+__global__ void __launch_bounds__(kQThreads, CS > 1 ? 2 : 1) csa_attend_kernel(QParams p) {
   using C = QCfg<BITS, CS>;
   extern __shared__ __align__(128) uint8_t smem[];
   // grid: ((sequence * chunks) + chunk) * CS + rank; a cluster of CS CTAs
@@ -1510,10 +1358,7 @@ __global__ void __launch_bounds__(kQThreads, 1) hca_attend_kernel(HcaParams p) {
   stamp(8);
 }
 
-#ifndef AETHER_ATTEND_CLUSTER
-#define AETHER_ATTEND_CLUSTER 2
-#endif
-constexpr int kAttendCluster = AETHER_ATTEND_CLUSTER;  // CTAs per sequence in the attention phase
+constexpr int kAttendCluster = 2;  // CTAs per sequence in the attention phase
 
 // Dynamic shared memory that keeps a second attend CTA off an SM.  The
 // attend CTA needs ~99 KB, so two fit on one SM; when a launch's CTAs fit the
@@ -1522,37 +1367,28 @@ constexpr int kAttendCluster = AETHER_ATTEND_CLUSTER;  // CTAs per sequence in t
 // latency-bound phases.  Larger launches (prefill) use the compact size.
 constexpr int kSpreadSmem = 116 * 1024;
 
-static int sm_count() {
-  static const int n = [] {
-    int dev = 0, v = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
-      cudaGetLastError();
-      return 148;
-    }
-    return v;
-  }();
-  return n;
+static int sm_count() {  // of the current device
+  int dev = 0, v = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+    cudaGetLastError();
+    return 148;
+  }
+  return v;
 }
 
 template <int BITS>
 static int set_smem_attrs() {
-  static bool done = false;
-  if (!done) {
-    AETHER_CUDA_TRY(cudaFuncSetAttribute(csa_score_kernel<BITS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         SCfg<BITS>::SMEM),
-                    "csa_decode: set shared memory size (score)");
-    AETHER_CUDA_TRY(cudaFuncSetAttribute(csa_attend_kernel<BITS, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         QCfg<BITS, 1>::SMEM),
-                    "csa_decode: set shared memory size (select)");
-    AETHER_CUDA_TRY(cudaFuncSetAttribute(csa_attend_kernel<BITS, kAttendCluster>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         QCfg<BITS, kAttendCluster>::SMEM > kSpreadSmem
-                                             ? QCfg<BITS, kAttendCluster>::SMEM
-                                             : kSpreadSmem),
-                    "csa_decode: set shared memory size (attend)");
-    done = true;
-  }
-  return 0;
+  int rc = ensure_smem_attr(reinterpret_cast<const void*>(csa_score_kernel<BITS>), SCfg<BITS>::SMEM,
+                            "csa_decode (score)");
+  if (!rc)
+    rc = ensure_smem_attr(reinterpret_cast<const void*>(csa_attend_kernel<BITS, 1>), QCfg<BITS, 1>::SMEM,
+                          "csa_decode (select)");
+  if (!rc)
+    rc = ensure_smem_attr(reinterpret_cast<const void*>(csa_attend_kernel<BITS, kAttendCluster>),
+                          QCfg<BITS, kAttendCluster>::SMEM > kSpreadSmem ? QCfg<BITS, kAttendCluster>::SMEM
+                                                                          : kSpreadSmem,
+                          "csa_decode (attend)");
+  return rc;
 }
 
 template <int BITS>
@@ -1671,18 +1507,10 @@ static int run_decode(QParams p, int B, int max_nblocks, bool pdl, cudaStream_t 
   int rc = set_smem_attrs<BITS>();
   if (rc) return rc;
   p.ws = reinterpret_cast<uint32_t*>(workspace);
-  static const int only = [] {  // profiling aid: 1 = score kernel only, 2 = attend kernel only
-    const char* e = getenv("AETHER_DECODE_ONLY");
-    return e ? atoi(e) : 0;
-  }();
   const int chunks = (max_nblocks + kMaxKeys - 1) / kMaxKeys;
-  if (only != 2) rc = launch_score<BITS>(p, B, max_nblocks, pdl, st);
-  if (rc || only == 1) return rc;
-  static const bool attend_pdl = [] {
-    const char* e = getenv("AETHER_ATTEND_PDL");
-    return !(e && e[0] == '0');
-  }();
-  if (chunks <= 1) return launch_attend<BITS>(p, B, attend_pdl, st);
+  rc = launch_score<BITS>(p, B, max_nblocks, pdl, st);
+  if (rc) return rc;
+  if (chunks <= 1) return launch_attend<BITS>(p, B, true, st);
   // long sequences: top-k per 8192-block chunk, then top-k of the chunk winners
   uint32_t* ckeys = p.ws + static_cast<size_t>(B) * p.ws_stride;
   int32_t* cids = reinterpret_cast<int32_t*>(ckeys + static_cast<size_t>(B) * chunks * kMaxTopK);
@@ -1740,13 +1568,7 @@ int hca_decode_cta(const void* q, const float* sink, const void* window, const i
   p.softmax_scale = softmax_scale;
   const int smem = bits == 4 ? HCfg<4>::SMEM : HCfg<8>::SMEM;
   auto kern = bits == 4 ? hca_attend_kernel<4> : hca_attend_kernel<8>;
-  static bool attr4 = false, attr8 = false;
-  bool& attr = bits == 4 ? attr4 : attr8;
-  if (!attr) {
-    AETHER_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
-                    "hca decode: set shared memory size");
-    attr = true;
-  }
+  if (int rc = ensure_smem_attr(reinterpret_cast<const void*>(kern), smem, "hca decode")) return rc;
   cudaLaunchAttribute at[2];
   at[0].id = cudaLaunchAttributeClusterDimension;
   at[0].val.clusterDim.x = kHcaCS;

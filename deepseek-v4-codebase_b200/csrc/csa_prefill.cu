@@ -149,15 +149,15 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, Mi
                                               bool backoff = false) {
   if (*reinterpret_cast<volatile int*>(&m->abort_flag)) return false;
   const uint32_t addr = smem_u32(bar);
-  for (int it = 0; it < (1 << 22); ++it) {
-    uint32_t done;
-    asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
-        : "=r"(done)
-        : "r"(addr), "r"(parity)
-        : "memory");
-    if (done) return true;
-    if (backoff) __nanosleep(64);
+  if (mbar_try_wait(addr, parity)) return true;
+  const uint64_t t0 = global_ns();
+  for (;;) {
+    for (int it = 0; it < 16; ++it) {
+      if (mbar_try_wait(addr, parity)) return true;
+      if (backoff) __nanosleep(64);
+    }
+    if (*reinterpret_cast<volatile int*>(&m->abort_flag)) return false;
+    if (global_ns() - t0 > kWaitLimitNs) break;
   }
   report_error(err, kErrWaitTimeout);
   *reinterpret_cast<volatile int*>(&m->abort_flag) = 1;
@@ -688,13 +688,9 @@ static long long* g_debug = nullptr;
 
 template <int BITS>
 static int launch(const Params& p, int ntiles, cudaStream_t st) {
-  static bool attr = false;
-  if (!attr) {
-    AETHER_CUDA_TRY(cudaFuncSetAttribute(csa_prefill_index_kernel<BITS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         Cfg<BITS>::SMEM),
-                    "csa_prefill: set shared memory size");
-    attr = true;
-  }
+  if (int rc = ensure_smem_attr(reinterpret_cast<const void*>(csa_prefill_index_kernel<BITS>), Cfg<BITS>::SMEM,
+                                "csa_prefill"))
+    return rc;
   csa_prefill_index_kernel<BITS><<<ntiles, kThreads, Cfg<BITS>::SMEM, st>>>(p);
   return check_launch("csa_prefill_topk");
 }
