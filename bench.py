@@ -232,32 +232,94 @@ def cpu_decode(bt, rows):
                             classify_ties=False)
 
 
+def cpu_predecode(bt, rows):
+    """The reference's memoised dequant (aether_2b/serving.py:368-375): each
+    sequence's index keys and main entries decoded once, outside the timing."""
+    from oracle import decode as odec
+    from oracle import turboquant as otq
+
+    p = bt["pools"]
+    cache = {}
+    for b in rows:
+        nb, table = int(bt["nblocks"][b]), bt["page_table"][b]
+        keys = otq.decode(odec.gather_pages(p["idx_codes"], table, nb),
+                          odec.gather_pages(p["idx_scale"], table, nb).unsqueeze(-1), CFG["bits"], 42)
+        main = otq.decode(odec.gather_pages(p["kv_codes"], table, nb),
+                          odec.gather_pages(p["kv_scale"], table, nb).unsqueeze(-1), CFG["bits"], 42)
+        cache[b] = (keys, main)
+    return cache
+
+
+def cpu_decode_memo(bt, rows, cache):
+    """One step of the reference path on already-decoded caches: indexer,
+    top-k, gather, sparse sink attention (oracle.decode.decode_step minus the
+    dequant)."""
+    from oracle import decode as odec
+
+    outs = []
+    for b in rows:
+        keys, main = cache[b]
+        k = min(CFG["top_k"], keys.shape[0])
+        s32 = odec.index_scores(bt["index_q"][b].float(), bt["index_weight"][b].float(), keys)
+        sel = torch.sort(odec.topk_stable(s32, k)).values
+        src = torch.cat([main[sel], bt["window"][b, : int(bt["window_len"][b])].float()], dim=0)
+        outs.append(odec.sink_attention(bt["q"][b].float(), src, bt["sink"].float(), bt["softmax_scale"]))
+    return torch.stack(outs)
+
+
 def cpu_baseline(steps: int, warmup: int, budget_s: float, full_line: bool = False):
+    """The reference's fp32 CPU path on the host cores, two ways: with the
+    dequant of every visible block in every step, and with the dequant
+    memoised (the reference re-decodes a sequence's cache only when an
+    emitted block changes its shape: every 4 tokens for CSA).  ``value`` is
+    the steady state of the reference's decode loop: the memoised step plus
+    a quarter of the dequant."""
     sys.path.insert(0, str(ROOT))
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
     bt = make_cpu_batch()
     B, per_step = CFG["batch"], 4
+
+    def rows_of(i):
+        return [(i * per_step + j) % B for j in range(per_step)]
+
     for i in range(max(warmup, 0)):
-        cpu_decode(bt, [(i * per_step + j) % B for j in range(per_step)])
+        cpu_decode(bt, rows_of(i))
+    half = budget_s / 2
     t0 = time.perf_counter()
     n = 0
     while n < max(steps, 1):
-        cpu_decode(bt, [(n * per_step + j) % B for j in range(per_step)])
+        cpu_decode(bt, rows_of(n))
         n += 1
-        if time.perf_counter() - t0 > budget_s:
+        if time.perf_counter() - t0 > half:
             break
-    dt = time.perf_counter() - t0
-    done = n * per_step
-    qps = done / dt
+    dt_full = (time.perf_counter() - t0) / n
+    # memoised: decode the sample's sequences first (untimed), then the steps
+    n_memo_rows = sorted({r for i in range(max(n, 1)) for r in rows_of(i)})
+    memo = cpu_predecode(bt, n_memo_rows)
+    cpu_decode_memo(bt, rows_of(0), memo)
+    t0 = time.perf_counter()
+    m = 0
+    while m < max(steps, 1):
+        cpu_decode_memo(bt, rows_of(m % max(n, 1)), memo)
+        m += 1
+        if time.perf_counter() - t0 > half:
+            break
+    dt_memo = (time.perf_counter() - t0) / m
+    dt_steady = dt_memo + (dt_full - dt_memo) / 4
+    qps = per_step / dt_steady
     base = {"value": round(qps, 2), "unit": UNIT, "cores": threads, "kind": "port",
-            "sample": f"{done} queries ({n} steps x {per_step} sequences of the 64-sequence, 16K-32K-token, "
-                      "4-bit batch); fp32 torch CPU restatement of the reference path incl. per-step dequant"}
+            "value_dequant_every_step": round(per_step / dt_full, 2),
+            "value_memoised_dequant": round(per_step / dt_memo, 2),
+            "sample": f"{n * per_step} + {m * per_step} queries ({n} steps with dequant, {m} with memoised dequant, "
+                      f"{per_step} sequences of the 64-sequence, 16K-32K-token, 4-bit batch per step); fp32 torch CPU "
+                      "restatement of the reference path; value = memoised step + 1/4 of the dequant (re-decode per "
+                      "emitted CSA block, every 4 tokens)"}
     if not full_line:
         return base
-    return {"metric": METRIC, "value": round(qps, 2), "unit": UNIT, "n_gpus": 0, "steps": n, "warmup": warmup,
-            "ms_per_step": round(dt / n * 1e3, 3), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "f32", "data": "synthetic", "impl": "reference",
+    return {"metric": METRIC, "value": round(qps, 2), "unit": UNIT, "n_gpus": 0, "steps": n + m, "warmup": warmup,
+            "ms_per_step": round(dt_steady * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
             "config": {"workload": "csa_decode_4bit_b64_ctx16k-32k", **CFG},
             "cpu_baseline": base,
             "e2e": {"value": round(qps, 2), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -275,7 +337,6 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-pdl", dest="pdl", action="store_false",
                     help="launch without programmatic dependent launch (no prefetch overlap across steps)")
-    ap.add_argument("--cluster", type=int, default=0, help="0: score + attend kernels; 4 or 8: cluster kernel")
     ap.add_argument("--microbatches", type=int, default=1,
                     help="split each step's batch into this many independent micro-batches on separate streams")
     ap.add_argument("--profile-launches", type=int, default=0,
@@ -331,7 +392,7 @@ def main():
         csa_decode_paged(s.q[lo:hi], s.index_q[lo:hi], s.index_weight[lo:hi], s.sink, s.window[lo:hi],
                          s.window_len[lo:hi], cache, s.page_table[lo:hi], s.nblocks[lo:hi], s.softmax_scale,
                          top_k=s.top_k, out=outs[i % len(sets)][lo:hi], indices=sels[i % len(sets)][lo:hi],
-                         err=err, overlap_prefetch=pdl, workspace=w, cluster=args.cluster)
+                         err=err, overlap_prefetch=pdl, workspace=w)
 
     def step(i, pdl=args.pdl):
         if mb == 1:
@@ -362,7 +423,11 @@ def main():
         return
 
     stream = torch.cuda.Stream(dev)
-    per_graph = 16 * len(sets)
+    # exactly args.steps timed steps: whole graphs of per_graph steps, then a
+    # graph with the remainder; consecutive steps read different cache sets
+    steps = max(1, args.steps)
+    per_graph = min(16 * len(sets), steps)
+    replays, rem = divmod(steps, per_graph)
     with torch.cuda.stream(stream):
         for i in range(args.warmup):
             step(i)
@@ -372,10 +437,15 @@ def main():
             for i in range(per_graph):
                 step(i)
         g.replay()
+        g_rem = None
+        if rem:
+            g_rem = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g_rem, stream=stream):
+                for i in range(rem):
+                    step(i)
+            g_rem.replay()
         stream.synchronize()
     assert int(err.item()) == 0, f"kernel error flag {int(err.item())}"
-    replays = max(1, (args.steps + per_graph - 1) // per_graph)
-    steps = replays * per_graph
 
     sampler = ClockSampler(local)
     if world > 1:
@@ -388,6 +458,8 @@ def main():
         ev0.record(stream)
         for _ in range(replays):
             g.replay()
+        if g_rem is not None:
+            g_rem.replay()
         ev1.record(stream)
     ev1.synchronize()
     clocks = sampler.stop()
@@ -464,14 +536,14 @@ def main():
         line = {
             "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world, "steps": steps,
             "warmup": args.warmup, "ms_per_step": round(ms_step, 6), "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "u8", "data": "synthetic",
+            "vs_baseline": None, "dtype": "s8+f16", "data": "synthetic",
             "config": {"workload": "csa_decode_4bit_b64_ctx16k-32k", **CFG, "cache_sets": len(sets),
                        "cache_bytes_cycled": int(sum(t.numel() * t.element_size() for t in cache.tensors())),
                        "l2_policy": "inputs larger than L2: each step reads a different cache set, sets > 4x L2",
                        "parallelism": f"request-sharded x{world}", "pdl": bool(args.pdl),
                        "microbatches": args.microbatches,
                        "timing": "CUDA graph replay, CUDA events"},
-            "gpu_launches": steps * (1 if args.cluster else 2),
+            "gpu_launches": steps * 2,
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_source": peak_src, "traffic": read_traffic(),
                          "algorithmic_bytes_per_launch": int(bytes_launch)},
@@ -592,7 +664,7 @@ def run_long(args):
         print(json.dumps({
             "metric": LONG_METRIC, "value": round(steps / (ms / 1e3), 1), "unit": "queries/s", "n_gpus": world,
             "steps": steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 6), "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "u8", "data": "synthetic",
+            "scaling": "strong", "vs_baseline": None, "dtype": "s8+f16", "data": "synthetic",
             "config": {"workload": "csa_decode_8bit_b1_ctx262k", "nblocks": NB, "blocks_per_gpu": per, "bits": bits,
                        "rope": "yarn x8", "cache_sets": nsets, "parallelism": f"context-parallel x{world}",
                        "l2_policy": "inputs larger than L2: each step reads a different cache set",
@@ -680,7 +752,7 @@ def run_hca(args):
         print(json.dumps({
             "metric": HCA_METRIC, "value": round(world * B * steps / (ms / 1e3), 1), "unit": "queries/s",
             "n_gpus": world, "steps": steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 6),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8", "data": "synthetic",
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "s8+f16", "data": "synthetic",
             "config": {"workload": "hca_decode_4bit_b32_ctx131k", "batch": B, "nblocks": 1024, "bits": bits,
                        "window": 128, "rope": "yarn x4", "cache_sets": nsets,
                        "cache_bytes_cycled": int(cache.kv_pages.numel()),

@@ -185,7 +185,6 @@ def csa_decode_paged(
     out: Optional[torch.Tensor] = None,
     indices: Optional[torch.Tensor] = None,
     err: Optional[torch.Tensor] = None,
-    cluster: int = 0,
     scores: Optional[torch.Tensor] = None,
     overlap_prefetch: bool = False,
     workspace: Optional[torch.Tensor] = None,
@@ -203,8 +202,8 @@ def csa_decode_paged(
     ``AttentionKernelBackend.sparse_attention`` returns) and the selected
     block indices in ascending order, -1 padded.
 
-    ``cluster`` 0 (default) runs one CTA per sequence; 4 or 8 spread each
-    sequence over a thread-block cluster.  ``overlap_prefetch=True`` launches
+    Two kernels run per step: a score kernel and a select/attend kernel with
+    a 2-CTA cluster per sequence.  ``overlap_prefetch=True`` launches
     with programmatic dependent launch: the kernel may start while the
     previous kernel on the stream is still running and, before waiting for
     it, reads ``page_table``, ``nblocks``, ``window_len``, the cache pages and
@@ -250,7 +249,7 @@ def csa_decode_paged(
     _check(workspace.is_cuda and workspace.numel() * workspace.element_size() >= need,
            f"workspace must hold {need} bytes")
     if rope_inv_freq is not None:
-        _check(scores is None and cluster <= 1, "the fused output RoPE needs cluster 0 and no score output")
+        _check(scores is None, "the fused output RoPE does not write scores")
         _cuda(rope_positions, "rope_positions")
         _cuda(rope_inv_freq, "rope_inv_freq")
         _check(rope_positions.dtype == torch.int32 and rope_positions.numel() == B, "rope_positions must be int32 [B]")
@@ -259,14 +258,14 @@ def csa_decode_paged(
                   int(overlap_prefetch), rope_positions.data_ptr(), rope_inv_freq.data_ptr(),
                   2 * rope_inv_freq.numel(), _stream(dev))
     elif scores is None:
-        _lib.call("aether_csa_decode_paged", *common, workspace.data_ptr(), _opt_ptr(err), int(cluster),
+        _lib.call("aether_csa_decode_paged", *common, workspace.data_ptr(), _opt_ptr(err), 0,
                   int(overlap_prefetch), _stream(dev))
     else:
         _cuda(scores, "scores")
         _check(scores.dtype == torch.float32 and scores.shape[0] == B and scores.shape[1] >= page_table.shape[1] * PAGE,
                "scores must be float32 [B, >= max_pages * 64]")
         _lib.call("aether_csa_decode_paged_scores", *common, scores.data_ptr(), scores.shape[1],
-                  workspace.data_ptr(), _opt_ptr(err), int(cluster), int(overlap_prefetch), _stream(dev))
+                  workspace.data_ptr(), _opt_ptr(err), 0, int(overlap_prefetch), _stream(dev))
     return out, indices
 
 
@@ -488,15 +487,12 @@ def hca_decode_paged(
     softmax_scale: float,
     out: Optional[torch.Tensor] = None,
     err: Optional[torch.Tensor] = None,
-    cluster: int = 0,
     overlap_prefetch: bool = False,
 ) -> torch.Tensor:
     """One fused HCA decode step: attention over every visible compressed
     block plus the sliding window (aether_2b/serving.py:507-522).
 
-    ``cluster`` 0 (default) runs a 4-CTA cluster per sequence; 4 or 8 the
-    older single-kernel cluster path.  ``overlap_prefetch=True`` (cluster 0)
-    launches with programmatic dependent launch: before waiting for the
+    One 4-CTA cluster per sequence.  ``overlap_prefetch=True`` launches with programmatic dependent launch: before waiting for the
     previous kernel on the stream the kernel reads ``page_table``,
     ``nblocks``, ``window_len``, the cache pages and every window row except
     the newest; use it only when that kernel writes none of those."""
@@ -515,7 +511,7 @@ def hca_decode_paged(
         q.data_ptr(), sink.data_ptr(), window.data_ptr(), window_len.data_ptr(), cache.kv_pages.data_ptr(),
         page_table.data_ptr(), page_table.shape[1], cache.num_pages, nblocks.data_ptr(),
         page_table.shape[1] * PAGE, rademacher_diag(HEAD_DIM, cache.seed, dev).data_ptr(),
-        B, H, window.shape[1], cache.bits, float(softmax_scale), out.data_ptr(), _opt_ptr(err), int(cluster),
+        B, H, window.shape[1], cache.bits, float(softmax_scale), out.data_ptr(), _opt_ptr(err), 0,
         int(overlap_prefetch), _stream(dev),
     )
     return out

@@ -1449,7 +1449,6 @@ static int launch_attend(const QParams& p, int B, bool pdl, cudaStream_t st) {
 }
 
 static long long* g_cta_debug = nullptr;
-long long* cta_debug_buffer() { return g_cta_debug; }
 
 // workspace layout: u32 keys [B][ws_stride], then candidate keys / ids
 // [B][chunks * kMaxTopK] each (only for sequences longer than 8192 blocks)

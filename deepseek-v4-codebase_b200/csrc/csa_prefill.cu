@@ -42,11 +42,6 @@
 namespace aether {
 namespace prefill {
 
-// Tuning variant, off by default: pair two queries per packed fp32 FMA in
-// the epilogue (B rows ordered so a pair's columns are adjacent in TMEM).
-#ifndef AETHER_PF_PAIRED
-#define AETHER_PF_PAIRED 0
-#endif
 
 // packed fp32x2 helpers (sm_100 fma.rn.f32x2: per-lane IEEE fma)
 __device__ __forceinline__ uint64_t pack_f2(float lo, float hi) {
@@ -72,7 +67,6 @@ constexpr int kThreads = 512;
 constexpr int kQ = 32;                  // query tokens per CTA
 constexpr int kTileKeys = 128;          // keys per MMA tile (M)
 constexpr int kN = kQ * kIdxHeads * 2;  // 256 accumulator columns per tile
-constexpr int kCapMax = 512;            // candidate buffer entries per query (largest variant)
 constexpr int kMaxK = 256;
 constexpr uint32_t kLBO = 128, kSBO = 1024;  // canonical layout strides (bytes)
 
@@ -342,13 +336,10 @@ __global__ void __launch_bounds__(kThreads, 1) csa_prefill_index_kernel(Params p
       const int qint = valid ? __float2int_rn(__fdiv_rn(k ? x1 : x0, s)) : 0;
       const int a = (qint + 1024) >> 11, b = qint - a * 2048;
       const int d = 2 * lane + k;
-#if AETHER_PF_PAIRED
       // B row (query pair, head, limb, query & 1): the two queries of a pair
-      // sit in adjacent accumulator columns
+      // sit in adjacent accumulator columns, so the epilogue pairs them in
+      // packed fp32 FMAs
       const int n0 = ((qi >> 1) * kIdxHeads + h) * 4 + (qi & 1), nb = n0 + 2;
-#else
-      const int n0 = (qi * kIdxHeads + h) * 2, nb = n0 + 1;
-#endif
       *reinterpret_cast<__half*>(smem + C::OFF_B + canon(n0, d)) = __int2half_rn(a);
       *reinterpret_cast<__half*>(smem + C::OFF_B + canon(nb, d)) = __int2half_rn(b);
     }
@@ -507,9 +498,9 @@ __global__ void __launch_bounds__(kThreads, 1) csa_prefill_index_kernel(Params p
               "=r"(v[57]), "=r"(v[58]), "=r"(v[59]), "=r"(v[60]), "=r"(v[61]), "=r"(v[62]), "=r"(v[63])
             : "r"(ta));
         asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#if AETHER_PF_PAIRED
-        // two queries per packed fp32 FMA; each lane rounds exactly as the
-        // scalar sequence below, so the keys are bit-identical
+        // two queries per packed fp32 FMA (fma.rn.f32x2): each lane rounds
+        // exactly as the scalar fmaf(2048, D_a, D_b), fmaf(alpha, relu, acc)
+        // sequence, so the keys are bit-identical to the oracle's
 #pragma unroll
         for (int pp = 0; pp < 4; ++pp) {
           const int qa = half * 16 + c2 * 8 + 2 * pp;
@@ -530,21 +521,6 @@ __global__ void __launch_bounds__(kThreads, 1) csa_prefill_index_kernel(Params p
           xo[qa * kTileKeys + r] = __float_as_uint(__fmul_rn(s0, kscale)) + 1u;
           xo[(qa + 1) * kTileKeys + r] = __float_as_uint(__fmul_rn(s1, kscale)) + 1u;
         }
-#else
-#pragma unroll
-        for (int qq = 0; qq < 8; ++qq) {
-          const int qi = half * 16 + c2 * 8 + qq;
-          const float4 al = *reinterpret_cast<const float4*>(m->alpha[qi]);
-          const float alh[4] = {al.x, al.y, al.z, al.w};
-          float sc = 0.f;
-#pragma unroll
-          for (int h = 0; h < 4; ++h) {
-            const float dot = fmaf(2048.f, __uint_as_float(v[qq * 8 + h * 2]), __uint_as_float(v[qq * 8 + h * 2 + 1]));
-            sc = fmaf(alh[h], fmaxf(dot, 0.f), sc);
-          }
-          xo[qi * kTileKeys + r] = __float_as_uint(__fmul_rn(sc, kscale)) + 1u;
-        }
-#endif
       }
       // this warp's TMEM reads are done: the accumulator may be overwritten
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");

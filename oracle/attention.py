@@ -43,6 +43,15 @@ def dense_index_topk(index_q, index_kv, index_weight, k):
     return torch.sort(s, dim=-1, descending=True, stable=True).indices[:, :k], s
 
 
+def dense_index_scores64(index_q, index_kv, index_weight):
+    """fp64 indexer scores [B, S] and each row's score magnitude bound
+    sum_h softplus(w_h) max_s sum_c |q_hc k_sc| (the near-tie scale)."""
+    q, kv, w = index_q.double(), index_kv.double(), torch.nn.functional.softplus(index_weight.double())
+    s = (torch.relu(torch.einsum("bhc,bsc->bhs", q, kv)) * w.unsqueeze(-1)).sum(dim=1)
+    mag = (torch.einsum("bhc,bsc->bhs", q.abs(), kv.abs()) * w.unsqueeze(-1)).sum(dim=1).amax(dim=-1)
+    return s, mag
+
+
 def hca_compress(buffer_c, buffer_z):
     w = torch.softmax(buffer_z.float(), dim=1)
     return (w * buffer_c.float()).sum(dim=1)

@@ -11,7 +11,7 @@ ties to the lower block index.  Near-tie rows are flagged as in
 """
 from __future__ import annotations
 
-from typing import List, Sequence, Tuple
+from typing import List, Optional, Sequence, Tuple
 
 import torch
 
@@ -21,15 +21,21 @@ from .decode import gather_pages, index_scores, topk_stable
 
 def prefill_topk(index_q, index_weight, idx_codes, idx_scale, page_table, requests: Sequence[Tuple[int, int, int, int]],
                  bits: int, top_k: int, compression: int = 4, seed: int = 42,
-                 tie_tol: float = 1e-5) -> Tuple[List[torch.Tensor], List[bool]]:
+                 tie_tol: float = 1e-5, rows: Optional[Sequence[int]] = None) -> Tuple[List[torch.Tensor], List[bool]]:
     """requests: (first_row, num_queries, position of query 0, nblocks) per
     request.  Returns per query row (in request order) the selected block ids
-    ascending, and a near-tie flag."""
+    ascending, and a near-tie flag; with ``rows`` (query rows to check, in
+    ascending order) only those rows, in that order."""
     sels, ties = [], []
+    want = None if rows is None else set(int(x) for x in rows)
     for r, (row0, nq, pos0, nblk) in enumerate(requests):
+        if want is not None and not any(row0 <= x < row0 + nq for x in want):
+            continue
         keys = tq.decode(gather_pages(idx_codes, page_table[r], nblk),
                          gather_pages(idx_scale, page_table[r], nblk).unsqueeze(-1), bits, seed)
         for i in range(nq):
+            if want is not None and row0 + i not in want:
+                continue
             vis = min(nblk, (pos0 + i) // compression)
             k = min(top_k, vis)
             if vis == 0:

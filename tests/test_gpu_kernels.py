@@ -112,14 +112,18 @@ def test_csa_indexer_topk(ak, S, k):
     ikv = torch.randn(3, S, 64, generator=g)
     iw = torch.randn(3, 4, generator=g)
     got = csa_indexer_topk(iq.cuda(), ikv.cuda(), iw.cuda(), k).cpu()
-    exp, scores = oatt.dense_index_topk(iq, ikv, iw, k)
+    exp, _ = oatt.dense_index_topk(iq, ikv, iw, k)
+    s64, mag = oatt.dense_index_scores64(iq, ikv, iw)
     assert got.dtype == torch.int64 and got.shape == (3, k)
     for b in range(3):
-        s = scores[b]
-        # same set and the same (score desc, index asc) order, except where the
-        # fp32 scores of two candidates are within rounding of each other
-        if not torch.equal(got[b], exp[b]):
-            assert torch.allclose(s[got[b]], s[exp[b]], rtol=1e-5, atol=1e-6)
+        band = 1e-5 * float(mag[b])  # fp32 rounding of the score sums, scaled to the row
+        srt = torch.sort(s64[b], descending=True).values
+        # the selected set is exact unless ranks k and k+1 are a near tie
+        if not torch.equal(torch.sort(got[b]).values, torch.sort(exp[b]).values):
+            assert k < S and float(srt[k - 1] - srt[k]) <= band, f"row {b}: set differs outside the near-tie band"
+        # the order is score descending up to the same band, lower index first on equal scores
+        sg = s64[b][got[b]]
+        assert bool((sg[:-1] >= sg[1:] - band).all()), f"row {b}: order"
 
 
 def test_csa_indexer_topk_ties_lowest_index(ak):
@@ -148,7 +152,7 @@ def test_hca_compress(ak, dtype):
 
 
 # ------------------------------------------------ fused paged decode path
-def _run_decode(ak, batch, check_rows=None, cluster=0):
+def _run_decode(ak, batch, check_rows=None):
     from aether_kernels.paged import csa_decode_paged, hca_decode_paged
 
     c = batch.cache
@@ -156,10 +160,10 @@ def _run_decode(ak, batch, check_rows=None, cluster=0):
     if batch.kind == "csa":
         out, sel = csa_decode_paged(batch.q, batch.index_q, batch.index_weight, batch.sink, batch.window,
                                     batch.window_len, c, batch.page_table, batch.nblocks, batch.softmax_scale,
-                                    top_k=batch.top_k, err=err, cluster=cluster)
+                                    top_k=batch.top_k, err=err)
     else:
         out = hca_decode_paged(batch.q, batch.sink, batch.window, batch.window_len, c, batch.page_table,
-                               batch.nblocks, batch.softmax_scale, err=err, cluster=cluster)
+                               batch.nblocks, batch.softmax_scale, err=err)
         sel = None
     torch.cuda.synchronize()
     assert int(err.item()) == 0
@@ -204,12 +208,11 @@ def _check_decode(batch, out, sel, rows=None):
 
 
 @pytest.mark.parametrize("bits", [8, 4])
-@pytest.mark.parametrize("cluster", [0, 4, 8])
-def test_csa_decode_small_ragged(ak, bits, cluster):
+def test_csa_decode_small_ragged(ak, bits):
     from aether_kernels.synthetic import make_decode_batch
 
     batch = make_decode_batch("csa", 6, 40, 6000, bits, 4, seed=11 + bits, device="cuda")
-    out, sel = _run_decode(ak, batch, cluster=cluster)
+    out, sel = _run_decode(ak, batch)
     _check_decode(batch, out, sel)
 
 
@@ -288,16 +291,15 @@ def test_csa_decode_exact_ties(ak):
 
 
 @pytest.mark.parametrize("bits", [4, 8])
-@pytest.mark.parametrize("cluster", [0, 8])
-def test_hca_decode(ak, bits, cluster):
+def test_hca_decode(ak, bits):
     """BASELINE config 2 shapes (HCA, 131072 tokens -> 1024 blocks, YaRN 4) at
-    batch 6: the 4-CTA cluster kernel (cluster 0) and the older 8-CTA one."""
+    batch 6."""
     from aether_kernels.rope import RopeConfig
     from aether_kernels.synthetic import make_decode_batch
 
     batch = make_decode_batch("hca", 6, 60000, 131072, bits, 128, seed=5, device="cuda",
                               rope=RopeConfig.yarn(4.0))
-    out, _ = _run_decode(ak, batch, cluster=cluster)
+    out, _ = _run_decode(ak, batch)
     _check_decode(batch, out, None)
 
 
