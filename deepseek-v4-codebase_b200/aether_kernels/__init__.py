@@ -3,6 +3,7 @@ paged TurboQuant KV cache, behind the reference's ``aether_kernels`` API."""
 from .loader import cuda_build_environment, cuda_extension_unavailable_reason, load_aether_cuda_kernels
 from .sparse_attention import sparse_sink_attention
 from .paged import TurboQuantPagedCache, csa_decode_paged, hca_decode_paged
+from .prefix_store import QuantizedPrefixStore
 
 __all__ = [
     "cuda_build_environment",
@@ -12,4 +13,5 @@ __all__ = [
     "TurboQuantPagedCache",
     "csa_decode_paged",
     "hca_decode_paged",
+    "QuantizedPrefixStore",
 ]

@@ -80,6 +80,22 @@ SIGNATURES = {
             _p, _p, _p, _c_int, _p, _p, _c_int, _c_int, _p,  # out, sel, score_out, stride, ws, err, cluster, pdl, stream
         ],
     ),
+    "aether_csa_decode_paged_levels": (
+        _c_int,
+        [
+            _p, _p, _p, _p, _p, _p,            # q, index_q, index_w, sink, window, window_len
+            _p, _p,                            # idx_pages, kv_pages
+            _p, _c_int, _c_int, _p, _c_int,    # page_table, stride, num_pages, nblocks, max_nblocks
+            _p, _p,                            # diag_idx, diag_kv
+            _c_int, _c_int, _c_int, _c_int, _c_int, _c_f,  # B, H, W, bits, top_k, scale
+            _p, _p, _p, _p, _p, _c_int, _p,    # levels, out, sel_out, workspace, err, pdl, stream
+        ],
+    ),
+    "aether_hca_decode_paged_levels": (
+        _c_int,
+        [_p, _p, _p, _p, _p, _p, _c_int, _c_int, _p, _c_int, _p,  # q .. diag_kv
+         _c_int, _c_int, _c_int, _c_int, _c_f, _p, _p, _p, _c_int, _p],  # B, H, W, bits, scale, levels, out, err, pdl, stream
+    ),
     "aether_csa_decode_smem_bytes": (_c_int, [_c_int]),
     "aether_csa_decode_workspace_bytes": (ctypes.c_size_t, [_c_int, _c_int]),
     "aether_csa_decode_set_debug_timer": (None, [_p]),

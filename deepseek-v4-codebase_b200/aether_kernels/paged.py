@@ -36,14 +36,27 @@ INDEX_DIM = 64
 INDEX_HEADS = 4
 
 
-class TurboQuantPagedCache:
-    """Device page pool for one CSA or HCA layer (free-list page allocator)."""
+def _check_codebook(codebook: str) -> str:
+    if codebook not in ("uniform", "lloyd-max"):
+        raise ValueError(f"codebook must be 'uniform' or 'lloyd-max', got {codebook!r}")
+    return codebook
 
-    def __init__(self, num_pages: int, bits: int, device, with_index: bool = True, seed: int = 42):
+
+class TurboQuantPagedCache:
+    """Device page pool for one CSA or HCA layer (free-list page allocator).
+
+    ``codebook`` selects the code format of the pages: "uniform" (the
+    reference's PolarQuant levels) or "lloyd-max" (level indices into the
+    Lloyd-Max N(0, 1) table, ``PolarQuant(bits, codebook="lloyd-max")``); the
+    decode kernels apply the level table themselves."""
+
+    def __init__(self, num_pages: int, bits: int, device, with_index: bool = True, seed: int = 42,
+                 codebook: str = "uniform"):
         if bits not in (4, 8):
             raise ValueError(f"bits must be 4 or 8, got {bits}")
         self.bits = bits
         self.seed = seed
+        self.codebook = _check_codebook(codebook)
         self.num_pages = int(num_pages)
         self.device = torch.device(device)
         self.kv_row = HEAD_DIM * bits // 8
@@ -55,13 +68,13 @@ class TurboQuantPagedCache:
 
     @classmethod
     def from_pools(cls, kv_pages: torch.Tensor, idx_pages: Optional[torch.Tensor], bits: int,
-                   seed: int = 42) -> "TurboQuantPagedCache":
+                   seed: int = 42, codebook: str = "uniform") -> "TurboQuantPagedCache":
         """Wrap existing page pools (e.g. ``PagedKVAllocator.pool('kv')``) without
         copying; page allocation then belongs to whoever owns the pools."""
         if bits not in (4, 8):
             raise ValueError(f"bits must be 4 or 8, got {bits}")
         self = cls.__new__(cls)
-        self.bits, self.seed = bits, seed
+        self.bits, self.seed, self.codebook = bits, seed, _check_codebook(codebook)
         self.kv_row, self.idx_row = HEAD_DIM * bits // 8, INDEX_DIM * bits // 8
         _check(kv_pages.dtype == torch.uint8 and kv_pages.dim() == 2
                and kv_pages.shape[1] == PAGE * self.kv_row + PAGE * 4, "kv_pages must be uint8 [P, page_bytes]")
@@ -126,10 +139,32 @@ class TurboQuantPagedCache:
               index: Optional[torch.Tensor] = None, err: Optional[torch.Tensor] = None) -> None:
         """Quantize ``kv`` [B, n, 128] (and ``index`` [B, n, 64]) and store
         them at logical positions start_pos[b] .. start_pos[b]+n-1."""
+        if self.codebook == "lloyd-max":
+            self._write_levels(page_table, start_pos, kv, self.kv_pages, self.kv_row)
+            if index is not None:
+                _check(self.idx_pages is not None, "this cache has no indexer stream")
+                self._write_levels(page_table, start_pos, index, self.idx_pages, self.idx_row)
+            return
         tq_encode_into_pages(kv, self.bits, page_table, start_pos, self.kv_pages, self.seed, err)
         if index is not None:
             _check(self.idx_pages is not None, "this cache has no indexer stream")
             tq_encode_into_pages(index, self.bits, page_table, start_pos, self.idx_pages, self.seed, err)
+
+    def _write_levels(self, page_table, start_pos, x, pool, row):
+        """Lloyd-Max format: encode densely, then scatter the rows to their
+        page slots (a cache build step, not the decode path)."""
+        from .ops import tq_encode_lut
+
+        _check(x.dim() == 3, "x must have shape [B, n, D]")
+        B, n, _ = x.shape
+        if n == 0:
+            return
+        codes, scale = tq_encode_lut(x.contiguous(), self.bits, self.seed)
+        pos = start_pos.long().view(B, 1) + torch.arange(n, device=x.device).view(1, n)
+        page = page_table.long().gather(1, pos // PAGE)
+        slot = pos % PAGE
+        self._codes(pool, row)[page, slot] = codes
+        self._scales(pool, row)[page, slot] = scale.squeeze(-1)
 
 
     # ---------------------------------------------------- compress-on-emit
@@ -139,6 +174,7 @@ class TurboQuantPagedCache:
         """Finish one HCA block per sequence (aether_2b/serving.py:495-505):
         buffer_c / buffer_z [B, 128, 128] (bias already in z), entry written
         at logical position slot_pos[b]; one kernel launch."""
+        _check(self.codebook == "uniform", "compress-on-emit writes the uniform code format")
         compress_emit(buffer_c, buffer_z, positions=positions, inv_freq=inv_freq, norm_weight=norm_weight,
                       norm_eps=norm_eps, bits=self.bits, page_table=page_table, slot_pos=slot_pos,
                       page_pool=self.kv_pages, seed=self.seed, want_out=False, err=err)
@@ -153,6 +189,7 @@ class TurboQuantPagedCache:
         sequence's first block).  Main entries get RoPE at ``positions`` and
         RMSNorm, index entries neither; two kernel launches."""
         _check(self.idx_pages is not None, "this cache has no indexer stream")
+        _check(self.codebook == "uniform", "compress-on-emit writes the uniform code format")
         a_c, a_z, ba, b_c, b_z, bb = main
         compress_emit(a_c, a_z, ba, b_c, b_z, bb, has_prev, positions=positions, inv_freq=inv_freq,
                       norm_weight=norm_weight, norm_eps=norm_eps, bits=self.bits, page_table=page_table,
@@ -248,6 +285,15 @@ def csa_decode_paged(
         workspace = torch.zeros(max(need, 16), dtype=torch.uint8, device=dev)
     _check(workspace.is_cuda and workspace.numel() * workspace.element_size() >= need,
            f"workspace must hold {need} bytes")
+    if getattr(cache, "codebook", "uniform") == "lloyd-max":
+        from .codebook import device_codebook
+
+        _check(scores is None and rope_inv_freq is None,
+               "a Lloyd-Max cache decodes without score output or fused output RoPE")
+        lv, _ = device_codebook(cache.bits, dev)
+        _lib.call("aether_csa_decode_paged_levels", *common[:21], lv.data_ptr(), *common[21:], workspace.data_ptr(),
+                  _opt_ptr(err), int(overlap_prefetch), _stream(dev))
+        return out, indices
     if rope_inv_freq is not None:
         _check(scores is None, "the fused output RoPE does not write scores")
         _cuda(rope_positions, "rope_positions")
@@ -506,12 +552,16 @@ def hca_decode_paged(
     dev = q.device
     if out is None:
         out = torch.empty(B, H, D, dtype=torch.bfloat16, device=dev)
-    _lib.call(
-        "aether_hca_decode_paged",
-        q.data_ptr(), sink.data_ptr(), window.data_ptr(), window_len.data_ptr(), cache.kv_pages.data_ptr(),
-        page_table.data_ptr(), page_table.shape[1], cache.num_pages, nblocks.data_ptr(),
-        page_table.shape[1] * PAGE, rademacher_diag(HEAD_DIM, cache.seed, dev).data_ptr(),
-        B, H, window.shape[1], cache.bits, float(softmax_scale), out.data_ptr(), _opt_ptr(err), 0,
-        int(overlap_prefetch), _stream(dev),
-    )
+    head = (q.data_ptr(), sink.data_ptr(), window.data_ptr(), window_len.data_ptr(), cache.kv_pages.data_ptr(),
+            page_table.data_ptr(), page_table.shape[1], cache.num_pages, nblocks.data_ptr(),
+            page_table.shape[1] * PAGE, rademacher_diag(HEAD_DIM, cache.seed, dev).data_ptr(),
+            B, H, window.shape[1], cache.bits, float(softmax_scale))
+    if getattr(cache, "codebook", "uniform") == "lloyd-max":
+        from .codebook import device_codebook
+
+        lv, _ = device_codebook(cache.bits, dev)
+        _lib.call("aether_hca_decode_paged_levels", *head, lv.data_ptr(), out.data_ptr(), _opt_ptr(err),
+                  int(overlap_prefetch), _stream(dev))
+        return out
+    _lib.call("aether_hca_decode_paged", *head, out.data_ptr(), _opt_ptr(err), 0, int(overlap_prefetch), _stream(dev))
     return out

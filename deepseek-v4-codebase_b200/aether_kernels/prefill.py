@@ -55,6 +55,7 @@ def csa_prefill_topk(index_q: torch.Tensor, index_weight: torch.Tensor, cache: T
     _cuda(index_q, "index_q")
     _cuda(index_weight, "index_weight")
     _cuda(page_table, "page_table")
+    _check(getattr(cache, "codebook", "uniform") == "uniform", "chunked prefill reads the uniform code format")
     _check(index_q.dtype == torch.float32 and index_weight.dtype == torch.float32,
            "index_q and index_weight must be float32")
     Q = index_q.shape[0]

@@ -31,8 +31,11 @@ class PolarQuant:
 
     ``codebook="lloyd-max"`` (not in the reference) selects the Lloyd-Max
     level format for N(0, 1) instead of the uniform levels: codes are level
-    indices (uint8 [..., D], or index nibbles [..., D/2]).  The fused paged
-    decode kernels read the uniform format only.
+    indices (uint8 [..., D], or index nibbles [..., D/2]).  A
+    ``TurboQuantPagedCache(..., codebook="lloyd-max")`` holds pages in this
+    format and the fused paged decode kernels apply the level table
+    themselves (the prefill indexer and compress-on-emit write / read the
+    uniform format only).
     """
 
     def __init__(self, bits: int, seed: int = 42, codebook: str = "uniform") -> None:

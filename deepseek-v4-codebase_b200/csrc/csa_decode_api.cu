@@ -15,7 +15,7 @@ namespace aether {
 int hca_decode_cta(const void* q, const float* sink, const void* window, const int32_t* window_len,
                    const uint8_t* kv_pages, const int32_t* page_table, int table_stride, int num_pages,
                    const int32_t* nblocks, int max_nblocks, const float* diag_kv, int B, int H, int W, int bits,
-                   float softmax_scale, void* out, int* err, int pdl, void* stream);
+                   float softmax_scale, void* out, int* err, int pdl, void* stream, const float* levels = nullptr);
 int csa_decode_cta(const void* q, const float* index_q, const float* index_w, const float* sink, const void* window,
                    const int32_t* window_len, const uint8_t* idx_pages, const uint8_t* kv_pages,
                    const int32_t* page_table, int table_stride, int num_pages, const int32_t* nblocks,
@@ -23,7 +23,8 @@ int csa_decode_cta(const void* q, const float* index_q, const float* index_w, co
                    int top_k, float softmax_scale, void* out, int32_t* sel_out, float* score_out, int score_stride,
                    uint32_t* workspace, int* err, int pdl, void* stream,
                    const int32_t* rope_pos = nullptr, const float* rope_inv_freq = nullptr,
-                   int rope_dim = 0, const uint32_t* step_flags = nullptr, uint32_t step_seq = 0);
+                   int rope_dim = 0, const uint32_t* step_flags = nullptr, uint32_t step_seq = 0,
+                   const float* levels = nullptr);
 
 }  // namespace aether
 
@@ -326,6 +327,37 @@ int aether_csa_decode_paged_scores(const void* q, const float* index_q, const fl
   return csa_decode_cta(q, index_q, index_w, sink, window, window_len, idx_pages, kv_pages, page_table, table_stride,
                         num_pages, nblocks, max_nblocks, diag_idx, diag_kv, B, H, W, bits, top_k, softmax_scale, out,
                         sel_out, score_out, score_stride, workspace, err, pdl, stream);
+}
+
+
+// aether_csa_decode_paged for a cache in the Lloyd-Max level format: codes
+// are indices into levels [2^bits] (fp32), entries levels[c] * scale in the
+// rotated domain.  The level table is applied inside the score and attend
+// kernels (no dequantized copy of the cache).
+int aether_csa_decode_paged_levels(const void* q, const float* index_q, const float* index_w, const float* sink,
+                                   const void* window, const int32_t* window_len, const uint8_t* idx_pages,
+                                   const uint8_t* kv_pages, const int32_t* page_table, int table_stride,
+                                   int num_pages, const int32_t* nblocks, int max_nblocks, const float* diag_idx,
+                                   const float* diag_kv, int B, int H, int W, int bits, int top_k,
+                                   float softmax_scale, const float* levels, void* out, int32_t* sel_out,
+                                   uint32_t* workspace, int* err, int pdl, void* stream) {
+  AETHER_REQUIRE(index_q && index_w && idx_pages && diag_idx, "csa_decode_paged: null index input");
+  AETHER_REQUIRE(levels, "csa_decode_paged_levels: null level table");
+  return csa_decode_cta(q, index_q, index_w, sink, window, window_len, idx_pages, kv_pages, page_table,
+                        table_stride, num_pages, nblocks, max_nblocks, diag_idx, diag_kv, B, H, W, bits, top_k,
+                        softmax_scale, out, sel_out, nullptr, 0, workspace, err, pdl, stream, nullptr, nullptr, 0,
+                        nullptr, 0, levels);
+}
+
+// aether_hca_decode_paged for a cache in the Lloyd-Max level format.
+int aether_hca_decode_paged_levels(const void* q, const float* sink, const void* window, const int32_t* window_len,
+                                   const uint8_t* kv_pages, const int32_t* page_table, int table_stride,
+                                   int num_pages, const int32_t* nblocks, int max_nblocks, const float* diag_kv,
+                                   int B, int H, int W, int bits, float softmax_scale, const float* levels,
+                                   void* out, int* err, int pdl, void* stream) {
+  AETHER_REQUIRE(levels, "hca_decode_paged_levels: null level table");
+  return hca_decode_cta(q, sink, window, window_len, kv_pages, page_table, table_stride, num_pages, nblocks,
+                        max_nblocks, diag_kv, B, H, W, bits, softmax_scale, out, err, pdl, stream, levels);
 }
 
 }  // extern "C"

@@ -114,9 +114,15 @@ struct SCfg {
   static constexpr int OFF_MISC = OFF_LIMB + kIdxHeads * 3 * kIdxDim;
   static constexpr int OFF_BAR = OFF_MISC + 128;
   static constexpr int SMEM = OFF_BAR + 16;
+  // codebook caches (csa_score_levels_kernel): rotated query fp32 [4][64],
+  // level table fp32 [2^BITS]
+  static constexpr int OFF_QROT = SMEM;
+  static constexpr int OFF_LV = OFF_QROT + kIdxHeads * kIdxDim * 4;
+  static constexpr int SMEM_LEVELS = OFF_LV + 256 * 4;
 };
 
 struct QParams {
+  const float* levels;  // Lloyd-Max level table [2^bits] (codebook caches), or null (uniform codes)
   const __nv_bfloat16* q;
   const float* index_q;
   const float* index_w;
@@ -406,6 +412,100 @@ __global__ void __launch_bounds__(kSThreads) csa_score_kernel(QParams p, int spl
   stamp(4);
 }
 
+// Score kernel for caches in the Lloyd-Max level format: a key's rotated
+// entries are levels[c] * scale, so q_h . k_s = scale_s * (WHT(diag * q_h) .
+// levels[c_s]) (aether_2b/modeling.py:609-611 with the keys decoded as
+// levels, not integers).  The exact integer limb MMAs of csa_score_kernel do
+// not apply to non-integer levels: fp32 FMAs instead, one index head per
+// lane, the four heads of a key on the four lanes of a quad.  The same CTA
+// shape, staging and key format as csa_score_kernel.
+template <int BITS>
+__global__ void __launch_bounds__(kSThreads) csa_score_levels_kernel(QParams p, int splits) {
+  using C = SCfg<BITS>;
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int b = blockIdx.x / splits, sp = blockIdx.x % splits;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (p.step_flags) {  // this step's inputs are copied on another stream
+    if (tid == 0) flag_wait(p.step_flags, p.step_seq, p.err);
+    __syncthreads();
+  }
+  pdl_launch_dependents();
+  int nb = p.nblocks[b];
+  nb = max(0, min(nb, min(kMaxBlocks, p.table_stride * kPage)));
+  const int npages = (nb + kPage - 1) / kPage;
+  const int pg0 = sp * C::PPC;
+  if (pg0 >= npages) return;
+  const int np = min(C::PPC, npages - pg0);
+  float* qrot = reinterpret_cast<float*>(smem + C::OFF_QROT);
+  float* lv = reinterpret_cast<float*>(smem + C::OFF_LV);
+  float* alpha = reinterpret_cast<float*>(smem + C::OFF_MISC);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+  if (tid == 0) {
+    mbar_init(bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (warp == 0) {  // the pages are cache state: staged before the wait
+    if (lane == 0) mbar_expect_tx(bar, np * C::PB_IDX);
+    __syncwarp();
+    if (lane < np) {
+      int phys = p.page_table[static_cast<long long>(b) * p.table_stride + pg0 + lane];
+      if (phys < 0 || phys >= p.num_pages) {
+        report_error(p.err, kErrBadPage);
+        phys = 0;
+      }
+      bulk_g2s(smem + lane * C::PB_IDX, p.idx_pages + static_cast<long long>(phys) * C::PB_IDX, C::PB_IDX, bar);
+    }
+  }
+  pdl_wait();
+  if (tid < (1 << BITS)) lv[tid] = p.levels[tid];
+  if (warp < kIdxHeads) {
+    float v0, v1;
+    rotate_index_query(p.index_q, p.diag_idx, b, warp, lane, v0, v1);
+    qrot[warp * kIdxDim + 2 * lane] = v0;
+    qrot[warp * kIdxDim + 2 * lane + 1] = v1;
+    if (lane == 0) alpha[warp] = softplus_f(p.index_w[b * kIdxHeads + warp]);
+  }
+  __syncthreads();
+  const int h = lane & 3;
+  float qr[kIdxDim];
+#pragma unroll
+  for (int d = 0; d < kIdxDim; ++d) qr[d] = qrot[h * kIdxDim + d];
+  const float a_h = alpha[h];
+  mbar_wait(bar, 0, p.err);
+  uint32_t* out = p.ws + static_cast<long long>(b) * p.ws_stride;
+  // a quad per key: every pass covers 64 keys, so every lane of a quad runs
+  // the same passes
+  for (int key = tid >> 2; key < np * kPage; key += kSThreads / 4) {
+    const uint8_t* page = smem + (key >> 6) * C::PB_IDX;
+    const int slot = key & 63;
+    const uint8_t* row = page + slot * C::RB_IDX;
+    float dot = 0.f;
+#pragma unroll
+    for (int c = 0; c < C::RB_IDX; c += 4) {
+      const uint32_t w = *reinterpret_cast<const uint32_t*>(row + c);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const uint32_t byte = (w >> (8 * e)) & 0xFFu;
+        if (BITS == 4) {
+          dot = fmaf(qr[2 * (c + e)], lv[byte & 15u], dot);
+          dot = fmaf(qr[2 * (c + e) + 1], lv[byte >> 4], dot);
+        } else {
+          dot = fmaf(qr[c + e], lv[byte], dot);
+        }
+      }
+    }
+    float sc = a_h * fmaxf(dot, 0.f);
+    sc += __shfl_xor_sync(0xffffffffu, sc, 1);
+    sc += __shfl_xor_sync(0xffffffffu, sc, 2);
+    const int gk = (pg0 + (key >> 6)) * kPage + slot;
+    if (h == 0 && gk < nb) {
+      const float ks = reinterpret_cast<const float*>(page + kPage * C::RB_IDX)[slot];
+      out[gk] = __float_as_uint(__fadd_rn(__fmul_rn(sc, ks), 0.0f)) + 1u;  // order-preserving key
+    }
+  }
+}
+
 template <int BITS, int CS>
 __global__ void __launch_bounds__(kQThreads, CS > 1 ? 2 : 1) csa_attend_kernel(QParams p) {
   using C = QCfg<BITS, CS>;
@@ -435,7 +535,7 @@ __global__ void __launch_bounds__(kQThreads, CS > 1 ? 2 : 1) csa_attend_kernel(Q
   uint32_t* wtot = reinterpret_cast<uint32_t*>(smem + C::OFF_SCAN);
   QMisc* misc = reinterpret_cast<QMisc*>(smem + C::OFF_MISC);
   uint32_t* lut = reinterpret_cast<uint32_t*>(smem + C::OFF_LUT);
-  if (BITS == 4 && tid < 256) lut[tid] = nib_byte_to_h2(static_cast<uint32_t>(tid));
+  if ((BITS == 4 || p.levels) && tid < 256) lut[tid] = code_lut_entry(BITS, p.levels, static_cast<uint32_t>(tid));
 
   // ------------------------------------------------------------ prologue
   int nb = p.nblocks[b];  // blocks of sequence b held on this device
@@ -802,8 +902,9 @@ __global__ void __launch_bounds__(kQThreads, CS > 1 ? 2 : 1) csa_attend_kernel(Q
         o = make_uint4(lut[w & 0xFFu], lut[(w >> 8) & 0xFFu], lut[(w >> 16) & 0xFFu], lut[w >> 24]);
       } else {
         const uint2 w = *reinterpret_cast<const uint2*>(raw + row * C::RAWS + c8);
-        o = make_uint4(s8pair_to_h2(w.x & 0xFFFFu), s8pair_to_h2(w.x >> 16), s8pair_to_h2(w.y & 0xFFFFu),
-                       s8pair_to_h2(w.y >> 16));
+        const bool lv = p.levels != nullptr;
+        o = make_uint4(code8_pair(w.x, lut, lv), code8_pair(w.x >> 16, lut, lv), code8_pair(w.y, lut, lv),
+                       code8_pair(w.y >> 16, lut, lv));
       }
     } else if ((i & 15) == 0) {
       ks[row] = 0.f;
@@ -1047,6 +1148,7 @@ struct HCfg {
 };
 
 struct HcaParams {
+  const float* levels;          // Lloyd-Max level table [2^bits], or null (uniform codes)
   const __nv_bfloat16* q;       // [B, H, 128]
   const float* sink;            // [H]
   const __nv_bfloat16* window;  // [B, W, 128]
@@ -1126,7 +1228,7 @@ __global__ void __launch_bounds__(kQThreads, 1) hca_attend_kernel(HcaParams p) {
       bulk_g2s(raw + lane * C::PB_KV, p.kv_pages + static_cast<long long>(phys) * C::PB_KV, C::PB_KV, bar + lane);
     }
   }
-  if (BITS == 4 && tid < 256) lut[tid] = nib_byte_to_h2(static_cast<uint32_t>(tid));
+  if ((BITS == 4 || p.levels) && tid < 256) lut[tid] = code_lut_entry(BITS, p.levels, static_cast<uint32_t>(tid));
   // window rows other than the newest are cache state
   const long long wbase = static_cast<long long>(b) * W;
   {
@@ -1156,8 +1258,9 @@ __global__ void __launch_bounds__(kQThreads, 1) hca_attend_kernel(HcaParams p) {
           o = make_uint4(lut[w & 0xFFu], lut[(w >> 8) & 0xFFu], lut[(w >> 16) & 0xFFu], lut[w >> 24]);
         } else {
           const uint2 w = *reinterpret_cast<const uint2*>(src + prow * C::RB_KV + c8);
-          o = make_uint4(s8pair_to_h2(w.x & 0xFFFFu), s8pair_to_h2(w.x >> 16), s8pair_to_h2(w.y & 0xFFFFu),
-                         s8pair_to_h2(w.y >> 16));
+          const bool lv = p.levels != nullptr;
+          o = make_uint4(code8_pair(w.x, lut, lv), code8_pair(w.x >> 16, lut, lv), code8_pair(w.y, lut, lv),
+                         code8_pair(w.y >> 16, lut, lv));
         }
       }
       if ((i & 15) == 0)
@@ -1381,6 +1484,9 @@ static int set_smem_attrs() {
   int rc = ensure_smem_attr(reinterpret_cast<const void*>(csa_score_kernel<BITS>), SCfg<BITS>::SMEM,
                             "csa_decode (score)");
   if (!rc)
+    rc = ensure_smem_attr(reinterpret_cast<const void*>(csa_score_levels_kernel<BITS>), SCfg<BITS>::SMEM_LEVELS,
+                          "csa_decode (score, level table)");
+  if (!rc)
     rc = ensure_smem_attr(reinterpret_cast<const void*>(csa_attend_kernel<BITS, 1>), QCfg<BITS, 1>::SMEM,
                           "csa_decode (select)");
   if (!rc)
@@ -1402,11 +1508,14 @@ static int launch_score(const QParams& p, int B, int max_nblocks, bool pdl, cuda
   cudaLaunchConfig_t c = {};
   c.gridDim = dim3(B * splits);
   c.blockDim = dim3(kSThreads);
-  c.dynamicSmemBytes = CA::SMEM;
+  c.dynamicSmemBytes = p.levels ? CA::SMEM_LEVELS : CA::SMEM;
   c.stream = st;
   c.attrs = at;
   c.numAttrs = pdl ? 1 : 0;
-  AETHER_CUDA_TRY(cudaLaunchKernelEx(&c, csa_score_kernel<BITS>, p, splits), "csa_decode: launch (score)");
+  if (p.levels)
+    AETHER_CUDA_TRY(cudaLaunchKernelEx(&c, csa_score_levels_kernel<BITS>, p, splits), "csa_decode: launch (score)");
+  else
+    AETHER_CUDA_TRY(cudaLaunchKernelEx(&c, csa_score_kernel<BITS>, p, splits), "csa_decode: launch (score)");
   return 0;
 }
 
@@ -1537,7 +1646,7 @@ static int run_decode(QParams p, int B, int max_nblocks, bool pdl, cudaStream_t 
 int hca_decode_cta(const void* q, const float* sink, const void* window, const int32_t* window_len,
                    const uint8_t* kv_pages, const int32_t* page_table, int table_stride, int num_pages,
                    const int32_t* nblocks, int max_nblocks, const float* diag_kv, int B, int H, int W, int bits,
-                   float softmax_scale, void* out, int* err, int pdl, void* stream) {
+                   float softmax_scale, void* out, int* err, int pdl, void* stream, const float* levels) {
   AETHER_REQUIRE(bits == 4 || bits == 8, "bits must be 4 or 8, got %d", bits);
   AETHER_REQUIRE(H >= 1 && H <= kMaxHeads, "num_heads must be in [1, %d], got %d", kMaxHeads, H);
   AETHER_REQUIRE(W >= 0 && W <= kWinMax, "window capacity must be in [0, %d], got %d", kWinMax, W);
@@ -1549,6 +1658,7 @@ int hca_decode_cta(const void* q, const float* sink, const void* window, const i
                  "hca decode: null argument");
   if (B == 0) return 0;
   HcaParams p{};
+  p.levels = levels;
   p.q = static_cast<const __nv_bfloat16*>(q);
   p.sink = sink;
   p.window = static_cast<const __nv_bfloat16*>(window);
@@ -1592,7 +1702,8 @@ int csa_decode_cta(const void* q, const float* index_q, const float* index_w, co
                    int max_nblocks, const float* diag_idx, const float* diag_kv, int B, int H, int W, int bits,
                    int top_k, float softmax_scale, void* out, int32_t* sel_out, float* score_out, int score_stride,
                    uint32_t* workspace, int* err, int pdl, void* stream, const int32_t* rope_pos,
-                   const float* rope_inv_freq, int rope_dim, const uint32_t* step_flags, uint32_t step_seq) {
+                   const float* rope_inv_freq, int rope_dim, const uint32_t* step_flags, uint32_t step_seq,
+                   const float* levels) {
   int rc = check_common(bits, H, W, top_k, max_nblocks, table_stride, num_pages);
   AETHER_REQUIRE(!rope_inv_freq || (rope_pos && rope_dim > 0 && rope_dim <= kHeadDim && rope_dim % 4 == 0),
                  "csa decode: output RoPE needs positions and rope_dim in (0, 128], a multiple of 4");
@@ -1611,6 +1722,7 @@ int csa_decode_cta(const void* q, const float* index_q, const float* index_w, co
   p.rope_dim = rope_dim;
   p.step_flags = step_flags;
   p.step_seq = step_seq;
+  p.levels = levels;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   rc = bits == 4 ? run_decode<4>(p, B, max_nblocks, pdl != 0, st, reinterpret_cast<uint8_t*>(workspace))
                  : run_decode<8>(p, B, max_nblocks, pdl != 0, st, reinterpret_cast<uint8_t*>(workspace));

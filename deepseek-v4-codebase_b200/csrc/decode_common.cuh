@@ -52,6 +52,21 @@ __device__ __forceinline__ void mma_bf16(float (&c)[4], const uint32_t (&a)[4], 
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
+// Entry `i` of the shared code LUT: uniform 4-bit codes map a byte to the
+// half2 of its two signed nibbles; a level table (Lloyd-Max format) maps a
+// 4-bit byte to half2(levels[lo], levels[hi]) and an 8-bit code to
+// half(levels[i]) in the low half.  Uniform 8-bit codes convert
+// arithmetically (s8pair_to_h2) and need no entry.
+__device__ __forceinline__ uint32_t code_lut_entry(int bits, const float* levels, uint32_t i) {
+  if (levels) return bits == 4 ? pack_half2(levels[i & 15u], levels[i >> 4]) : pack_half2(levels[i], 0.f);
+  return nib_byte_to_h2(i);
+}
+// two 8-bit codes (low 16 bits of w) -> half2, uniform or through the LUT
+__device__ __forceinline__ uint32_t code8_pair(uint32_t w, const uint32_t* lut, bool levels) {
+  if (!levels) return s8pair_to_h2(w & 0xFFFFu);
+  return (lut[w & 0xFFu] & 0xFFFFu) | (lut[(w >> 8) & 0xFFu] << 16);
+}
+
 // In-warp normalised 128-point WHT of 4 consecutive values per lane (unscaled).
 __device__ __forceinline__ void warp_wht128(float (&v)[4], int lane) {
   {
@@ -75,13 +90,13 @@ __device__ __forceinline__ void warp_wht128(float (&v)[4], int lane) {
 
 // Rotated index query of head `warp` (warps 0-3): 24-bit limbs into `limb`,
 // their per-limb sums and alpha_h = softplus(w_h) * scale_h into misc.
-__device__ __forceinline__ void index_query_limbs(const float* index_q, const float* index_w, const float* diag_idx,
-                                                  int b, int warp, int lane, int8_t* limb, float* alpha,
-                                                  int (*lsum)[3]) {
-  const int h = warp;
+// Rotated index query of head h, WHT(diag * q_h) with the normalised
+// 64-point WHT: lane l holds dims 2l and 2l + 1 (in-warp butterfly).
+__device__ __forceinline__ void rotate_index_query(const float* index_q, const float* diag_idx, int b, int h,
+                                                   int lane, float& v0, float& v1) {
   const float* src = index_q + (static_cast<long long>(b) * kIdxHeads + h) * kIdxDim;
-  float v0 = src[lane * 2] * diag_idx[lane * 2];
-  float v1 = src[lane * 2 + 1] * diag_idx[lane * 2 + 1];
+  v0 = src[lane * 2] * diag_idx[lane * 2];
+  v1 = src[lane * 2 + 1] * diag_idx[lane * 2 + 1];
   {
     const float a = v0, c2 = v1;
     v0 = a + c2;
@@ -97,6 +112,14 @@ __device__ __forceinline__ void index_query_limbs(const float* index_q, const fl
   }
   v0 *= 0.125f;
   v1 *= 0.125f;
+}
+
+__device__ __forceinline__ void index_query_limbs(const float* index_q, const float* index_w, const float* diag_idx,
+                                                  int b, int warp, int lane, int8_t* limb, float* alpha,
+                                                  int (*lsum)[3]) {
+  const int h = warp;
+  float v0, v1;
+  rotate_index_query(index_q, diag_idx, b, h, lane, v0, v1);
   const float am = warp_max(fmaxf(fabsf(v0), fabsf(v1)));
   const float s = am > 0.f ? am / 8355000.0f : 1.0f;
   int ls[3] = {0, 0, 0};

@@ -166,6 +166,30 @@ int aether_csa_decode_paged_rope(const void* q, const float* index_q, const floa
                                  int32_t* sel_out, uint32_t* workspace, int* err, int pdl, const int32_t* rope_pos,
                                  const float* rope_inv_freq, int rope_dim, void* stream);
 
+/* As aether_csa_decode_paged (cluster 0) for a cache in the Lloyd-Max level
+ * format (PolarQuant(bits, codebook="lloyd-max")): codes are indices into
+ * levels [2^bits] fp32 (4-bit: index nibbles, even element in the low
+ * nibble), an entry is levels[code] * scale in the rotated domain.  The level
+ * table is applied inside the kernels: the index scores in fp32 (the exact
+ * integer limb MMAs need integer codes), the attention through its code LUT.
+ * Not in the reference (its PolarQuant has uniform levels only,
+ * aether_2b/turbo_quant.py:150-166). */
+int aether_csa_decode_paged_levels(const void* q, const float* index_q, const float* index_w, const float* sink,
+                                   const void* window, const int32_t* window_len, const uint8_t* idx_pages,
+                                   const uint8_t* kv_pages, const int32_t* page_table, int table_stride,
+                                   int num_pages, const int32_t* nblocks, int max_nblocks, const float* diag_idx,
+                                   const float* diag_kv, int B, int H, int W, int bits, int top_k,
+                                   float softmax_scale, const float* levels, void* out, int32_t* sel_out,
+                                   uint32_t* workspace, int* err, int pdl, void* stream);
+
+/* As aether_hca_decode_paged (cluster 0) for a cache in the Lloyd-Max level
+ * format (see aether_csa_decode_paged_levels). */
+int aether_hca_decode_paged_levels(const void* q, const float* sink, const void* window, const int32_t* window_len,
+                                   const uint8_t* kv_pages, const int32_t* page_table, int table_stride,
+                                   int num_pages, const int32_t* nblocks, int max_nblocks, const float* diag_kv,
+                                   int B, int H, int W, int bits, float softmax_scale, const float* levels,
+                                   void* out, int* err, int pdl, void* stream);
+
 /* As aether_csa_decode_paged, also writing each visible block's index score
  * to score_out[b * score_stride + block]. */
 int aether_csa_decode_paged_scores(const void* q, const float* index_q, const float* index_w, const float* sink,

@@ -75,22 +75,28 @@ class DecodeResult:
 def decode_step(kind: str, q, index_q, index_weight, sink, window, window_len, idx_codes, idx_scale, kv_codes,
                 kv_scale, page_table, nblocks, bits: int, top_k: int, softmax_scale: float, seed: int = 42,
                 tie_tol: float = 1e-5, use_selection: Optional[List[torch.Tensor]] = None,
-                classify_ties: bool = True) -> DecodeResult:
+                classify_ties: bool = True, levels: Optional[torch.Tensor] = None) -> DecodeResult:
     """All tensors on the CPU.  ``use_selection`` replaces the oracle's top-k
     by a given per-row selection (to check attention on a near-tie row);
-    ``classify_ties=False`` skips the fp64 near-tie bookkeeping (timing)."""
+    ``classify_ties=False`` skips the fp64 near-tie bookkeeping (timing);
+    ``levels`` decodes a cache in the Lloyd-Max level format
+    (``oracle.turboquant.decode_lut``) instead of the uniform one."""
     B, H, D = q.shape
+
+    def dec(codes, scale):
+        if levels is None:
+            return tq.decode(codes, scale, bits, seed)
+        return tq.decode_lut(codes, scale, bits, levels, seed)
+
     outs, sels, ties = [], [], []
     for b in range(B):
         nb = int(nblocks[b])
         wl = int(window_len[b])
         table = page_table[b]
-        main = tq.decode(gather_pages(kv_codes, table, nb), gather_pages(kv_scale, table, nb).unsqueeze(-1), bits,
-                         seed)
+        main = dec(gather_pages(kv_codes, table, nb), gather_pages(kv_scale, table, nb).unsqueeze(-1))
         tie = False
         if kind == "csa":
-            keys = tq.decode(gather_pages(idx_codes, table, nb), gather_pages(idx_scale, table, nb).unsqueeze(-1),
-                             bits, seed)
+            keys = dec(gather_pages(idx_codes, table, nb), gather_pages(idx_scale, table, nb).unsqueeze(-1))
             k = min(top_k, nb)
             if use_selection is not None:
                 sel = use_selection[b].long()
