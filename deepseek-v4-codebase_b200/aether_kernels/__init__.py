@@ -4,6 +4,7 @@ from .loader import cuda_build_environment, cuda_extension_unavailable_reason, l
 from .sparse_attention import sparse_sink_attention
 from .paged import TurboQuantPagedCache, csa_decode_paged, hca_decode_paged
 from .prefix_store import QuantizedPrefixStore
+from .engine import AttentionLayerSpec, DecodeRound
 
 __all__ = [
     "cuda_build_environment",
@@ -14,4 +15,6 @@ __all__ = [
     "csa_decode_paged",
     "hca_decode_paged",
     "QuantizedPrefixStore",
+    "AttentionLayerSpec",
+    "DecodeRound",
 ]
