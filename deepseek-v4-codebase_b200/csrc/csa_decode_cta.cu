@@ -1860,40 +1860,6 @@ extern "C" int aether_csa_attend_candidates(const void* q, const float* sink, co
   return check_launch("csa_attend_candidates");
 }
 
-// Chunked prefill attention: query b attends its candidate list (the exact
-// top-k of aether_csa_prefill_topk) plus its causal window, reading
-// page-table row q_row[b] and window rows win_row[b] .. + window_len[b] - 1 of
-// a flat [rows][128] bf16 buffer.
-extern "C" int aether_csa_prefill_attend(const void* q, const float* sink, const void* window,
-                                         const long long* win_row, const int32_t* window_len, const uint8_t* kv_pages,
-                                         const int32_t* page_table, int table_stride, int num_pages,
-                                         const int32_t* q_row, const int32_t* nblocks, int max_nblocks,
-                                         const float* diag_kv, const uint32_t* cand_keys, const int32_t* cand_ids,
-                                         int cand_stride, int B, int H, int bits, int top_k, float softmax_scale,
-                                         void* out, int32_t* sel_out, int* err, void* stream) {
-  int rc = check_common(bits, H, kWinMax, top_k, max_nblocks, table_stride, num_pages);
-  if (rc) return rc;
-  AETHER_REQUIRE(cand_keys && cand_ids && win_row && q_row, "csa_prefill_attend: null argument");
-  AETHER_REQUIRE(cand_stride >= top_k && (cand_stride & 3) == 0,
-                 "csa_prefill_attend: cand_stride must be >= top_k and a multiple of 4");
-  if (B == 0) return 0;
-  QParams p = base_params(q, nullptr, nullptr, sink, window, window_len, nullptr, kv_pages, page_table, table_stride,
-                          num_pages, nblocks, max_nblocks, nullptr, diag_kv, H, kWinMax, top_k, softmax_scale, err);
-  p.out = static_cast<__nv_bfloat16*>(out);
-  p.sel_out = sel_out;
-  p.cand_keys = cand_keys;
-  p.cand_ids = cand_ids;
-  p.cand_n = top_k;
-  p.cand_stride = cand_stride;
-  p.q_row = q_row;
-  p.win_row = win_row;
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  rc = bits == 4 ? set_smem_attrs<4>() : set_smem_attrs<8>();
-  if (!rc) rc = bits == 4 ? launch_attend<4>(p, B, false, st) : launch_attend<8>(p, B, false, st);
-  if (rc) return rc;
-  return check_launch("csa_prefill_attend");
-}
-
 // Combine G partial attention results (from aether_csa_attend_candidates on
 // G devices, gathered as part_o [G][B][H][128], part_ml [G][B][H][2]) with the
 // per-head sink into the bf16 output [B][H][128].

@@ -330,7 +330,8 @@ int aether_csa_prefill_topk(const float* index_q, const float* index_w, const ui
  * nblocks[b] (<= max_nblocks); window rows win_row[b] .. win_row[b] +
  * window_len[b] - 1 (oldest first, window_len <= 128) of the flat bf16
  * buffer window [rows][128].  out [B][H][128] bf16 (before the inverse output
- * RoPE); sel_out [B][top_k] (optional) the attended block ids. */
+ * RoPE); sel_out [B][top_k] (optional) the attended block ids.  Runs as one
+ * persistent CTA per SM on the tcgen05 tensor cores (top_k <= 256, H <= 16). */
 int aether_csa_prefill_attend(const void* q, const float* sink, const void* window, const long long* win_row,
                               const int32_t* window_len, const uint8_t* kv_pages, const int32_t* page_table,
                               int table_stride, int num_pages, const int32_t* q_row, const int32_t* nblocks,

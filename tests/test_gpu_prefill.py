@@ -220,3 +220,62 @@ def test_prefill_config4_shape(lib):
     assert mism <= len(rows) // 100
     assert worst < 2e-2, worst
     assert total / n < 1e-3, total / n
+
+
+@pytest.mark.parametrize("bits,H,top_k", [(4, 5, 256), (8, 16, 64)])
+def test_prefill_attention_sequence_start(lib, bits, H, top_k):
+    """Query tokens from position 0: the first tokens see no compressed
+    block (an empty candidate list) and windows shorter than 128 rows; later
+    ones see fewer than top_k blocks.  Odd head counts and a short top-k."""
+    from aether_kernels.prefill import PrefillRequest, csa_prefill_chunk
+    from aether_kernels.synthetic import make_decode_batch
+    from oracle import decode as odec
+    from oracle import turboquant as otq
+
+    batch = make_decode_batch("csa", 2, 1200, 1600, bits, 4, seed=90 + bits, device="cuda")
+    nq = [300, 157]
+    reqs, Q = [], 0
+    for b, n in enumerate(nq):
+        reqs.append(PrefillRequest(Q, n, 0, int(batch.nblocks[b])))
+        Q += n
+    g = torch.Generator().manual_seed(7 + bits)
+    iq = torch.randn(Q, 4, 64, generator=g)
+    iw = torch.randn(Q, 4, generator=g)
+    q = torch.randn(Q, H, 128, generator=g).to(torch.bfloat16)
+    sink = torch.randn(H, generator=g)
+    first, rows = [], 0
+    for r in reqs:
+        first.append(rows)
+        rows += 127 + r.num_queries
+    window = torch.randn(rows, 128, generator=g).to(torch.bfloat16)
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    out, ids = csa_prefill_chunk(q.cuda(), iq.cuda(), iw.cuda(), sink.cuda(), window.cuda(), first, batch.cache,
+                                 batch.page_table, reqs, batch.softmax_scale, top_k=top_k, err=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    c = batch.cache
+    sels, ties = opf.prefill_topk(iq, iw, c.idx_codes.cpu(), c.idx_scale.cpu(), batch.page_table.cpu(),
+                                  [(r.first_row, r.num_queries, r.position, r.nblocks) for r in reqs], bits, top_k)
+    ids, out = ids.cpu(), out.float().cpu()
+    kvc, kvs, pt = c.kv_codes.cpu(), c.kv_scale.cpu(), batch.page_table.cpu()
+    worst, total, n = 0.0, 0.0, 0
+    for ri, r in enumerate(reqs):
+        main = otq.decode(odec.gather_pages(kvc, pt[ri], r.nblocks), odec.gather_pages(kvs, pt[ri], r.nblocks).unsqueeze(-1),
+                          bits)
+        for i in range(r.num_queries):
+            row = r.first_row + i
+            k = sels[row].numel()
+            assert k == min(top_k, i // 4)
+            got = ids[row, :k].long()
+            assert ties[row] or torch.equal(got, sels[row]), f"row {row}: selection"
+            assert (ids[row, k:] == -1).all(), f"row {row}: unused index slots hold -1"
+            wl = min(128, i + 1)
+            w0 = first[ri] + i + (128 - wl)
+            src = torch.cat([main[got], window[w0: w0 + wl].float()], dim=0)
+            ref = odec.sink_attention(q[row].float(), src, sink, batch.softmax_scale)
+            d = (out[row] - ref).abs()
+            worst = max(worst, float(d.max()))
+            total += float(d.sum())
+            n += d.numel()
+    assert worst < 2e-2, worst
+    assert total / n < 1e-3, total / n
