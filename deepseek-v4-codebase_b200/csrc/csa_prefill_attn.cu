@@ -461,7 +461,7 @@ __global__ void __launch_bounds__(kThreads, 1) csa_prefill_attend_kernel(Params 
           tmem_wait_ld();
         }
         long long c1 = dbg ? clock64() : 0;
-        ph[0] += c1 - c0;
+        if (dbg) ph[0] += c1 - c0;
         const float sc0 = scl[s * kKeys + r], sc1 = scl[s * kKeys + 128 + r];
         const bool wv = r < m->wl[s];
         float ml[4], ll[4];
@@ -483,13 +483,13 @@ __global__ void __launch_bounds__(kThreads, 1) csa_prefill_attend_kernel(Params 
         }
         // P may be written once the previous token's P V has read it
         t0 = dbg ? clock64() : 0;
-        ph[1] += t0 - c1;
+        if (dbg) ph[1] += t0 - c1;
         const bool ok2 = i == 0 || wait_bar(&m->p_empty, (i - 1) & 1, m, p.err);
         if (dbg) wait2 += clock64() - t0;
         c0 = dbg ? clock64() : 0;
         if (named_any(bar, 128, !ok || !ok2 || aborted(m))) break;
         c1 = dbg ? clock64() : 0;
-        ph[2] += c1 - c0;
+        if (dbg) ph[2] += c1 - c0;
         float corr[4];
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
@@ -543,7 +543,7 @@ __global__ void __launch_bounds__(kThreads, 1) csa_prefill_attend_kernel(Params 
           arrive(&m->o_empty[s]);
         }
         long long c1 = dbg ? clock64() : 0;
-        ph[4] += c1 - c0;
+        if (dbg) ph[4] += c1 - c0;
         // inverse WHT over the 128 dims: bits 5 and 6 through the group's
         // exchange buffer (two heads at a time), bits 0-4 by shuffles
         const int b5 = r & 31, idx = r >> 5;
@@ -568,7 +568,7 @@ __global__ void __launch_bounds__(kThreads, 1) csa_prefill_attend_kernel(Params 
         }
         if (stop) break;
         c0 = dbg ? clock64() : 0;
-        ph[5] += c0 - c1;
+        if (dbg) ph[5] += c0 - c1;
 #pragma unroll
         for (int ld = 1; ld < 32; ld <<= 1) {
           const bool up = (lane & ld) != 0;
