@@ -10,8 +10,9 @@ to those blocks plus its causal 128-token window with the sink.
 csa_prefill_index_kernel): 32 query tokens per CTA against 128-key tiles of
 the request's index pages.  ``csa_prefill_attend`` runs the sparse sink
 attention of every query token over its top-k blocks and its causal window
-(the decode attention kernel in candidate-list mode, one 2-CTA cluster per
-query token).  ``csa_prefill_chunk`` chains the two.
+on the tcgen05 tensor cores as well (kernel csa_prefill_attend_kernel: one
+persistent CTA per SM, S = K q^T and O^T = V^T P from one shared-memory tile
+of the token's rows).  ``csa_prefill_chunk`` chains the two.
 """
 from __future__ import annotations
 
