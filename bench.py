@@ -351,6 +351,8 @@ def main():
     ap.add_argument("--prefill-requests", type=int, default=8)
     ap.add_argument("--prefill-queries", type=int, default=4096)
     ap.add_argument("--prefill-cached", type=int, default=65536)
+    ap.add_argument("--indexer", default="exact", choices=["exact", "fp8"],
+                    help="prefill indexer: exact fp16 limbs, or the e4m3 low-precision indexer")
     args = ap.parse_args()
     if args.workload == "prefill":
         run_prefill(args)
@@ -817,7 +819,7 @@ def run_prefill(args):
     mid = torch.cuda.Event(enable_timing=True)
 
     def step():
-        keys, ids = csa_prefill_topk(iq, iw, cache, table, reqs, err=err, plan=plan)
+        keys, ids = csa_prefill_topk(iq, iw, cache, table, reqs, err=err, plan=plan, indexer=args.indexer)
         mid.record()
         return csa_prefill_attend(q, sink, window, wrow, wlen, cache, table, q_row, vis, keys, ids, 128 ** -0.5,
                                   err=err)
@@ -863,9 +865,9 @@ def run_prefill(args):
         print(json.dumps({
             "metric": PREFILL_METRIC, "value": round(world * R * NQ / (ms / 1e3), 1), "unit": "query tokens/s",
             "n_gpus": world, "steps": steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16 limbs / u8 codes",
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16 limbs / u8 codes" if args.indexer == "exact" else "e4m3 (indexer) / f16",
             "data": "synthetic",
-            "config": {"workload": "csa_prefill_4bit", "requests": R, "queries_per_request": NQ,
+            "config": {"workload": "csa_prefill_4bit", "indexer": args.indexer, "requests": R, "queries_per_request": NQ,
                        "cached_tokens": CACHED, "visible_blocks_max": nblk, "top_k": 256, "heads": H,
                        "timing": "CUDA events per step", "l2_policy": "index caches L2-resident (5 MB)"},
             "gpu_launches": steps * 2,

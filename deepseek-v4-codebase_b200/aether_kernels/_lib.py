@@ -123,6 +123,12 @@ SIGNATURES = {
          _p, _p, _c_int, _c_int, _p, _c_int, _c_int,  # req_info, tiles, ntiles, compression, diag, bits, top_k
          _p, _p, _p, _p],                    # cand_keys, cand_ids, err, stream
     ),
+    "aether_csa_prefill_topk_fp8": (
+        _c_int,
+        [_p, _p, _p, _p, _c_int, _c_int,
+         _p, _p, _c_int, _c_int, _p, _c_int, _c_int,
+         _p, _p, _p, _p],
+    ),
     "aether_csa_decode_paged_rope": (
         _c_int,
         [_p, _p, _p, _p, _p, _p, _p, _p, _p, _c_int, _c_int, _p, _c_int, _p, _p,

@@ -47,12 +47,19 @@ def _plan(requests: Sequence[PrefillRequest], device) -> Tuple[torch.Tensor, tor
 def csa_prefill_topk(index_q: torch.Tensor, index_weight: torch.Tensor, cache: TurboQuantPagedCache,
                      page_table: torch.Tensor, requests: Sequence[PrefillRequest], compression: int = 4,
                      top_k: int = 256, err: Optional[torch.Tensor] = None,
-                     plan: Optional[Tuple[torch.Tensor, torch.Tensor, int]] = None) -> Tuple[torch.Tensor, torch.Tensor]:
+                     plan: Optional[Tuple[torch.Tensor, torch.Tensor, int]] = None,
+                     indexer: str = "exact") -> Tuple[torch.Tensor, torch.Tensor]:
     """Exact top-k blocks per query token.  index_q [Q, 4, 64] fp32,
     index_weight [Q, 4] fp32 raw head weights, page_table [R, max_pages] int32
     (row r for requests[r]).  Returns (keys, ids), each [Q, top_k] int32 (keys
     are order-preserving u32 score bits + 1, reinterpreted), ids ascending,
-    padded with key 0 / id -1."""
+    padded with key 0 / id -1.
+
+    ``indexer="exact"`` computes the scores exactly (two fp16 limbs of the
+    fixed-point rotated query).  ``indexer="fp8"`` computes them on e4m3
+    operands (the paper's low-precision indexer): one MMA column per (query,
+    head), half the tensor-core K steps; the selection then recalls the exact
+    top-k only approximately."""
     _cuda(index_q, "index_q")
     _cuda(index_weight, "index_weight")
     _cuda(page_table, "page_table")
@@ -71,7 +78,9 @@ def csa_prefill_topk(index_q: torch.Tensor, index_weight: torch.Tensor, cache: T
     info, tiles, ntiles = plan if plan is not None else _plan(requests, dev)
     keys = torch.zeros(Q, top_k, dtype=torch.int32, device=dev)
     ids = torch.full((Q, top_k), -1, dtype=torch.int32, device=dev)
-    _lib.call("aether_csa_prefill_topk", index_q.data_ptr(), index_weight.data_ptr(), cache.idx_pages.data_ptr(),
+    _check(indexer in ("exact", "fp8"), f"indexer must be 'exact' or 'fp8', got {indexer!r}")
+    entry = "aether_csa_prefill_topk" if indexer == "exact" else "aether_csa_prefill_topk_fp8"
+    _lib.call(entry, index_q.data_ptr(), index_weight.data_ptr(), cache.idx_pages.data_ptr(),
               page_table.data_ptr(), page_table.shape[1], cache.num_pages, info.data_ptr(), tiles.data_ptr(), ntiles,
               int(compression), rademacher_diag(INDEX_DIM, cache.seed, dev).data_ptr(), cache.bits, int(top_k),
               keys.data_ptr(), ids.data_ptr(), None if err is None else err.data_ptr(), _stream(dev))
@@ -135,10 +144,12 @@ def csa_prefill_attend(q: torch.Tensor, sink: torch.Tensor, window: torch.Tensor
 
 def csa_prefill_chunk(q, index_q, index_weight, sink, window, window_first_row: Sequence[int],
                       cache: TurboQuantPagedCache, page_table, requests: Sequence[PrefillRequest],
-                      softmax_scale: float, compression: int = 4, top_k: int = 256, err=None):
+                      softmax_scale: float, compression: int = 4, top_k: int = 256, err=None,
+                      indexer: str = "exact"):
     """Indexer top-k then attention for every query token of the chunks.
     Returns (out [Q, H, 128] bf16, selected block ids [Q, top_k])."""
-    keys, ids = csa_prefill_topk(index_q, index_weight, cache, page_table, requests, compression, top_k, err)
+    keys, ids = csa_prefill_topk(index_q, index_weight, cache, page_table, requests, compression, top_k, err,
+                                 indexer=indexer)
     q_row, vis, wrow, wlen = query_rows(requests, compression, 128, window_first_row, q.device)
     return csa_prefill_attend(q, sink, window, wrow, wlen, cache, page_table, q_row, vis, keys, ids, softmax_scale,
                               err=err)

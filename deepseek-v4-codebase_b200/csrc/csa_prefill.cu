@@ -35,6 +35,8 @@
 // and raises T to that key; later keys equal to T lose the tie (they have
 // higher block indices).  At the end the exact top-k of the buffer is
 // written in ascending block order.
+#include <cuda_fp8.h>
+
 #include "aether_b200.h"
 #include "capi_util.cuh"
 #include "common.cuh"
@@ -98,6 +100,7 @@ struct alignas(16) Misc {
   int vis[kQ];
   uint32_t thr[kQ];  // per-query threshold and buffer count (owned by one warp)
   uint32_t cnt[kQ];
+  uint32_t lut8[16];
 };
 static_assert(sizeof(Misc) <= 2048, "misc area");
 
@@ -131,6 +134,25 @@ __host__ __device__ constexpr uint32_t umma_idesc(int n, int m) {
 // byte offset of element (row r, k) in the canonical no-swizzle K-major layout
 __device__ __forceinline__ uint32_t canon(int r, int k) {
   return (r >> 3) * kSBO + (k >> 3) * kLBO + (r & 7) * 16 + (k & 7) * 2;
+}
+// The e4m3 indexer (F8): 64-dim rows of 8-bit elements are 4 core matrices
+// of 16 elements, so the 8-row group stride is 512 bytes
+constexpr uint32_t kSBO8 = 512;
+constexpr int kN8 = kQ * kIdxHeads;  // 128 accumulator columns per tile: (query, head)
+__device__ __forceinline__ uint32_t canon8(int r, int k) {
+  return (r >> 3) * kSBO8 + (k >> 4) * kLBO + (r & 7) * 16 + (k & 15);
+}
+__device__ __forceinline__ uint64_t umma_desc8(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>((kLBO >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>((kSBO8 >> 4) & 0x3FFFu) << 32;
+  d |= static_cast<uint64_t>(1) << 46;
+  return d;
+}
+// e4m3 bytes of two floats (saturating, round to nearest even)
+__device__ __forceinline__ uint32_t e4m3x2(float lo, float hi) {
+  return static_cast<uint32_t>(__nv_cvt_float2_to_fp8x2(make_float2(lo, hi), __NV_SATFINITE, __NV_E4M3));
 }
 
 __device__ __forceinline__ void mbar_arrive_cta(uint64_t* bar) {
@@ -267,7 +289,7 @@ __device__ __noinline__ uint32_t warp_prune_call(uint2* buf, int n, int K, int l
   return warp_prune<CAP>(buf, n, K, lane);
 }
 
-template <int BITS>
+template <int BITS, bool F8 = false>
 __global__ void __launch_bounds__(kThreads, 1) csa_prefill_index_kernel(Params p) {
   using C = Cfg<BITS>;
   extern __shared__ __align__(1024) uint8_t smem[];
@@ -302,6 +324,8 @@ __global__ void __launch_bounds__(kThreads, 1) csa_prefill_index_kernel(Params p
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_u32(&m->tmem)));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
+  uint32_t* lut8 = m->lut8;  // F8: signed 4-bit code -> e4m3 byte
+  if (F8 && tid < 16) lut8[tid] = e4m3x2(static_cast<float>(static_cast<int>(tid ^ 8u) - 8), 0.f) & 0xFFu;
   // ---- prologue: rotated fixed-point query limbs (B operand), head weights
   // and causal limits; one warp per (query, head)
   for (int v = warp; v < kQ * kIdxHeads; v += kThreads / 32) {
@@ -330,6 +354,16 @@ __global__ void __launch_bounds__(kThreads, 1) csa_prefill_index_kernel(Params p
     x0 *= 0.125f;
     x1 *= 0.125f;
     const float am = warp_max(fmaxf(fabsf(x0), fabsf(x1)));
+    if constexpr (F8) {
+      // e4m3 query, one scale per (query, head): the largest element maps to
+      // 448, the largest finite e4m3 value; B row (query, head)
+      const float s8 = am > 0.f ? am / 448.0f : 1.0f;
+      const uint32_t b2 = valid ? e4m3x2(x0 / s8, x1 / s8) : 0u;
+      *reinterpret_cast<uint16_t*>(smem + C::OFF_B + canon8(qi * kIdxHeads + h, 2 * lane)) =
+          static_cast<uint16_t>(b2);
+      if (lane == 0) m->alpha[qi][h] = valid ? softplus_f(w) * s8 : 0.f;
+      continue;
+    }
     const float s = am > 0.f ? am / 2097152.0f : 1.0f;  // 2^21
 #pragma unroll
     for (int k = 0; k < 2; ++k) {
@@ -389,7 +423,7 @@ __global__ void __launch_bounds__(kThreads, 1) csa_prefill_index_kernel(Params p
   } else if (warp == 1) {
     // ------------------------------------------------ MMA issue
     if (lane == 0) {
-      constexpr uint32_t idesc = umma_idesc(kN, kTileKeys);
+      constexpr uint32_t idesc = umma_idesc(F8 ? kN8 : kN, kTileKeys);
       const uint32_t sB = smem_u32(smem + C::OFF_B);
       for (int j = 0; j < ntiles; ++j) {
         const int st = j & 1, use = j >> 1;
@@ -398,13 +432,24 @@ __global__ void __launch_bounds__(kThreads, 1) csa_prefill_index_kernel(Params p
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const uint32_t sA = smem_u32(smem + C::OFF_A + st * kTileKeys * kIdxDim * 2);
         const uint32_t dt = tmem + st * kN;
+        if constexpr (F8) {
 #pragma unroll
-        for (int kk = 0; kk < kIdxDim / 16; ++kk) {
-          const uint64_t da = umma_desc(sA + kk * 2 * kLBO), db = umma_desc(sB + kk * 2 * kLBO);
-          asm volatile(
-              "{ .reg .pred p; setp.ne.u32 p, %4, 0;\n"
-              "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p; }" ::"r"(dt),
-              "l"(da), "l"(db), "r"(idesc), "r"(static_cast<uint32_t>(kk)));
+          for (int kk = 0; kk < kIdxDim / 32; ++kk) {  // 32 e4m3 elements = 2 core matrices per step
+            const uint64_t da = umma_desc8(sA + kk * 2 * kLBO), db = umma_desc8(sB + kk * 2 * kLBO);
+            asm volatile(
+                "{ .reg .pred p; setp.ne.u32 p, %4, 0;\n"
+                "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p; }" ::"r"(dt),
+                "l"(da), "l"(db), "r"(idesc), "r"(static_cast<uint32_t>(kk)));
+          }
+        } else {
+#pragma unroll
+          for (int kk = 0; kk < kIdxDim / 16; ++kk) {
+            const uint64_t da = umma_desc(sA + kk * 2 * kLBO), db = umma_desc(sB + kk * 2 * kLBO);
+            asm volatile(
+                "{ .reg .pred p; setp.ne.u32 p, %4, 0;\n"
+                "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p; }" ::"r"(dt),
+                "l"(da), "l"(db), "r"(idesc), "r"(static_cast<uint32_t>(kk)));
+          }
         }
         asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
                          smem_u32(&m->a_empty[st]))
@@ -425,7 +470,31 @@ __global__ void __launch_bounds__(kThreads, 1) csa_prefill_index_kernel(Params p
       const uint8_t* page = smem + C::OFF_RAW + slot * ((C::RAW_BYTES + 127) & ~127) + (r >> 6) * C::PB;
       const uint8_t* row = page + (r & 63) * C::RB;
       uint8_t* A = smem + C::OFF_A + st * kTileKeys * kIdxDim * 2;
-      if (BITS == 4) {
+      if constexpr (F8) {
+        // codes -> e4m3: exact for the 4-bit range [-8, 7], rounded for 8-bit
+#pragma unroll
+        for (int c = 0; c < kIdxDim / 16; ++c) {  // 16 dims per 16-byte chunk
+          uint32_t o[4];
+          if (BITS == 4) {
+            const uint2 w = *reinterpret_cast<const uint2*>(row + 8 * c);
+            const uint32_t wb[2] = {w.x, w.y};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const uint32_t b0 = (wb[i >> 1] >> (16 * (i & 1))) & 0xFFu, b1 = (wb[i >> 1] >> (16 * (i & 1) + 8)) & 0xFFu;
+              o[i] = lut8[b0 & 15u] | (lut8[b0 >> 4] << 8) | (lut8[b1 & 15u] << 16) | (lut8[b1 >> 4] << 24);
+            }
+          } else {
+            const uint4 w = *reinterpret_cast<const uint4*>(row + 16 * c);
+            const uint32_t wb[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const int8_t* c8 = reinterpret_cast<const int8_t*>(&wb[i]);
+              o[i] = e4m3x2(c8[0], c8[1]) | (e4m3x2(c8[2], c8[3]) << 16);
+            }
+          }
+          *reinterpret_cast<uint4*>(A + canon8(r, 16 * c)) = make_uint4(o[0], o[1], o[2], o[3]);
+        }
+      } else if (BITS == 4) {
         const uint4 v0 = *reinterpret_cast<const uint4*>(row), v1 = *reinterpret_cast<const uint4*>(row + 16);
         const uint32_t wv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
 #pragma unroll
@@ -478,8 +547,38 @@ __global__ void __launch_bounds__(kThreads, 1) csa_prefill_index_kernel(Params p
       t_wait += c1 - c0;
       const float kscale = sscl[(j & 3) * kTileKeys + r];
       uint32_t* xo = xbuf;
+      if constexpr (F8) {  // 64 columns: (query, head) of this half's 16 queries
+        uint32_t v[64];
+        const uint32_t ta = tmem + (static_cast<uint32_t>(32 * quad) << 16) + st * kN + half * 64;
+        asm volatile(
+            "tcgen05.ld.sync.aligned.32x32b.x64.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+            "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32,%33,%34,%35,%36,%37,%38,%39,"
+            "%40,%41,%42,%43,%44,%45,%46,%47,%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, "
+            "[%64];"
+            : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+              "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]),
+              "=r"(v[15]), "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]),
+              "=r"(v[22]), "=r"(v[23]), "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]),
+              "=r"(v[29]), "=r"(v[30]), "=r"(v[31]), "=r"(v[32]), "=r"(v[33]), "=r"(v[34]), "=r"(v[35]),
+              "=r"(v[36]), "=r"(v[37]), "=r"(v[38]), "=r"(v[39]), "=r"(v[40]), "=r"(v[41]), "=r"(v[42]),
+              "=r"(v[43]), "=r"(v[44]), "=r"(v[45]), "=r"(v[46]), "=r"(v[47]), "=r"(v[48]), "=r"(v[49]),
+              "=r"(v[50]), "=r"(v[51]), "=r"(v[52]), "=r"(v[53]), "=r"(v[54]), "=r"(v[55]), "=r"(v[56]),
+              "=r"(v[57]), "=r"(v[58]), "=r"(v[59]), "=r"(v[60]), "=r"(v[61]), "=r"(v[62]), "=r"(v[63])
+            : "r"(ta));
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-      for (int c2 = 0; c2 < 2; ++c2) {  // 2 x 64 columns = 8 queries each
+        for (int qq = 0; qq < 16; ++qq) {
+          const int qa = half * 16 + qq;
+          const float4 a = *reinterpret_cast<const float4*>(m->alpha[qa]);
+          float sc = a.x * fmaxf(__uint_as_float(v[4 * qq]), 0.f);
+          sc = fmaf(a.y, fmaxf(__uint_as_float(v[4 * qq + 1]), 0.f), sc);
+          sc = fmaf(a.z, fmaxf(__uint_as_float(v[4 * qq + 2]), 0.f), sc);
+          sc = fmaf(a.w, fmaxf(__uint_as_float(v[4 * qq + 3]), 0.f), sc);
+          xo[qa * kTileKeys + r] = __float_as_uint(__fmul_rn(sc, kscale)) + 1u;
+        }
+      }
+#pragma unroll
+      for (int c2 = 0; c2 < (F8 ? 0 : 2); ++c2) {  // 2 x 64 columns = 8 queries each
         uint32_t v[64];
         const uint32_t ta = tmem + (static_cast<uint32_t>(32 * quad) << 16) + st * kN + half * 128 + c2 * 64;
         asm volatile(
@@ -662,13 +761,13 @@ __global__ void __launch_bounds__(kThreads, 1) csa_prefill_index_kernel(Params p
 
 static long long* g_debug = nullptr;
 
-template <int BITS>
+template <int BITS, bool F8>
 static int launch(const Params& p, int ntiles, cudaStream_t st) {
-  if (int rc = ensure_smem_attr(reinterpret_cast<const void*>(csa_prefill_index_kernel<BITS>), Cfg<BITS>::SMEM,
+  if (int rc = ensure_smem_attr(reinterpret_cast<const void*>(csa_prefill_index_kernel<BITS, F8>), Cfg<BITS>::SMEM,
                                 "csa_prefill"))
     return rc;
-  csa_prefill_index_kernel<BITS><<<ntiles, kThreads, Cfg<BITS>::SMEM, st>>>(p);
-  return check_launch("csa_prefill_topk");
+  csa_prefill_index_kernel<BITS, F8><<<ntiles, kThreads, Cfg<BITS>::SMEM, st>>>(p);
+  return check_launch(F8 ? "csa_prefill_topk_fp8" : "csa_prefill_topk");
 }
 
 }  // namespace prefill
@@ -690,7 +789,29 @@ extern "C" int aether_csa_prefill_topk(const float* index_q, const float* index_
   prefill::Params p{index_q, index_w, idx_pages, page_table, req_info, tiles, diag_idx, cand_keys, cand_ids, err,
                     prefill::g_debug, table_stride, num_pages, compression, top_k};
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  return bits == 4 ? prefill::launch<4>(p, ntiles, st) : prefill::launch<8>(p, ntiles, st);
+  return bits == 4 ? prefill::launch<4, false>(p, ntiles, st) : prefill::launch<8, false>(p, ntiles, st);
+}
+
+// As aether_csa_prefill_topk, with the scores computed on e4m3 operands
+// (tcgen05 kind::f8f6f4): the rotated index query is quantised to e4m3 per
+// (query, head), 4-bit codes are exact in e4m3 and 8-bit codes are rounded to
+// it.  The selection is the exact top-k of these approximate scores, so it
+// agrees with the exact indexer only up to a recall below 1.
+extern "C" int aether_csa_prefill_topk_fp8(const float* index_q, const float* index_w, const uint8_t* idx_pages,
+                                           const int32_t* page_table, int table_stride, int num_pages,
+                                           const int32_t* req_info, const int32_t* tiles, int ntiles,
+                                           int compression, const float* diag_idx, int bits, int top_k,
+                                           uint32_t* cand_keys, int32_t* cand_ids, int* err, void* stream) {
+  AETHER_REQUIRE(bits == 4 || bits == 8, "bits must be 4 or 8, got %d", bits);
+  AETHER_REQUIRE(top_k >= 1 && top_k <= prefill::kMaxK, "top_k must be in [1, %d], got %d", prefill::kMaxK, top_k);
+  AETHER_REQUIRE(compression >= 1, "compression must be positive");
+  AETHER_REQUIRE(table_stride >= 1 && num_pages >= 1, "page table / pool must be non-empty");
+  AETHER_REQUIRE(ntiles >= 0, "negative tile count");
+  if (ntiles == 0) return 0;
+  prefill::Params p{index_q, index_w, idx_pages, page_table, req_info, tiles, diag_idx, cand_keys, cand_ids, err,
+                    prefill::g_debug, table_stride, num_pages, compression, top_k};
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  return bits == 4 ? prefill::launch<4, true>(p, ntiles, st) : prefill::launch<8, true>(p, ntiles, st);
 }
 
 // Profiling aid: when buf is non-null, later prefill launches record per-CTA

@@ -323,6 +323,18 @@ int aether_csa_prefill_topk(const float* index_q, const float* index_w, const ui
                             const int32_t* tiles, int ntiles, int compression, const float* diag_idx, int bits,
                             int top_k, uint32_t* cand_keys, int32_t* cand_ids, int* err, void* stream);
 
+/* The optional low-precision indexer of the paper's CSA indexer path
+ * (Aether.txt:765-769, 1087-1093; no counterpart kernel in the reference
+ * code): as aether_csa_prefill_topk, with the scores computed on e4m3
+ * operands on tcgen05 (kind::f8f6f4).  The rotated index query is quantised
+ * to e4m3 per (query, head) with scale max|q| / 448; 4-bit codes are exact in
+ * e4m3, 8-bit codes are rounded to it.  The rows are the exact top-k of those
+ * scores: they match the exact indexer's only up to a recall below 1. */
+int aether_csa_prefill_topk_fp8(const float* index_q, const float* index_w, const uint8_t* idx_pages,
+                                const int32_t* page_table, int table_stride, int num_pages, const int32_t* req_info,
+                                const int32_t* tiles, int ntiles, int compression, const float* diag_idx, int bits,
+                                int top_k, uint32_t* cand_keys, int32_t* cand_ids, int* err, void* stream);
+
 /* Chunked-prefill attention (aether_2b/modeling.py:616-640 per query row):
  * query b attends the blocks of its candidate row (cand_keys / cand_ids from
  * aether_csa_prefill_topk, cand_stride >= top_k) plus its window, with the
