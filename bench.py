@@ -351,6 +351,8 @@ def main():
     ap.add_argument("--prefill-requests", type=int, default=8)
     ap.add_argument("--prefill-queries", type=int, default=4096)
     ap.add_argument("--prefill-cached", type=int, default=65536)
+    ap.add_argument("--cp-exchange", default="peer", choices=["peer", "nccl"],
+                    help="long workload on several GPUs: peer-memory stores or NCCL all-gathers")
     ap.add_argument("--indexer", default="exact", choices=["exact", "fp8"],
                     help="prefill indexer: exact fp16 limbs, or the e4m3 low-precision indexer")
     args = ap.parse_args()
@@ -572,10 +574,13 @@ def run_long(args):
     all-gather, exact global top-256, attention over the owned winners,
     all-gather of the partials, LSE merge (aether_kernels.dist).  One rank:
     the single-device path (per-chunk top-256, then the top-256 of the chunk
-    winners).  Cache sets cycle so every step reads cold HBM."""
+    winners).  Cache sets cycle so every step reads cold HBM.  On N ranks the
+    two exchanges are stores into the peers' memory (aether_peer_push /
+    aether_peer_wait, PeerContextParallel) and a CUDA graph of the steps is
+    replayed; --cp-exchange nccl runs the NCCL all-gather path eagerly."""
     import torch.distributed as dist
 
-    from aether_kernels.dist import csa_decode_context_parallel
+    from aether_kernels.dist import PeerContextParallel, csa_decode_context_parallel
     from aether_kernels.paged import PAGE, TurboQuantPagedCache, csa_decode_paged, csa_workspace_bytes
     from aether_kernels.rope import RopeConfig
     from aether_kernels.synthetic import make_decode_batch
@@ -605,6 +610,8 @@ def run_long(args):
     out = torch.empty(1, 12, 128, dtype=torch.bfloat16, device=dev)
     ws = torch.zeros(csa_workspace_bytes(1, NB), dtype=torch.uint8, device=dev)
     err = torch.zeros(1, dtype=torch.int32, device=dev)
+    peer = world > 1 and args.cp_exchange == "peer"
+    plan = PeerContextParallel(1, 12, per, 256, device=dev) if peer else None
 
     def step(i):
         st = sets[i % nsets]
@@ -612,6 +619,9 @@ def run_long(args):
         if world == 1:
             csa_decode_paged(st.q, st.index_q, st.index_weight, st.sink, st.window, st.window_len, cache, table, nb,
                              st.softmax_scale, out=out, workspace=ws, err=err)
+        elif peer:
+            plan.step(st.q, st.index_q, st.index_weight, st.sink, st.window, wl, cache, table, nb, rank * per,
+                      st.softmax_scale, err=err)
         else:
             csa_decode_context_parallel(st.q, st.index_q, st.index_weight, st.sink, st.window, wl, cache, table, nb,
                                         rank * per, st.softmax_scale, err=err)
@@ -622,11 +632,13 @@ def run_long(args):
             step(i)
     torch.cuda.synchronize(dev)
     assert int(err.item()) == 0, f"kernel error flag {int(err.item())}"
-    # one GPU: a CUDA graph of nsets steps replayed.  Several GPUs: eager
-    # launches (a captured graph holding NCCL collectives left the ranks
-    # hanging in process-group teardown, so collectives are not captured)
+    # one GPU, or the peer exchange: a CUDA graph of nsets steps replayed.
+    # The NCCL path runs eagerly (a captured graph holding NCCL collectives
+    # left the ranks hanging in process-group teardown)
     graph = None
-    if world == 1:
+    if world == 1 or peer:
+        if peer:
+            dist.barrier()
         try:
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g, stream=stream):
@@ -673,12 +685,17 @@ def run_long(args):
             "config": {"workload": "csa_decode_8bit_b1_ctx262k", "nblocks": NB, "blocks_per_gpu": per, "bits": bits,
                        "rope": "yarn x8", "cache_sets": nsets, "parallelism": f"context-parallel x{world}",
                        "l2_policy": "inputs larger than L2: each step reads a different cache set",
-                       "timing": "CUDA graph replay on 1 GPU, eager launches with NCCL on N > 1; CUDA events"},
+                       "exchange": None if world == 1 else args.cp_exchange,
+                       "timing": ("CUDA graph replay; CUDA events" if graph is not None
+                                  else "eager launches with NCCL; CUDA events")},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": round(peak * world, 1),
                          "unit": "GB/s", "frac": round(achieved / (peak * world), 4), "peak_source": src,
                          "traffic": None, "algorithmic_bytes_per_launch": per_q},
             "clocks": clocks,
         }), flush=True)
+    if plan is not None:
+        del graph
+        plan.close()
     if world > 1:
         dist.destroy_process_group()
 

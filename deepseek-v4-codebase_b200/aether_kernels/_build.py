@@ -14,7 +14,7 @@ from typing import List, Optional
 PKG = Path(__file__).resolve().parent
 CSRC = PKG.parent / "csrc"
 INCLUDE = PKG.parent.parent / "include"  # aether_b200.h: the sources include it, so drift fails to compile
-SOURCES = ["capi.cu", "tq.cu", "compat.cu", "csa_decode_api.cu", "csa_decode_cta.cu", "csa_prefill.cu", "csa_prefill_attn.cu"]
+SOURCES = ["capi.cu", "tq.cu", "compat.cu", "csa_decode_api.cu", "csa_decode_cta.cu", "csa_prefill.cu", "csa_prefill_attn.cu", "cp_exchange.cu"]
 OUT = PKG / "libaether_b200.so"
 
 NVCC_FLAGS = [

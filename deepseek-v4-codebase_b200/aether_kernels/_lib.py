@@ -109,6 +109,18 @@ SIGNATURES = {
          _c_int, _c_int, _c_int, _c_int, _c_int, _c_f, _p, _p, _p, _p, _p, _p],
     ),
     "aether_lse_merge": (_c_int, [_p, _p, _p, _c_int, _c_int, _c_int, _p, _p]),
+    "aether_cp_control_bytes": (_c_ll, []),
+    "aether_cp_buffer_create": (_c_int, [_c_ll, ctypes.POINTER(_p), _p]),
+    "aether_cp_buffer_open": (_c_int, [_p, ctypes.POINTER(_p)]),
+    "aether_cp_buffer_close": (_c_int, [_p]),
+    "aether_cp_buffer_destroy": (_c_int, [_p]),
+    "aether_peer_push": (
+        _c_int,
+        [_p, _c_ll, _c_ll, _c_ll,            # src, rows, row_bytes, src_stride
+         _p, _c_int, _c_int,                 # bases[G], G, rank
+         _c_ll, _c_ll, _c_ll, _c_int, _c_int, _p],  # dst_offset, dst_stride, dst_col, kind, bump, stream
+    ),
+    "aether_peer_wait": (_c_int, [_p, _c_int, _c_int, _p, _p]),
     "aether_lse_merge_strided": (_c_int, [_p, _p, _c_ll, _c_ll, _p, _c_int, _c_int, _c_int, _p, _p]),
     "aether_csa_prefill_attend": (
         _c_int,

@@ -21,6 +21,7 @@ NCCL and, in the CPU tests, with reference-math callables over gloo.
 """
 from __future__ import annotations
 
+import ctypes
 from typing import Callable, Optional, Tuple
 
 import torch
@@ -155,3 +156,114 @@ def csa_decode_context_parallel(q, index_q, index_weight, sink, window, window_l
                                        softmax_scale, top_k, partial=True, err=err),
         lambda po, pml: lse_merge(po, pml, sink),
         group=group)
+
+
+# ------------------------------------------------------ peer-memory exchange
+def _pad16(n: int) -> int:
+    return (n + 15) & ~15
+
+
+class PeerContextParallel:
+    """Context-parallel CSA decode whose two exchanges are stores into the
+    other GPUs' memory (``aether_peer_push`` / ``aether_peer_wait``) instead
+    of NCCL all-gathers: the same math as ``csa_decode_context_parallel``
+    (candidate lists in rank order, exact global top-k on every rank, the
+    log-sum-exp merge with the sink counted once), with no collective launch
+    and no host synchronisation inside a step, so a step can be captured in a
+    CUDA graph.
+
+    Every rank builds the plan with the same batch, head count and local
+    block capacity; the constructor exchanges CUDA IPC handles over
+    ``group`` (any backend).  Layout of each rank's exchange buffer: control
+    area, candidate keys [B][G * n], candidate ids [B][G * n] (rank r's
+    lists at column r * n), then G partial slots (O [B][H][128] and (max,
+    sum) [B][H][2], fp32).  Call ``close()`` on every rank when done."""
+
+    def __init__(self, batch: int, heads: int, max_local_blocks: int, top_k: int = 256, group=None, device=None):
+        self.G = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.group = group
+        self.B, self.H, self.top_k = batch, heads, top_k
+        self.dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        self.max_nb = (max(max_local_blocks, 1) + PAGE - 1) // PAGE * PAGE
+        self.n = chunks_for(self.max_nb) * top_k
+        lib = _lib.load()
+        ctrl = int(lib.aether_cp_control_bytes())
+        row = self.G * self.n * 4
+        self.off_k = ctrl
+        self.off_i = self.off_k + batch * row
+        self.off_p = _pad16(self.off_i + batch * row)
+        self.o_bytes = batch * heads * HEAD_DIM * 4
+        self.slot = _pad16(self.o_bytes + batch * heads * 2 * 4)
+        total = self.off_p + self.G * self.slot
+        ptr, handle = ctypes.c_void_p(), (ctypes.c_char * 64)()
+        _lib.call("aether_cp_buffer_create", total, ctypes.byref(ptr), handle)
+        self._own = ptr.value
+        handles = [None] * self.G
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        self._opened, bases = [], []
+        for g, h in enumerate(handles):
+            if g == self.rank:
+                bases.append(self._own)
+                continue
+            peer = ctypes.c_void_p()
+            _lib.call("aether_cp_buffer_open", ctypes.create_string_buffer(h, 64), ctypes.byref(peer))
+            self._opened.append(peer.value)
+            bases.append(peer.value)
+        self._bases = (ctypes.c_void_p * self.G)(*bases)
+        # local staging, allocated once (a captured step allocates nothing)
+        self.cand = torch.empty(2, batch, self.n, dtype=torch.int32, device=self.dev)
+        self.part = torch.empty(self.slot // 4, dtype=torch.float32, device=self.dev)
+        self.ws = torch.empty(max(csa_workspace_bytes(batch, self.max_nb), 16), dtype=torch.uint8, device=self.dev)
+        self.sel = torch.empty(batch, top_k, dtype=torch.int32, device=self.dev)
+        self.out = torch.empty(batch, heads, HEAD_DIM, dtype=torch.bfloat16, device=self.dev)
+        dist.barrier(group=group)
+
+    def step(self, q, index_q, index_weight, sink, window, window_len, cache: TurboQuantPagedCache, page_table,
+             nblocks, id_base: int, softmax_scale: float, err: Optional[torch.Tensor] = None):
+        """One decode step (same arguments as csa_decode_context_parallel);
+        returns (out bf16 [B,H,128], selected global block ids [B,top_k]),
+        both buffers of the plan, overwritten by the next step."""
+        B, H, n, G = self.B, self.H, self.n, self.G
+        _check(tuple(q.shape) == (B, H, HEAD_DIM), f"q must be [{B}, {H}, {HEAD_DIM}]")
+        _check(page_table.shape[1] * PAGE <= self.max_nb, "page table exceeds the plan's local block capacity")
+        dev = q.device
+        st = _stream(dev)
+        ep = None if err is None else err.data_ptr()
+        base = self._own
+        keys, ids = self.cand[0], self.cand[1]
+        _lib.call("aether_csa_local_candidates", index_q.data_ptr(), index_weight.data_ptr(),
+                  cache.idx_pages.data_ptr(), page_table.data_ptr(), page_table.shape[1], cache.num_pages,
+                  nblocks.data_ptr(), self.max_nb, rademacher_diag(INDEX_DIM, cache.seed, dev).data_ptr(), B,
+                  cache.bits, int(self.top_k), int(id_base), keys.data_ptr(), ids.data_ptr(), self.ws.data_ptr(),
+                  ep, st)
+        # keys then ids: 2B rows of n words into column rank * n of [2B][G n]
+        _lib.call("aether_peer_push", self.cand.data_ptr(), 2 * B, n * 4, n * 4,
+                  ctypes.cast(self._bases, ctypes.c_void_p), G, self.rank, self.off_k, G * n * 4,
+                  self.rank * n * 4, 0, 1, st)
+        _lib.call("aether_peer_wait", base, G, 0, ep, st)
+        po = self.part.data_ptr()
+        _lib.call("aether_csa_attend_candidates", q.data_ptr(), sink.data_ptr(), window.data_ptr(),
+                  window_len.data_ptr(), cache.kv_pages.data_ptr(), page_table.data_ptr(), page_table.shape[1],
+                  cache.num_pages, nblocks.data_ptr(), page_table.shape[1] * PAGE,
+                  rademacher_diag(HEAD_DIM, cache.seed, dev).data_ptr(), base + self.off_k, base + self.off_i,
+                  G * n, G * n, int(id_base), B, H, window.shape[1], cache.bits, int(self.top_k),
+                  float(softmax_scale), None, self.sel.data_ptr(), po, po + self.o_bytes, ep, st)
+        _lib.call("aether_peer_push", po, 1, self.slot, self.slot, ctypes.cast(self._bases, ctypes.c_void_p), G,
+                  self.rank, self.off_p, self.slot, self.rank * self.slot, 1, 0, st)
+        _lib.call("aether_peer_wait", base, G, 1, ep, st)
+        _lib.call("aether_lse_merge_strided", base + self.off_p, base + self.off_p + self.o_bytes, self.slot // 4,
+                  self.slot // 4, sink.data_ptr(), G, B, H, self.out.data_ptr(), st)
+        return self.out, self.sel
+
+    def close(self) -> None:
+        """Release the buffers (collective: every rank calls it)."""
+        if self._own is None:
+            return
+        torch.cuda.synchronize(self.dev)
+        dist.barrier(group=self.group)  # no rank still reads or writes a buffer
+        for pp in self._opened:
+            _lib.call("aether_cp_buffer_close", pp)
+        self._opened = []
+        _lib.call("aether_cp_buffer_destroy", self._own)
+        self._own = None

@@ -363,6 +363,32 @@ size_t aether_csa_decode_workspace_bytes(int B, int max_nblocks);
 /* Shared-memory bytes of the select/attend CSA decode kernel. */
 int aether_csa_decode_smem_bytes(int bits);
 
+/* ---- peer-memory exchange for context-parallel decode (no counterpart in
+ * the reference, which has no multi-GPU decode; it replaces the two NCCL
+ * all-gathers of a context-parallel step).  One process per GPU.  Each rank
+ * creates one exchange buffer and shares its 64-byte CUDA IPC handle; the
+ * others open it.  The first aether_cp_control_bytes() bytes of a buffer are
+ * its control area (flag words and the step word).
+ *
+ * aether_peer_push: copy `rows` rows of `row_bytes` (row stride src_stride)
+ * from local device memory into every buffer bases[0..G-1] at
+ * dst_offset + dst_col + row * dst_stride, then raise this rank's flag of
+ * `kind` (0..3) in every buffer to the step number.  bump = 1 starts a new
+ * step (the local step word is incremented first).  Sizes, strides and
+ * offsets are multiples of 16 bytes; dst_offset lies past the control area.
+ * aether_peer_wait: stream-ordered wait until all G flags of `kind` in the
+ * local buffer reach the local step number; bounded (0.2 s), a timeout sets
+ * the wait-timeout bit of *err. */
+long long aether_cp_control_bytes(void);
+int aether_cp_buffer_create(long long bytes, void** ptr, void* ipc_handle);
+int aether_cp_buffer_open(const void* ipc_handle, void** ptr);
+int aether_cp_buffer_close(void* ptr);
+int aether_cp_buffer_destroy(void* ptr);
+int aether_peer_push(const void* src, long long rows, long long row_bytes, long long src_stride, void* const* bases,
+                     int G, int rank, long long dst_offset, long long dst_stride, long long dst_col, int kind,
+                     int bump, void* stream);
+int aether_peer_wait(const void* local_base, int G, int kind, int* err, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

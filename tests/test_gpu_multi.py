@@ -60,8 +60,41 @@ def _worker(rank, world, port, q_out):
         got = sel[0].cpu().long()
         oracle_sel_ok = bool(torch.equal(got, o.selected[0])) or o.near_tie[0]
         d = (out.float().cpu()[0] - o.out[0]).abs()
+    # the same step with the peer-memory exchange: two eager steps (the step
+    # counter advances), then three replays of a captured CUDA graph; every
+    # result must equal the NCCL path's exactly (same kernels, same inputs)
+    from aether_kernels.dist import PeerContextParallel
+
+    plan = PeerContextParallel(1, b.q.shape[1], per * 64, b.top_k, device=dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    args = (b.q, b.index_q, b.index_weight, b.sink, b.window, wl, b.cache, pt, nb, rank * per * 64, b.softmax_scale)
+    peer_same = True
+    for _ in range(2):
+        po, psel = plan.step(*args, err=err)
+        torch.cuda.synchronize()
+        peer_same &= bool(torch.equal(po, out)) and bool(torch.equal(psel, sel))
+    s = torch.cuda.Stream(dev)
+    s.wait_stream(torch.cuda.current_stream(dev))
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(s):
+        plan.step(*args, err=err)  # warm-up on the capture stream
+        torch.cuda.synchronize()
+        dist.barrier()
+        with torch.cuda.graph(g, stream=s):
+            plan.step(*args, err=err)
+    torch.cuda.synchronize()
+    dist.barrier()
+    for _ in range(3):
+        plan.out.zero_()
+        g.replay()
+        torch.cuda.synchronize()
+        peer_same &= bool(torch.equal(plan.out, out)) and bool(torch.equal(plan.sel, sel))
+    peer_err = int(err.item())
+    plan.close()
+    del g
+    if rank == 0:
         q_out.put((bool(torch.equal(sel, ref_sel)), float((out.float() - ref.float()).abs().max()), oracle_sel_ok,
-                   float(d.max()), float(d.mean())))
+                   float(d.max()), float(d.mean()), peer_same, peer_err))
     dist.barrier()
     dist.destroy_process_group()
 
@@ -76,7 +109,7 @@ def test_context_parallel_nccl():
     procs = [ctx.Process(target=_worker, args=(r, world, port, q_out)) for r in range(world)]
     for p in procs:
         p.start()
-    same_sel, max_diff, oracle_sel_ok, omax, omean = q_out.get(timeout=600)
+    same_sel, max_diff, oracle_sel_ok, omax, omean, peer_same, peer_err = q_out.get(timeout=600)
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
@@ -84,3 +117,5 @@ def test_context_parallel_nccl():
     assert omax < 2e-2 and omean < 1e-3, (omax, omean)
     assert same_sel
     assert max_diff < 1e-2
+    assert peer_err == 0, f"peer exchange error word {peer_err}"
+    assert peer_same, "the peer-memory exchange differs from the NCCL path"
