@@ -163,6 +163,23 @@ def _pad16(n: int) -> int:
     return (n + 15) & ~15
 
 
+def peer_layout(batch: int, heads: int, n: int, world: int, control_bytes: int = 256) -> dict:
+    """Byte layout of one rank's exchange buffer: control area; candidate
+    keys [batch][world * n] int32 (rank r's list at column r * n); candidate
+    ids, the same shape right after the keys (so keys and ids of a rank are
+    2 * batch rows of one strided copy); then ``world`` partial slots, each O
+    [batch][heads][128] fp32 followed by (max, sum) [batch][heads][2] fp32
+    and padded to 16 bytes."""
+    row = world * n * 4
+    off_k = control_bytes
+    off_i = off_k + batch * row
+    off_p = _pad16(off_i + batch * row)
+    o_bytes = batch * heads * HEAD_DIM * 4
+    slot = _pad16(o_bytes + batch * heads * 2 * 4)
+    return dict(row_bytes=row, off_k=off_k, off_i=off_i, off_p=off_p, o_bytes=o_bytes, slot=slot,
+                total=off_p + world * slot)
+
+
 class PeerContextParallel:
     """Context-parallel CSA decode whose two exchanges are stores into the
     other GPUs' memory (``aether_peer_push`` / ``aether_peer_wait``) instead
@@ -188,14 +205,9 @@ class PeerContextParallel:
         self.max_nb = (max(max_local_blocks, 1) + PAGE - 1) // PAGE * PAGE
         self.n = chunks_for(self.max_nb) * top_k
         lib = _lib.load()
-        ctrl = int(lib.aether_cp_control_bytes())
-        row = self.G * self.n * 4
-        self.off_k = ctrl
-        self.off_i = self.off_k + batch * row
-        self.off_p = _pad16(self.off_i + batch * row)
-        self.o_bytes = batch * heads * HEAD_DIM * 4
-        self.slot = _pad16(self.o_bytes + batch * heads * 2 * 4)
-        total = self.off_p + self.G * self.slot
+        lay = peer_layout(batch, heads, self.n, self.G, int(lib.aether_cp_control_bytes()))
+        self.off_k, self.off_i, self.off_p = lay["off_k"], lay["off_i"], lay["off_p"]
+        self.o_bytes, self.slot, total = lay["o_bytes"], lay["slot"], lay["total"]
         ptr, handle = ctypes.c_void_p(), (ctypes.c_char * 64)()
         _lib.call("aether_cp_buffer_create", total, ctypes.byref(ptr), handle)
         self._own = ptr.value
