@@ -14,9 +14,12 @@
 // reference adds it once per source token), and the indexer uses the
 // canonical softplus/ReLU score with an exact, (score desc, index asc)
 // ordered top-k instead of a raw weighted dot with an unordered serial pick.
+#include <type_traits>
+
 #include "aether_b200.h"
 #include "capi_util.cuh"
 #include "common.cuh"
+#include "decode_common.cuh"
 
 namespace aether {
 
@@ -97,6 +100,179 @@ __global__ void __launch_bounds__(256) sink_attn_kernel(const T* __restrict__ q,
   }
 }
 
+
+// ---------------------------------------------------------------------------
+// Tensor-core path for the common shape (16-bit inputs, D = 128, H <= 16):
+// one CTA per target token serves all heads.  Gathered K / V rows arrive in
+// 128-row tiles (cp.async, double-buffered); S = Q K^T on mma.sync (16 heads x
+// 16 sources per warp), an online softmax per head across tiles, O += P V on
+// mma.sync (16 output dims per warp, fp16 P, V converted to fp16 in
+// registers for bf16 inputs); the sink enters the denominator once at the end.
+constexpr int kTcRows = 128;  // sources per tile
+constexpr int kTcRow = 136;   // padded smem row (elements)
+constexpr int kTcSt = kTcRows + 4;  // logit row stride (floats)
+constexpr int kTcPst = kTcRows + 8;  // P row stride (halves)
+constexpr int kTcSmem = (16 * kTcRow + 4 * kTcRows * kTcRow) * 2 + 16 * kTcSt * 4 + 16 * kTcPst * 2 + 2 * kTcRows * 4 +
+                        3 * 16 * 4;
+
+template <typename T>
+__device__ __forceinline__ void tc_mma_qk(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) mma_bf16(c, a, b0, b1);
+  else mma_f16(c, a, b0, b1);
+}
+
+template <typename T, typename I>
+__global__ void __launch_bounds__(256) sink_attn_tc_kernel(const T* __restrict__ q, const T* __restrict__ kv,
+                                                           const I* __restrict__ idx, const T* __restrict__ sink,
+                                                           T* __restrict__ out, int Tt, int H, int S, int K,
+                                                           float scale, int sink_scalar) {
+  constexpr int D = 128;
+  extern __shared__ __align__(128) uint8_t smem[];
+  T* Qs = reinterpret_cast<T*>(smem);
+  T* Ks = Qs + 16 * kTcRow;                 // [2][128][kTcRow]
+  T* Vs = Ks + 2 * kTcRows * kTcRow;        // [2][128][kTcRow]
+  float* Ls = reinterpret_cast<float*>(Vs + 2 * kTcRows * kTcRow);  // [16][kTcSt]
+  __half* Ps = reinterpret_cast<__half*>(Ls + 16 * kTcSt);          // [16][kTcPst]
+  int* valid = reinterpret_cast<int*>(Ps + 16 * kTcPst);            // [2][128]
+  float* mh = reinterpret_cast<float*>(valid + 2 * kTcRows);        // [16] running max
+  float* lh = mh + 16;                                              // [16] running sum
+  float* sch = lh + 16;                                             // [16] this tile's rescale
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, t = lane & 3;
+  const long long bt = blockIdx.x;
+  const int b = static_cast<int>(bt / Tt);
+  const I* ip = idx ? idx + bt * K : nullptr;
+  const T* kvb = kv + static_cast<long long>(b) * S * 2 * D;
+  // queries: heads past H are zero rows
+  for (int i = tid; i < 16 * 16; i += 256) {
+    const int h = i >> 4, c = i & 15;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (h < H) v = *reinterpret_cast<const uint4*>(q + (bt * H + h) * D + c * 8);
+    *reinterpret_cast<uint4*>(Qs + h * kTcRow + c * 8) = v;
+  }
+  if (tid < 16) {
+    mh[tid] = -INFINITY;
+    lh[tid] = 0.f;
+  }
+  const int ntiles = (K + kTcRows - 1) / kTcRows;
+  auto load_tile = [&](int j, int buf) {
+    T* kd = Ks + buf * kTcRows * kTcRow;
+    T* vd = Vs + buf * kTcRows * kTcRow;
+    for (int i = tid; i < kTcRows * 16; i += 256) {
+      const int r = i >> 4, c = i & 15, e = j * kTcRows + r;
+      long long src = -1;
+      if (e < K) src = ip ? static_cast<long long>(ip[e]) : e;
+      const bool ok = src >= 0 && src < S;
+      if (c == 0) valid[buf * kTcRows + r] = ok;
+      if (ok) {
+        cp_async16(kd + r * kTcRow + c * 8, kvb + src * 2 * D + c * 8);
+        cp_async16(vd + r * kTcRow + c * 8, kvb + src * 2 * D + D + c * 8);
+      } else {
+        *reinterpret_cast<uint4*>(kd + r * kTcRow + c * 8) = make_uint4(0, 0, 0, 0);
+        *reinterpret_cast<uint4*>(vd + r * kTcRow + c * 8) = make_uint4(0, 0, 0, 0);
+      }
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  float oacc[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
+  if (ntiles > 0) load_tile(0, 0);
+  for (int j = 0; j < ntiles; ++j) {
+    const int buf = j & 1;
+    if (j + 1 < ntiles) {
+      load_tile(j + 1, buf ^ 1);
+      asm volatile("cp.async.wait_group 1;" ::: "memory");
+    } else {
+      asm volatile("cp.async.wait_group 0;" ::: "memory");
+    }
+    __syncthreads();
+    // ---- S: warp w scores sources [16 w, 16 w + 16) for all 16 heads
+    {
+      const T* kt = Ks + buf * kTcRows * kTcRow + warp * 16 * kTcRow;
+      float c[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
+#pragma unroll
+      for (int kk = 0; kk < D / 16; ++kk) {
+        uint32_t a[4], b0, b1, b2, b3;
+        ldsm_x4(a[0], a[1], a[2], a[3], Qs + (lane & 15) * kTcRow + kk * 16 + (lane >> 4) * 8);
+        ldsm_x4(b0, b1, b2, b3, kt + ((lane & 7) + ((lane >> 4) << 3)) * kTcRow + kk * 16 + ((lane >> 3) & 1) * 8);
+        tc_mma_qk<T>(c[0], a, b0, b1);
+        tc_mma_qk<T>(c[1], a, b2, b3);
+      }
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int h = g + (e >> 1) * 8, col = warp * 16 + nt * 8 + 2 * t + (e & 1);
+          Ls[h * kTcSt + col] = valid[buf * kTcRows + col] ? c[nt][e] * scale : -INFINITY;
+        }
+    }
+    __syncthreads();
+    // ---- online softmax: warp w owns heads 2w, 2w + 1; 4 sources per lane
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      const int h = 2 * warp + hh;
+      const float4 z = *reinterpret_cast<const float4*>(Ls + h * kTcSt + 4 * lane);
+      const float mt = warp_max(fmaxf(fmaxf(z.x, z.y), fmaxf(z.z, z.w)));
+      const float mo = mh[h], mn = fmaxf(mo, mt);
+      const float base = mn == -INFINITY ? 0.f : mn;
+      const float p0 = __expf(z.x - base), p1 = __expf(z.y - base), p2 = __expf(z.z - base), p3 = __expf(z.w - base);
+      *reinterpret_cast<uint2*>(Ps + h * kTcPst + 4 * lane) = make_uint2(pack_half2(p0, p1), pack_half2(p2, p3));
+      const float ps = warp_sum((p0 + p1) + (p2 + p3));
+      const float sc = mo == -INFINITY ? 0.f : __expf(mo - base);
+      if (lane == 0) {
+        lh[h] = lh[h] * sc + ps;
+        mh[h] = mn;
+        sch[h] = sc;
+      }
+    }
+    __syncthreads();
+    // ---- O = O * rescale + P V: warp w owns output dims [16 w, 16 w + 16)
+    {
+      const float s_lo = sch[g], s_hi = sch[g + 8];
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) {
+        oacc[nt][0] *= s_lo; oacc[nt][1] *= s_lo;
+        oacc[nt][2] *= s_hi; oacc[nt][3] *= s_hi;
+      }
+      const T* vt = Vs + buf * kTcRows * kTcRow;
+#pragma unroll 4
+      for (int kt = 0; kt < kTcRows / 16; ++kt) {
+        uint32_t a[4];
+        ldsm_x4(a[0], a[1], a[2], a[3], Ps + (lane & 15) * kTcPst + kt * 16 + (lane >> 4) * 8);
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+          uint32_t b0, b1;
+          asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0,%1}, [%2];"
+                       : "=r"(b0), "=r"(b1)
+                       : "r"(smem_u32(vt + (kt * 16 + (lane & 7) + ((lane >> 3) & 1) * 8) * kTcRow + warp * 16 +
+                                      nt * 8)));
+          if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+            b0 = bf2_to_h2(b0);
+            b1 = bf2_to_h2(b1);
+          }
+          mma_f16(oacc[nt], a, b0, b1);
+        }
+      }
+    }
+    __syncthreads();  // this tile's buffers are reused by the load two tiles on
+  }
+  // ---- sink and output: rows g and g + 8 of each n-tile
+#pragma unroll
+  for (int hr = 0; hr < 2; ++hr) {
+    const int h = g + hr * 8;
+    if (h >= H) continue;
+    const float sk = tofl<T>(sink[sink_scalar ? 0 : h]);
+    const float m = mh[h], M = fmaxf(m, sk);
+    const float a = m == -INFINITY ? 0.f : __expf(m - M);
+    const float inv = a / (lh[h] * a + __expf(sk - M));
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      const int d = warp * 16 + nt * 8 + 2 * t;
+      T* o = out + (bt * H + h) * D + d;
+      o[0] = fromfl<T>(oacc[nt][2 * hr] * inv);
+      o[1] = fromfl<T>(oacc[nt][2 * hr + 1] * inv);
+    }
+  }
+}
+
 template <typename T, typename I>
 static void launch_sink_attn(const void* q, const void* kv, const void* idx, const void* sink, void* out, int B,
                              int Tt, int H, int D, int S, int K, float scale, int sink_scalar, cudaStream_t st) {
@@ -108,6 +284,17 @@ static void launch_sink_attn(const void* q, const void* kv, const void* idx, con
                                      static_cast<const I*>(idx), static_cast<const T*>(sink),
                                      static_cast<T*>(out), B, Tt, H, D, S, K, scale, sink_scalar);
   };
+  if constexpr (!std::is_same<T, float>::value) {
+    if (D == 128 && H <= 16) {  // the tensor-core path
+      if (ensure_smem_attr(reinterpret_cast<const void*>(sink_attn_tc_kernel<T, I>), kTcSmem,
+                           "sparse_sink_attention") == 0) {
+        sink_attn_tc_kernel<T, I><<<static_cast<unsigned>(static_cast<long long>(B) * Tt), 256, kTcSmem, st>>>(
+            static_cast<const T*>(q), static_cast<const T*>(kv), static_cast<const I*>(idx),
+            static_cast<const T*>(sink), static_cast<T*>(out), Tt, H, S, K, scale, sink_scalar);
+        return;
+      }
+    }
+  }
   if (D <= 32) args(sink_attn_kernel<T, I, 1>);
   else if (D <= 64) args(sink_attn_kernel<T, I, 2>);
   else if (D <= 128) args(sink_attn_kernel<T, I, 4>);
