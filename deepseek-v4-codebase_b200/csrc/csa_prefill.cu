@@ -202,11 +202,17 @@ __device__ __forceinline__ uint32_t s8x2h2(uint32_t w) {
 // ---------------------------------------------------------------- selection
 // One warp: the K-th largest key of n <= CAP entries (key desc, block asc),
 // keeping exactly min(K, n) of them at the front of buf (order not kept).
-// Returns the threshold key.  The keys sit in registers (16 per lane) and
+// Returns the threshold key.  With slack > 0 (streaming prunes) the radix
+// walk stops as soon as the keys at or above the current prefix number at
+// most K + slack: those are all kept, the returned threshold is that prefix
+// and *kept their count.  Every key of the exact top-K is among them, and a
+// later key equal to the threshold cannot enter the top-K (at least K kept
+// keys are >= it with lower block indices), so insertion stays "key > thr".  The keys sit in registers (16 per lane) and
 // an MSB-first bitwise radix select counts matches with warp reductions:
 // no shared-memory atomics, which serialise when keys share their top bits.
 template <int CAP>
-__device__ __forceinline__ uint32_t warp_prune(uint2* buf, int n, int K, int lane) {
+__device__ __forceinline__ uint32_t warp_prune(uint2* buf, int n, int K, int lane, int slack = 0,
+                                               int* kept = nullptr) {
   constexpr int PER = CAP / 32;
   uint32_t kk[PER];
 #pragma unroll
@@ -230,6 +236,8 @@ __device__ __forceinline__ uint32_t warp_prune(uint2* buf, int n, int K, int lan
   const int top = diff ? 31 - __clz(diff) : -1;
   uint32_t prefix = top >= 31 ? 0u : (kand & ~((2u << top) - 1u)), R = static_cast<uint32_t>(K);
   if (top < 0) prefix = kand;  // all keys equal
+  uint32_t inrange = static_cast<uint32_t>(n);  // keys matching prefix on the bits walked so far
+  bool early = false;
 #pragma unroll 1
   for (int bit = top; bit >= 0; --bit) {
     const uint32_t want = prefix | (1u << bit), hm = ~((1u << bit) - 1u);
@@ -237,11 +245,36 @@ __device__ __forceinline__ uint32_t warp_prune(uint2* buf, int n, int K, int lan
 #pragma unroll
     for (int i = 0; i < PER; ++i) c += (kk[i] & hm) == want;
     c = __reduce_add_sync(0xffffffffu, c);
-    if (c >= R)
+    if (c >= R) {
       prefix = want;
-    else
+      inrange = c;
+    } else {
       R -= c;
+      inrange -= c;
+    }
+    // keys >= prefix (lower bits zero): the K - R above the range and the range itself
+    if (slack > 0 && static_cast<uint32_t>(K) - R + inrange <= static_cast<uint32_t>(K + slack)) {
+      early = true;
+      break;
+    }
   }
+  if (early) {  // keep every key >= prefix
+    uint32_t out = 0;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      if (i * 32 >= n) break;
+      const bool keep = i * 32 + lane < n && kk[i] >= prefix;
+      const uint2 e = keep ? buf[i * 32 + lane] : make_uint2(0, 0);
+      const uint32_t bal = __ballot_sync(0xffffffffu, keep);
+      __syncwarp();
+      if (keep) buf[out + __popc(bal & ((1u << lane) - 1u))] = e;
+      out += __popc(bal);
+      __syncwarp();
+    }
+    if (kept) *kept = static_cast<int>(out);
+    return prefix;
+  }
+  if (kept) *kept = min(K, n);
   const uint32_t thr = prefix, take_eq = R;
   uint32_t eq = 0;
 #pragma unroll
@@ -667,10 +700,13 @@ __global__ void __launch_bounds__(kThreads, 1) csa_prefill_index_kernel(Params p
           for (uint32_t mk = need; mk; mk &= mk - 1u) {
             const int qi = 4 * e + __ffs(mk) - 1;
             const int n = static_cast<int>(m->cnt[qi]);
-            const uint32_t t = warp_prune<C::CAP>(cbuf + qi * C::CAP, n, p.top_k, lane);
+            // a tile adds at most kTileKeys keys: the slack keeps that much room
+            const int slack = max(0, min(64, C::CAP - p.top_k - kTileKeys));
+            int kept = 0;
+            const uint32_t t = warp_prune<C::CAP>(cbuf + qi * C::CAP, n, p.top_k, lane, slack, &kept);
             if (lane == 0) {
               m->thr[qi] = t;
-              m->cnt[qi] = static_cast<uint32_t>(min(p.top_k, n));
+              m->cnt[qi] = static_cast<uint32_t>(kept);
             }
             ++nprune;
             __syncwarp();
