@@ -701,7 +701,7 @@ __global__ void __launch_bounds__(kThreads, 1) csa_prefill_index_kernel(Params p
             const int qi = 4 * e + __ffs(mk) - 1;
             const int n = static_cast<int>(m->cnt[qi]);
             // a tile adds at most kTileKeys keys: the slack keeps that much room
-            const int slack = max(0, min(64, C::CAP - p.top_k - kTileKeys));
+            const int slack = max(0, min(32, C::CAP - p.top_k - kTileKeys));
             int kept = 0;
             const uint32_t t = warp_prune<C::CAP>(cbuf + qi * C::CAP, n, p.top_k, lane, slack, &kept);
             if (lane == 0) {
