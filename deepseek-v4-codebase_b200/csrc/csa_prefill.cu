@@ -565,6 +565,12 @@ __global__ void __launch_bounds__(kThreads, 1) csa_prefill_index_kernel(Params p
     uint32_t* xbuf = reinterpret_cast<uint32_t*>(smem + C::OFF_X);
     long long t_wait = 0, t_ld = 0, t_ins = 0, t_prune = 0;
     int nprune = 0;
+    // threshold, buffer count and causal limit of this warp's four queries
+    // (owner phase), kept in registers for the whole stream
+    uint32_t thr_r[4] = {0u, 0u, 0u, 0u}, cnt_r[4] = {0u, 0u, 0u, 0u};
+    int vis_r[4];
+#pragma unroll
+    for (int qq = 0; qq < 4; ++qq) vis_r[qq] = m->vis[4 * e + qq];
     for (int j = 0; j < ntiles; ++j) {
       const int st = j & 1, use = j >> 1;
       long long c0 = clock64();
@@ -665,15 +671,13 @@ __global__ void __launch_bounds__(kThreads, 1) csa_prefill_index_kernel(Params p
       // owner phase: queries 4e .. 4e + 3, all 128 keys of the tile; the
       // four queries are processed side by side (independent latency chains)
       {
-        uint32_t kv[4][4], pm[4], npass[4], thrq[4], cntq[4];
-        int visq[4];
+        uint32_t kv[4][4], pm[4], npass[4];
+        uint32_t (&thrq)[4] = thr_r, (&cntq)[4] = cnt_r;
+        const int(&visq)[4] = vis_r;
         const int b0 = j * kTileKeys + 4 * lane;
 #pragma unroll
         for (int qq = 0; qq < 4; ++qq) {
           const int qi = 4 * e + qq;
-          visq[qq] = m->vis[qi];
-          thrq[qq] = m->thr[qi];
-          cntq[qq] = m->cnt[qi];
           const uint4 v4 = *reinterpret_cast<const uint4*>(xo + qi * kTileKeys + 4 * lane);
           kv[qq][0] = v4.x; kv[qq][1] = v4.y; kv[qq][2] = v4.z; kv[qq][3] = v4.w;
         }
@@ -698,24 +702,25 @@ __global__ void __launch_bounds__(kThreads, 1) csa_prefill_index_kernel(Params p
         if (need) {
           const long long cp0 = clock64();
           for (uint32_t mk = need; mk; mk &= mk - 1u) {
-            const int qi = 4 * e + __ffs(mk) - 1;
-            const int n = static_cast<int>(m->cnt[qi]);
+            const int qq = __ffs(mk) - 1, qi = 4 * e + qq;
+            // register arrays indexed without local memory
+            const int n = static_cast<int>(qq == 0 ? cntq[0] : qq == 1 ? cntq[1] : qq == 2 ? cntq[2] : cntq[3]);
             // a tile adds at most kTileKeys keys: the slack keeps that much room
             const int slack = max(0, min(32, C::CAP - p.top_k - kTileKeys));
             int kept = 0;
             const uint32_t t = warp_prune<C::CAP>(cbuf + qi * C::CAP, n, p.top_k, lane, slack, &kept);
-            if (lane == 0) {
-              m->thr[qi] = t;
-              m->cnt[qi] = static_cast<uint32_t>(kept);
-            }
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+              if (k == qq) {
+                thrq[k] = t;
+                cntq[k] = static_cast<uint32_t>(kept);
+              }
             ++nprune;
             __syncwarp();
           }
           t_prune += clock64() - cp0;
 #pragma unroll
           for (int qq = 0; qq < 4; ++qq) {
-            thrq[qq] = m->thr[4 * e + qq];
-            cntq[qq] = m->cnt[4 * e + qq];
             pm[qq] = 0;
             npass[qq] = 0;
 #pragma unroll
@@ -731,26 +736,25 @@ __global__ void __launch_bounds__(kThreads, 1) csa_prefill_index_kernel(Params p
         const uint32_t lt = (1u << lane) - 1u;
 #pragma unroll
         for (int qq = 0; qq < 4; ++qq) {
+          if (npass[qq] == 0) continue;  // warp-uniform: nothing passes (the common case late on)
           uint2* qb = cbuf + (4 * e + qq) * C::CAP;
           uint32_t pos = cntq[qq] + __popc(bal[qq][0] & lt) + __popc(bal[qq][1] & lt) + __popc(bal[qq][2] & lt) +
                          __popc(bal[qq][3] & lt);
 #pragma unroll
           for (int i = 0; i < 4; ++i)
             if ((pm[qq] >> i) & 1u) qb[pos++] = make_uint2(kv[qq][i], static_cast<uint32_t>(b0 + i));
+          cntq[qq] += npass[qq];
         }
-        __syncwarp();
-        if (lane < 4) {
-          m->thr[4 * e + lane] = lane == 0 ? thrq[0] : lane == 1 ? thrq[1] : lane == 2 ? thrq[2] : thrq[3];
-          m->cnt[4 * e + lane] = lane == 0 ? cntq[0] + npass[0]
-                                 : lane == 1 ? cntq[1] + npass[1]
-                                 : lane == 2 ? cntq[2] + npass[2]
-                                             : cntq[3] + npass[3];
-        }
-        __syncwarp();
+        __syncwarp();  // appends land before the next tile's prunes read them
       }
       t_ins += clock64() - c2;
       named_sync(1, 256);  // the exchange area is rewritten by the next tile
     }
+    if (lane < 4) {
+      m->thr[4 * e + lane] = lane == 0 ? thr_r[0] : lane == 1 ? thr_r[1] : lane == 2 ? thr_r[2] : thr_r[3];
+      m->cnt[4 * e + lane] = lane == 0 ? cnt_r[0] : lane == 1 ? cnt_r[1] : lane == 2 ? cnt_r[2] : cnt_r[3];
+    }
+    __syncwarp();
     if (tid == 256 && p.dbg) {
       p.dbg[blockIdx.x * 16 + 8] = t_wait;
       p.dbg[blockIdx.x * 16 + 9] = t_ld;
