@@ -1382,41 +1382,62 @@ __global__ void __launch_bounds__(kQThreads, 1) hca_attend_kernel(HcaParams p) {
   }
   __syncthreads();
   stamp(6);
-  // ---- O = P V; warp w owns output dims [8w, 8w+8); partials go to the
-  // head's owner CTA, which merges them
+  // ---- O = P V; warp w owns output dims [16 (w % 8), +16) over the 16-row
+  // tiles of parity w / 8, so each warp reads half of P (P is every warp's A
+  // operand: shared-memory reads of P, not the MMAs, bound this phase); the
+  // odd-parity half is added through the dead logit area, then the sums go to
+  // the head's owner CTA, which merges them
   const int hpc = (p.H + kHcaCS - 1) / kHcaCS;
   {
-    // two accumulator chains over the compressed tiles
-    float orot[4] = {0, 0, 0, 0}, orot2[4] = {0, 0, 0, 0}, owin[4] = {0, 0, 0, 0};
-    for (int kt = 0; kt < ntc; ++kt) {
-      uint32_t a[4], b0, b1;
+    static_assert(kQWarps == 16 && 16 * C::LST >= 8 * 32 * 16, "P V split: 16 warps, exchange fits the logits");
+    const int dg = warp & 7, kh = warp >> 3;
+    float orot[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}}, owin[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
+    const int vr = (lane & 7) + ((lane >> 3) & 1) * 8, vc = dg * 16 + (lane >> 4) * 8;  // x4.trans source
+    for (int kt = kh; kt < ntc; kt += 2) {
+      uint32_t a[4], b[4];
       ldsm_x4(a[0], a[1], a[2], a[3], P + (lane & 15) * C::PST + kt * 16 + (lane >> 4) * 8);
-      asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0,%1}, [%2];"
-                   : "=r"(b0), "=r"(b1)
-                   : "r"(smem_u32(Kc + (kt * 16 + (lane & 7) + ((lane >> 3) & 1) * 8) * C::KROW + warp * 8)));
-      mma_f16((kt & 1) ? orot2 : orot, a, b0, b1);
+      ldsm_x4_t(b[0], b[1], b[2], b[3], Kc + (kt * 16 + vr) * C::KROW + vc);
+      mma_f16(orot[0], a, b[0], b[1]);
+      mma_f16(orot[1], a, b[2], b[3]);
     }
-#pragma unroll
-    for (int e = 0; e < 4; ++e) orot[e] += orot2[e];
-    for (int kt = ntc; kt < ntc + ntw; ++kt) {
-      uint32_t a[4], b0, b1;
+    for (int kt = ntc + kh; kt < ntc + ntw; kt += 2) {
+      uint32_t a[4], b[4];
       ldsm_x4(a[0], a[1], a[2], a[3], P + (lane & 15) * C::PST + kt * 16 + (lane >> 4) * 8);
-      const uint8_t* wt = winb + (kt - ntc) * 16 * kWRow;
-      asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0,%1}, [%2];"
-                   : "=r"(b0), "=r"(b1)
-                   : "r"(smem_u32(wt + ((lane & 7) + ((lane >> 3) & 1) * 8) * kWRow + warp * 16)));
-      mma_f16(owin, a, bf2_to_h2(b0), bf2_to_h2(b1));
+      ldsm_x4_t(b[0], b[1], b[2], b[3], winb + ((kt - ntc) * 16 + vr) * kWRow + vc * 2);
+      mma_f16(owin[0], a, bf2_to_h2(b[0]), bf2_to_h2(b[1]));
+      mma_f16(owin[1], a, bf2_to_h2(b[2]), bf2_to_h2(b[3]));
     }
+    float4* xh = reinterpret_cast<float4*>(logit) + (dg * 32 + lane) * 4;  // [8 dim groups][32 lanes][16 floats]
+    if (kh == 1) {
+      xh[0] = make_float4(orot[0][0], orot[0][1], orot[0][2], orot[0][3]);
+      xh[1] = make_float4(orot[1][0], orot[1][1], orot[1][2], orot[1][3]);
+      xh[2] = make_float4(owin[0][0], owin[0][1], owin[0][2], owin[0][3]);
+      xh[3] = make_float4(owin[1][0], owin[1][1], owin[1][2], owin[1][3]);
+    }
+    __syncthreads();
     asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
+    if (kh == 0) {
+      float4 x[4];
 #pragma unroll
-    for (int e = 0; e < 4; e += 2) {
-      const int h = g + (e >> 1) * 8;
-      if (h < p.H) {
-        const int owner = h / hpc, lh = h % hpc;
-        float* slot = cg::this_cluster().map_shared_rank(merge + (r * C::HPC + lh) * C::SLOT, owner);
-        const int dd = warp * 8 + 2 * t;
-        *reinterpret_cast<float2*>(slot + 4 + dd) = make_float2(orot[e], orot[e + 1]);
-        *reinterpret_cast<float2*>(slot + 4 + kHeadDim + dd) = make_float2(owin[e], owin[e + 1]);
+      for (int i = 0; i < 4; ++i) x[i] = xh[i];
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) {
+        orot[nt][0] += x[nt].x; orot[nt][1] += x[nt].y; orot[nt][2] += x[nt].z; orot[nt][3] += x[nt].w;
+        owin[nt][0] += x[2 + nt].x; owin[nt][1] += x[2 + nt].y; owin[nt][2] += x[2 + nt].z; owin[nt][3] += x[2 + nt].w;
+      }
+#pragma unroll
+      for (int e = 0; e < 4; e += 2) {
+        const int h = g + (e >> 1) * 8;
+        if (h < p.H) {
+          const int owner = h / hpc, lh = h % hpc;
+          float* slot = cg::this_cluster().map_shared_rank(merge + (r * C::HPC + lh) * C::SLOT, owner);
+#pragma unroll
+          for (int nt = 0; nt < 2; ++nt) {
+            const int dd = dg * 16 + nt * 8 + 2 * t;
+            *reinterpret_cast<float2*>(slot + 4 + dd) = make_float2(orot[nt][e], orot[nt][e + 1]);
+            *reinterpret_cast<float2*>(slot + 4 + kHeadDim + dd) = make_float2(owin[nt][e], owin[nt][e + 1]);
+          }
+        }
       }
     }
   }
