@@ -991,26 +991,34 @@ __global__ void __launch_bounds__(kQThreads, CS > 1 ? 2 : 1) csa_attend_kernel(Q
   }
   __syncthreads();
   stamp(8, tid == 0);
-  // ---- O = P V; warp w owns output dims [8w, 8w+8); partials go to the
-  // head's owner CTA (slot r), which merges them
+  // ---- O = P V.  Warps 0-7 take the compressed tiles, warps 8-15 the
+  // window tiles, each warp output dims [16 (w % 8), +16): every warp reads
+  // only its own part of P (P is every warp's A operand; its shared-memory
+  // reads, not the MMAs, bound this phase) and the two parts land in
+  // separate fields of the merge slot.  Partials go to the head's owner CTA
+  // (slot r), which merges them
   {
-    float orot[4] = {0, 0, 0, 0}, owin[4] = {0, 0, 0, 0};
-    for (int kt = 0; kt < ntc; ++kt) {
-      uint32_t a[4], b0, b1;
-      ldsm_x4(a[0], a[1], a[2], a[3], P + (lane & 15) * C::PST + kt * 16 + (lane >> 4) * 8);
-      asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0,%1}, [%2];"
-                   : "=r"(b0), "=r"(b1)
-                   : "r"(smem_u32(Kc + (kt * 16 + (lane & 7) + ((lane >> 3) & 1) * 8) * C::KROW + warp * 8)));
-      mma_f16(orot, a, b0, b1);
-    }
-    for (int kt = ntc; kt < ntc + ntw; ++kt) {
-      uint32_t a[4], b0, b1;
-      ldsm_x4(a[0], a[1], a[2], a[3], P + (lane & 15) * C::PST + kt * 16 + (lane >> 4) * 8);
-      const uint8_t* wt = winb + (kt - ntc) * 16 * kWRow;
-      asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0,%1}, [%2];"
-                   : "=r"(b0), "=r"(b1)
-                   : "r"(smem_u32(wt + ((lane & 7) + ((lane >> 3) & 1) * 8) * kWRow + warp * 16)));
-      mma_f16(owin, a, bf2_to_h2(b0), bf2_to_h2(b1));
+    static_assert(kQWarps == 16, "P V split: 16 warps");
+    const int dg = warp & 7;
+    const bool win_part = warp >= 8;
+    float o[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
+    const int vr = (lane & 7) + ((lane >> 3) & 1) * 8, vc = dg * 16 + (lane >> 4) * 8;  // x4.trans source
+    if (!win_part) {
+      for (int kt = 0; kt < ntc; ++kt) {
+        uint32_t a[4], bb[4];
+        ldsm_x4(a[0], a[1], a[2], a[3], P + (lane & 15) * C::PST + kt * 16 + (lane >> 4) * 8);
+        ldsm_x4_t(bb[0], bb[1], bb[2], bb[3], Kc + (kt * 16 + vr) * C::KROW + vc);
+        mma_f16(o[0], a, bb[0], bb[1]);
+        mma_f16(o[1], a, bb[2], bb[3]);
+      }
+    } else {
+      for (int kt = ntc; kt < ntc + ntw; ++kt) {
+        uint32_t a[4], bb[4];
+        ldsm_x4(a[0], a[1], a[2], a[3], P + (lane & 15) * C::PST + kt * 16 + (lane >> 4) * 8);
+        ldsm_x4_t(bb[0], bb[1], bb[2], bb[3], winb + ((kt - ntc) * 16 + vr) * kWRow + vc * 2);
+        mma_f16(o[0], a, bf2_to_h2(bb[0]), bf2_to_h2(bb[1]));
+        mma_f16(o[1], a, bf2_to_h2(bb[2]), bf2_to_h2(bb[3]));
+      }
     }
     const int hpc = (p.H + CS - 1) / CS;
     if constexpr (CS > 1) asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
@@ -1021,9 +1029,10 @@ __global__ void __launch_bounds__(kQThreads, CS > 1 ? 2 : 1) csa_attend_kernel(Q
         const int owner = h / hpc, lh = h % hpc;
         float* slot = merge + (r * C::HPC + lh) * C::SLOT;
         if constexpr (CS > 1) slot = cg::this_cluster().map_shared_rank(slot, owner);
-        const int dd = warp * 8 + 2 * t;
-        *reinterpret_cast<float2*>(slot + 4 + dd) = make_float2(orot[e], orot[e + 1]);
-        *reinterpret_cast<float2*>(slot + 4 + kHeadDim + dd) = make_float2(owin[e], owin[e + 1]);
+        slot += 4 + (win_part ? kHeadDim : 0);
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+          *reinterpret_cast<float2*>(slot + dg * 16 + nt * 8 + 2 * t) = make_float2(o[nt][e], o[nt][e + 1]);
       }
     }
   }
