@@ -8,6 +8,7 @@ from __future__ import annotations
 import os
 import shutil
 import subprocess
+from concurrent.futures import ThreadPoolExecutor
 from pathlib import Path
 from typing import List, Optional
 
@@ -44,21 +45,40 @@ def needs_build() -> bool:
 
 
 def build(force: bool = False, verbose: bool = False, extra: Optional[List[str]] = None) -> Path:
+    """Compile every source to an object in parallel, then link the library.
+
+    Objects go to ``_build/`` beside the package (git-ignored); only the
+    linked ``libaether_b200.so`` is loaded.
+    """
     if not force and not needs_build():
         return OUT
     nvcc = find_nvcc()
     if nvcc is None:
         raise RuntimeError("nvcc was not found; cannot build the Aether sm_100a kernels")
+    objdir = PKG / "_build"
+    objdir.mkdir(exist_ok=True)
+    compile_flags = [f for f in NVCC_FLAGS if f != "-shared"]
+
+    def compile_one(src: str) -> Path:
+        obj = objdir / (Path(src).stem + ".o")
+        cmd = [nvcc, *compile_flags, "-I", str(INCLUDE), *(extra or []), "-c", "-o", str(obj), str(CSRC / src)]
+        if verbose:
+            print(" ".join(cmd))
+        res = subprocess.run(cmd, capture_output=True, text=True)
+        if res.returncode != 0:
+            raise RuntimeError(f"nvcc failed on {src} ({res.returncode}):\n{res.stdout}\n{res.stderr}")
+        return obj
+
+    with ThreadPoolExecutor(max_workers=max(1, min(len(SOURCES), os.cpu_count() or 1))) as pool:
+        objs = list(pool.map(compile_one, SOURCES))
     tmp = OUT.with_suffix(".so.tmp")
-    cmd = [nvcc, *NVCC_FLAGS, "-I", str(INCLUDE), *(extra or []), "-o", str(tmp), *[str(CSRC / s) for s in SOURCES]]
-    if verbose:
-        print(" ".join(cmd))
+    cmd = [nvcc, "-gencode", "arch=compute_100a,code=sm_100a", "-shared", "-Xcompiler", "-fPIC",
+           "-o", str(tmp), *[str(o) for o in objs]]
     res = subprocess.run(cmd, capture_output=True, text=True)
     if res.returncode != 0:
-        raise RuntimeError(f"nvcc failed ({res.returncode}):\n{res.stdout}\n{res.stderr}")
+        raise RuntimeError(f"nvcc link failed ({res.returncode}):\n{res.stdout}\n{res.stderr}")
     os.replace(tmp, OUT)
     return OUT
-
 
 if __name__ == "__main__":
     print(build(force=True, verbose=True))
