@@ -195,6 +195,9 @@ struct QMisc {
   uint32_t take_eq;
   uint32_t nvalid;
   uint32_t nown;
+  // selection rescale: smallest / largest valid key, smallest per-thread
+  // maximum key, threads holding a valid key
+  uint32_t kmin, kmax, tmin, nact;
   float m_h[kMaxHeads];
   float l_h[kMaxHeads];
 };
@@ -583,6 +586,10 @@ __global__ void __launch_bounds__(kQThreads, CS > 1 ? 2 : 1) csa_attend_kernel(Q
     misc->nvalid = 0;
     misc->nown = 0;
     misc->ncand = 0;
+    misc->kmin = 0xFFFFFFFFu;
+    misc->kmax = 0;
+    misc->tmin = 0xFFFFFFFFu;
+    misc->nact = 0;
   }
   // window rows other than the newest are cache state: prefetch them now
   {
@@ -651,29 +658,67 @@ __global__ void __launch_bounds__(kQThreads, CS > 1 ? 2 : 1) csa_attend_kernel(Q
     // any update (the key loads above are already in flight)
     __syncthreads();
     {
-      uint32_t cnt = 0;
+      uint32_t cnt = 0, lo = 0xFFFFFFFFu, hi = 0;
   #pragma unroll
       for (int j = 0; j < PER; ++j) {
         kr[j] = i0 + j < n ? kr[j] : 0u;  // key 0 = no block
         if (kr[j]) {
-          if (need_select) atomicAdd(&hist[kr[j] >> 19], 1u);
           ++cnt;
+          lo = min(lo, kr[j]);
+          hi = max(hi, kr[j]);
         }
       }
-  #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) cnt += __shfl_xor_sync(0xffffffffu, cnt, o);
-      if (lane == 0 && cnt) atomicAdd(&misc->nvalid, cnt);
+      const uint32_t tmax = hi;
+      cnt = __reduce_add_sync(0xffffffffu, cnt);
+      uint32_t tlo = 0, nact = 0;
+      if (need_select) {
+        lo = __reduce_min_sync(0xffffffffu, lo);
+        hi = __reduce_max_sync(0xffffffffu, hi);
+        tlo = __reduce_min_sync(0xffffffffu, tmax ? tmax : 0xFFFFFFFFu);
+        nact = __popc(__ballot_sync(0xffffffffu, tmax != 0u));
+      }
+      if (lane == 0 && cnt) {
+        atomicAdd(&misc->nvalid, cnt);
+        if (need_select) {
+          atomicMin(&misc->kmin, lo);
+          atomicMax(&misc->kmax, hi);
+          atomicMin(&misc->tmin, tlo);
+          atomicAdd(&misc->nact, nact);
+        }
+      }
     }
     __syncthreads();
-    stamp(3, tid == 0);
-    const int nvalid = static_cast<int>(misc->nvalid);
-    const int K = min(p.top_k, nvalid);
     if (p.score_out && !explicit_list && r == 0) {
       float* so = p.score_out + static_cast<long long>(b) * p.score_stride + chunk * kMaxKeys + i0;
   #pragma unroll
       for (int j = 0; j < PER; ++j)
         if (i0 + j < n) so[j] = __uint_as_float(kr[j] - 1u);
     }
+    if (need_select) {
+      // Rescale the keys before binning.  lo is a lower bound of the K-th
+      // largest key: when at least K threads hold a valid key, the smallest
+      // per-thread maximum (each of those threads holds a key >= it), else
+      // the smallest key.  Keys >= lo map to (k - lo + 2) << z, z chosen so
+      // the largest stays below 2^31 (bins of key >> 19 stay < 4096): a
+      // strictly increasing map.  Keys < lo are never taken and all map to 1,
+      // below every mapped key >= lo.  So the selected set, its ties and their
+      // position order are unchanged, while the band [lo, kmax] -- a narrow
+      // range of float exponents -- spreads over all 4096 top-level bins and
+      // the boundary bin holds a key or two instead of dozens.
+      const uint32_t kq = static_cast<uint32_t>(min(p.top_k, static_cast<int>(misc->nvalid)));
+      const uint32_t lo = misc->nact >= kq ? misc->tmin : misc->kmin;
+      const int z = __clz(misc->kmax - lo + 2u) - 1;
+  #pragma unroll
+      for (int j = 0; j < PER; ++j)
+        if (kr[j]) {
+          kr[j] = kr[j] >= lo ? (kr[j] - lo + 2u) << z : 1u;
+          atomicAdd(&hist[kr[j] >> 19], 1u);
+        }
+      __syncthreads();
+    }
+    stamp(3, tid == 0);
+    const int nvalid = static_cast<int>(misc->nvalid);
+    const int K = min(p.top_k, nvalid);
 
     // ------------------------------------------------------------- select
     // Result: every key > thr is taken, and the take_eq lowest-position keys
