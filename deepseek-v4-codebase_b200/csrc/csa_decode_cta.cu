@@ -85,6 +85,7 @@ struct QCfg {
   // gathered code rows [SL][RAWS] share the logits / P / O area (dead by then)
   static constexpr int A_RAW = A_LOG;
   static_assert(A_RAW + SL * RAWS <= A_END, "raw rows fit the shared area");
+  static_assert(A_QW >= S_END, "the query rows are copied in during the selection");
   static constexpr int REGION = ((A_END > S_END ? A_END : S_END) + 127) & ~127;
 
   static constexpr int OFF_WIN = REGION;                     // bf16 [WSL][kWRow] this CTA's window rows
@@ -97,7 +98,8 @@ struct QCfg {
   static constexpr int OFF_MISC = OFF_SCAN + 64 * 4;
   static constexpr int MISC_BYTES = 512;
   static constexpr int OFF_LUT = OFF_MISC + MISC_BYTES;      // u32 [256]: code byte -> half2
-  static constexpr int SMEM = OFF_LUT + 256 * 4;
+  static constexpr int OFF_CONST = OFF_LUT + 256 * 4;        // fp32 [128] rotation signs, [16] sinks
+  static constexpr int SMEM = OFF_CONST + (kHeadDim + kMaxHeads) * 4;
   static_assert(SMEM <= 227 * 1024, "fits one CTA per SM");
 };
 
@@ -599,11 +601,27 @@ __global__ void __launch_bounds__(kQThreads, CS > 1 ? 2 : 1) csa_attend_kernel(Q
       cp_async16(winb + (i >> 4) * kWRow + (i & 15) * 16, wsrc + (i >> 4) * kHeadDim + (i & 15) * 8);
     asm volatile("cp.async.commit_group;" ::: "memory");
   }
+  // model constants read late in the chain, staged now so their global-load
+  // latency is not paid there: the rotation signs and the sinks
+  if (!select_only) {
+    float* cst = reinterpret_cast<float*>(smem + C::OFF_CONST);
+    if (tid < kHeadDim) cst[tid] = __ldg(p.diag_kv + tid);
+    if (!p.part_o && tid < p.H) cst[kHeadDim + tid] = __ldg(p.sink + tid);
+  }
   // the block keys come from the score kernel (or a previous select)
   pdl_wait();
   // the staging slot's previous output copy must be done before this step's
   // stores (the __syncthreads below orders the other threads)
   if (p.step_flags && tid == 0) flag_wait(p.step_flags + 1, p.step_seq - 1u, p.err);
+  // this warp's query head (a step input, so after the wait) is copied into
+  // its plain-query row now: the load latency overlaps the selection instead
+  // of the gather (the row lies outside the selection's shared area)
+  if (!select_only) {
+    if (warp < p.H)
+      cp_async8(smem + C::A_QW + (warp * C::KROW + lane * 4) * 2,
+                p.q + (static_cast<long long>(b) * p.H + warp) * kHeadDim + lane * 4);
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  }
   stamp(2, tid == 0);
   // a short explicit list that needs no selection (prefill's top-k lists):
   // one candidate per thread; the winners are the valid keys in list order
@@ -915,8 +933,11 @@ __global__ void __launch_bounds__(kQThreads, CS > 1 ? 2 : 1) csa_attend_kernel(Q
     const int h = warp;  // 16 warps, 16 padded heads
     float v[4];
     if (h < p.H) {
-      const uint2 r4 = *reinterpret_cast<const uint2*>(p.q + (static_cast<long long>(b) * p.H + h) * kHeadDim + lane * 4);
-      *reinterpret_cast<uint2*>(Qw + h * C::KROW + lane * 4) = r4;
+      // committed groups only: the query row (the gather's copies are not
+      // committed yet); each lane waits for its own copy, the warp then shares
+      asm volatile("cp.async.wait_group 0;" ::: "memory");
+      __syncwarp();
+      const uint2 r4 = *reinterpret_cast<const uint2*>(Qw + h * C::KROW + lane * 4);
       const __nv_bfloat162* bb = reinterpret_cast<const __nv_bfloat162*>(&r4);
       const float2 f0 = __bfloat1622float2(bb[0]), f1 = __bfloat1622float2(bb[1]);
       v[0] = f0.x; v[1] = f0.y; v[2] = f1.x; v[3] = f1.y;
@@ -925,7 +946,7 @@ __global__ void __launch_bounds__(kQThreads, CS > 1 ? 2 : 1) csa_attend_kernel(Q
       v[0] = v[1] = v[2] = v[3] = 0.f;
     }
 #pragma unroll
-    for (int k = 0; k < 4; ++k) v[k] *= p.diag_kv[lane * 4 + k];
+    for (int k = 0; k < 4; ++k) v[k] *= reinterpret_cast<const float*>(smem + C::OFF_CONST)[lane * 4 + k];
     warp_wht128(v, lane);
     const float cn = 0.0883883461356163f;
     *reinterpret_cast<uint2*>(Qr + h * C::KROW + lane * 4) =
@@ -1118,14 +1139,14 @@ __global__ void __launch_bounds__(kQThreads, CS > 1 ? 2 : 1) csa_attend_kernel(Q
       warp_wht128(vr, lane);
       float o[4];
 #pragma unroll
-      for (int k = 0; k < 4; ++k) o[k] = vr[k] * 0.0883883461356163f * p.diag_kv[lane * 4 + k] + vw[k];
+      for (int k = 0; k < 4; ++k) o[k] = vr[k] * 0.0883883461356163f * reinterpret_cast<const float*>(smem + C::OFF_CONST)[lane * 4 + k] + vw[k];
       if (p.part_o) {
         *reinterpret_cast<float4*>(p.part_o + (static_cast<long long>(b) * p.H + h) * kHeadDim + lane * 4) =
             make_float4(o[0], o[1], o[2], o[3]);
         if (lane == 0)
           *reinterpret_cast<float2*>(p.part_ml + (static_cast<long long>(b) * p.H + h) * 2) = make_float2(M, L);
       } else {
-        const float sk = p.sink[h];
+        const float sk = reinterpret_cast<const float*>(smem + C::OFF_CONST)[kHeadDim + h];
         const float Ms = fmaxf(M, sk);
         const float a = M == -INFINITY ? 0.f : __expf(M - Ms);
         const float inv = a / (L * a + __expf(sk - Ms));
