@@ -82,9 +82,6 @@ struct QCfg {
   static constexpr int A_LOG = A_QW + 16 * KROW * 2;         // fp32 [16][LST]
   static constexpr int A_P = A_LOG + 16 * LST * 4;           // f16 [16][PST]
   static constexpr int A_END = A_P + 16 * PST * 2;
-  // gathered code rows [SL][RAWS] share the logits / P / O area (dead by then)
-  static constexpr int A_RAW = A_LOG;
-  static_assert(A_RAW + SL * RAWS <= A_END, "raw rows fit the shared area");
   static_assert(A_QW >= S_END, "the query rows are copied in during the selection");
   static constexpr int REGION = ((A_END > S_END ? A_END : S_END) + 127) & ~127;
 
@@ -897,16 +894,25 @@ __global__ void __launch_bounds__(kQThreads, CS > 1 ? 2 : 1) csa_attend_kernel(Q
 
   // --------------------------------------------------------- attention
   __half* Kc = reinterpret_cast<__half*>(smem + C::A_KC);
-  uint8_t* raw = smem + C::A_RAW;
   float* ks = reinterpret_cast<float*>(smem + C::A_KS);
   __half* Qr = reinterpret_cast<__half*>(smem + C::A_QR);
   __nv_bfloat16* Qw = reinterpret_cast<__nv_bfloat16*>(smem + C::A_QW);
   float* logit = reinterpret_cast<float*>(smem + C::A_LOG);
   __half* P = reinterpret_cast<__half*>(smem + C::A_P);
   const int ntc = (kc + 15) / 16, ntw = (wn + 15) / 16;
+  // winners' code rows and scales straight into registers (expanded to fp16
+  // below, after the query work, once the loads have landed)
+  constexpr int CPR = C::RB_KV / 16;
+  constexpr int NCH = (C::SL * CPR + kQThreads - 1) / kQThreads;
+  uint4 cw[NCH];
+  float csc[NCH];
   {
-    constexpr int CPR = C::RB_KV / 16;
-    for (int i = tid; i < kc * CPR; i += kQThreads) {
+#pragma unroll
+    for (int u = 0; u < NCH; ++u) {
+      const int i = tid + u * kQThreads;
+      cw[u] = make_uint4(0, 0, 0, 0);
+      csc[u] = 0.f;
+      if (i >= kc * CPR) continue;
       const int row = i / CPR, ch = i % CPR;
       const int blk = min(max(own[s0 + row], 0), max(nb - 1, 0));
       int phys;
@@ -920,8 +926,8 @@ __global__ void __launch_bounds__(kQThreads, CS > 1 ? 2 : 1) csa_attend_kernel(Q
         phys = pt[min(max((blk >> 6) - pt0, 0), kMaxKeys / kPage - 1)];
       }
       const uint8_t* pg = p.kv_pages + static_cast<long long>(phys) * C::PB_KV;
-      cp_async16(raw + row * C::RAWS + ch * 16, pg + (blk & 63) * C::RB_KV + ch * 16);
-      if (ch == 0) cp_async4(ks + row, pg + kPage * C::RB_KV + (blk & 63) * 4);
+      cw[u] = *reinterpret_cast<const uint4*>(pg + (blk & 63) * C::RB_KV + ch * 16);
+      if (ch == 0) csc[u] = *reinterpret_cast<const float*>(pg + kPage * C::RB_KV + (blk & 63) * 4);
     }
     // newest window row (written by the previous step), if it is in this slice
     if (wl > 0 && wl - 1 >= w0 && wl - 1 < w0 + wsl && tid < 16)
@@ -933,8 +939,8 @@ __global__ void __launch_bounds__(kQThreads, CS > 1 ? 2 : 1) csa_attend_kernel(Q
     const int h = warp;  // 16 warps, 16 padded heads
     float v[4];
     if (h < p.H) {
-      // committed groups only: the query row (the gather's copies are not
-      // committed yet); each lane waits for its own copy, the warp then shares
+      // committed groups only: the query row (the newest window row's copy is
+      // not committed yet); each lane waits for its own copy, the warp then shares
       asm volatile("cp.async.wait_group 0;" ::: "memory");
       __syncwarp();
       const uint2 r4 = *reinterpret_cast<const uint2*>(Qw + h * C::KROW + lane * 4);
@@ -955,29 +961,40 @@ __global__ void __launch_bounds__(kQThreads, CS > 1 ? 2 : 1) csa_attend_kernel(Q
   // zero window rows past wn up to the tile edge
   for (int i = tid; i < (ntw * 16 - wn) * 16; i += kQThreads)
     *reinterpret_cast<uint4*>(winb + (wn + (i >> 4)) * kWRow + (i & 15) * 16) = make_uint4(0, 0, 0, 0);
+  // codes -> exact fp16 rows; rows past kc zero-filled to the tile edge
+#pragma unroll
+  for (int u = 0; u < NCH; ++u) {
+    const int i = tid + u * kQThreads;
+    if (i >= kc * CPR) continue;
+    const int row = i / CPR, ch = i % CPR;
+    if (ch == 0) ks[row] = csc[u];
+    const uint32_t wd[4] = {cw[u].x, cw[u].y, cw[u].z, cw[u].w};
+    if (BITS == 4) {
+      __half* dst = Kc + row * C::KROW + ch * 32;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const uint32_t w = wd[k];
+        *reinterpret_cast<uint4*>(dst + k * 8) =
+            make_uint4(lut[w & 0xFFu], lut[(w >> 8) & 0xFFu], lut[(w >> 16) & 0xFFu], lut[w >> 24]);
+      }
+    } else {
+      __half* dst = Kc + row * C::KROW + ch * 16;
+      const bool lv = p.levels != nullptr;
+#pragma unroll
+      for (int k = 0; k < 2; ++k)
+        *reinterpret_cast<uint4*>(dst + k * 8) =
+            make_uint4(code8_pair(wd[2 * k], lut, lv), code8_pair(wd[2 * k] >> 16, lut, lv),
+                       code8_pair(wd[2 * k + 1], lut, lv), code8_pair(wd[2 * k + 1] >> 16, lut, lv));
+    }
+  }
+  for (int i = tid; i < (ntc * 16 - kc) * 16; i += kQThreads) {
+    const int row = kc + (i >> 4);
+    *reinterpret_cast<uint4*>(Kc + row * C::KROW + (i & 15) * 8) = make_uint4(0, 0, 0, 0);
+    if ((i & 15) == 0) ks[row] = 0.f;
+  }
   cp_async_commit_wait_all();
   __syncthreads();
   stamp(6, tid == 0);
-  // codes -> exact fp16 rows (rows past kc zero-filled to the tile edge)
-  for (int i = tid; i < ntc * 16 * 16; i += kQThreads) {
-    const int row = i >> 4, c8 = (i & 15) * 8;
-    uint4 o = make_uint4(0, 0, 0, 0);
-    if (row < kc) {
-      if (BITS == 4) {
-        const uint32_t w = *reinterpret_cast<const uint32_t*>(raw + row * C::RAWS + c8 / 2);
-        o = make_uint4(lut[w & 0xFFu], lut[(w >> 8) & 0xFFu], lut[(w >> 16) & 0xFFu], lut[w >> 24]);
-      } else {
-        const uint2 w = *reinterpret_cast<const uint2*>(raw + row * C::RAWS + c8);
-        const bool lv = p.levels != nullptr;
-        o = make_uint4(code8_pair(w.x, lut, lv), code8_pair(w.x >> 16, lut, lv), code8_pair(w.y, lut, lv),
-                       code8_pair(w.y >> 16, lut, lv));
-      }
-    } else if ((i & 15) == 0) {
-      ks[row] = 0.f;
-    }
-    *reinterpret_cast<uint4*>(Kc + row * C::KROW + c8) = o;
-  }
-  __syncthreads();
 
   // ---- S = Q K^T, one 16-source tile per warp iteration
   for (int tile = warp; tile < ntc + ntw; tile += kQWarps) {
