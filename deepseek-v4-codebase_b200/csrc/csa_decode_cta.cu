@@ -1234,7 +1234,8 @@ struct HCfg {
   static constexpr int OFF_MISC = OFF_MERGE + kHcaCS * HPC * SLOT * 4;  // m_h[16], l_h[16]
   static constexpr int OFF_LUT = OFF_MISC + 2 * kMaxHeads * 4;          // u32 [256]: code byte -> half2
   static constexpr int OFF_BAR = OFF_LUT + 256 * 4;        // u64 [4]: one per staged page
-  static constexpr int SMEM = OFF_BAR + 8 * kHcaPages;
+  static constexpr int OFF_CONST = OFF_BAR + 8 * kHcaPages;  // fp32 [128] rotation signs, [16] sinks
+  static constexpr int SMEM = OFF_CONST + (kHeadDim + kMaxHeads) * 4;
   static_assert(A_RAW % 128 == 0 && PB_KV % 16 == 0, "bulk-copy destinations are 16-byte aligned");
   static_assert(SMEM <= 227 * 1024, "fits one CTA per SM");
 };
@@ -1321,6 +1322,12 @@ __global__ void __launch_bounds__(kQThreads, 1) hca_attend_kernel(HcaParams p) {
     }
   }
   if ((BITS == 4 || p.levels) && tid < 256) lut[tid] = code_lut_entry(BITS, p.levels, static_cast<uint32_t>(tid));
+  // model constants (rotation signs, sinks) staged with the cache state
+  {
+    float* cst = reinterpret_cast<float*>(smem + C::OFF_CONST);
+    if (tid < kHeadDim) cst[tid] = __ldg(p.diag_kv + tid);
+    if (tid < p.H) cst[kHeadDim + tid] = __ldg(p.sink + tid);
+  }
   // window rows other than the newest are cache state
   const long long wbase = static_cast<long long>(b) * W;
   {
@@ -1379,7 +1386,7 @@ __global__ void __launch_bounds__(kQThreads, 1) hca_attend_kernel(HcaParams p) {
       v[0] = v[1] = v[2] = v[3] = 0.f;
     }
 #pragma unroll
-    for (int k = 0; k < 4; ++k) v[k] *= p.diag_kv[lane * 4 + k];
+    for (int k = 0; k < 4; ++k) v[k] *= reinterpret_cast<const float*>(smem + C::OFF_CONST)[lane * 4 + k];
     warp_wht128(v, lane);
     const float cn = 0.0883883461356163f;
     *reinterpret_cast<uint2*>(Qr + h * C::KROW + lane * 4) =
@@ -1546,7 +1553,7 @@ __global__ void __launch_bounds__(kQThreads, 1) hca_attend_kernel(HcaParams p) {
   for (int lh = warp; lh < hpc; lh += kQWarps) {
     const int h = r * hpc + lh;
     if (h >= p.H) break;
-    const float sk = p.sink[h];
+    const float sk = reinterpret_cast<const float*>(smem + C::OFF_CONST)[kHeadDim + h];
     float M = sk;
 #pragma unroll
     for (int rr = 0; rr < kHcaCS; ++rr) M = fmaxf(M, merge[(rr * C::HPC + lh) * C::SLOT]);
@@ -1566,7 +1573,7 @@ __global__ void __launch_bounds__(kQThreads, 1) hca_attend_kernel(HcaParams p) {
     const float inv = 1.f / L;
     float o[4];
 #pragma unroll
-    for (int k = 0; k < 4; ++k) o[k] = (vr[k] * 0.0883883461356163f * p.diag_kv[lane * 4 + k] + vw[k]) * inv;
+    for (int k = 0; k < 4; ++k) o[k] = (vr[k] * 0.0883883461356163f * reinterpret_cast<const float*>(smem + C::OFF_CONST)[lane * 4 + k] + vw[k]) * inv;
     __nv_bfloat162 o01 = __floats2bfloat162_rn(o[0], o[1]), o23 = __floats2bfloat162_rn(o[2], o[3]);
     *reinterpret_cast<uint2*>(p.out + (static_cast<long long>(b) * p.H + h) * kHeadDim + lane * 4) =
         make_uint2(*reinterpret_cast<uint32_t*>(&o01), *reinterpret_cast<uint32_t*>(&o23));
