@@ -329,6 +329,55 @@ def cpu_baseline(steps: int, warmup: int, budget_s: float, full_line: bool = Fal
 
 
 # ------------------------------------------------------------------- main
+ATTEND_PHASES = ["keys_rescale_histogram", "select", "compaction", "gather_expand", "qk", "softmax",
+                 "pv_merge", "final"]
+SCORE_PHASES = ["page_table_tma_issue", "wait_and_index_query_limbs", "page_wait", "scoring"]
+
+
+def phase_stamps(n, step, err, dev):
+    """Median per-CTA phase durations (us) of the two decode kernels over n
+    eager steps (no PDL), from the library's SM-clock phase stamps."""
+    import ctypes
+
+    import numpy as np
+    from aether_kernels import _lib
+
+    lib = _lib.load()
+    buf = torch.zeros(65536 + 8 * 8192, dtype=torch.int64, device=dev)
+    for i in range(3):
+        step(i, False)
+    torch.cuda.synchronize()
+    khz = getattr(torch.cuda.get_device_properties(dev), "clock_rate", 0)
+    if khz:
+        mhz = float(khz) / 1000.0
+    else:  # max SM clock from nvidia-smi (the stamps count SM cycles)
+        out = subprocess.run(["nvidia-smi", "-i", str(dev.index or 0), "--query-gpu=clocks.max.sm",
+                              "--format=csv,noheader,nounits"], capture_output=True, text=True).stdout
+        mhz = float(out.strip().splitlines()[0])
+    att, sco = [], []
+    lib.aether_csa_decode_set_debug_timer(ctypes.c_void_p(buf.data_ptr()))
+    try:
+        for i in range(n):
+            buf.zero_()
+            torch.cuda.synchronize()
+            step(i, False)
+            torch.cuda.synchronize()
+            a = buf[:65536].view(-1, 16).cpu().numpy().astype(np.float64)
+            a = a[(a[:, 2] > 0) & (a[:, 10] > 0)]
+            att.append(np.median(np.diff(a[:, 2:11], axis=1), axis=0))
+            sc = buf[65536:].view(-1, 8).cpu().numpy().astype(np.float64)
+            sc = sc[(sc[:, 0] > 0) & (sc[:, 4] > 0)]
+            sco.append(np.median(np.diff(sc[:, :5], axis=1), axis=0))
+    finally:
+        lib.aether_csa_decode_set_debug_timer(ctypes.c_void_p(0))
+    assert int(err.item()) == 0
+    ma, ms = np.median(np.array(att), axis=0) / mhz, np.median(np.array(sco), axis=0) / mhz
+    return {"phase_stamps_us": {"attend": dict(zip(ATTEND_PHASES, np.round(ma, 3).tolist())),
+                                "attend_chain_total": round(float(ma.sum()), 3),
+                                "score": dict(zip(SCORE_PHASES, np.round(ms, 3).tolist()))},
+            "clock_mhz": mhz, "steps": n, "mode": "eager launches, no PDL"}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -344,6 +393,9 @@ def main():
                     help="split each step's batch into this many independent micro-batches on separate streams")
     ap.add_argument("--profile-launches", type=int, default=0,
                     help="profiling mode: build the sets, run this many plain launches, print timings, exit")
+    ap.add_argument("--phase-stamps", type=int, default=0,
+                    help="decode: run N eager steps with the per-CTA SM-clock phase stamps on and print the "
+                         "median phase durations (profiling aid; prints no bench line)")
     ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "hca", "long"],
                     help="decode: BASELINE config 1 (the headline); prefill: config 4 chunked prefill; "
                          "hca: config 2 HCA decode; long: config 3 single 262K-token sequence, block range "
@@ -413,6 +465,10 @@ def main():
                 launch(i, k * mbs, (k + 1) * mbs, pdl, ws[k])
         for k in range(mb):
             cur.wait_stream(side[k])
+
+    if args.phase_stamps:
+        print(json.dumps(phase_stamps(args.phase_stamps, step, err, dev)), flush=True)
+        return
 
     if args.profile_launches:
         evs = [torch.cuda.Event(enable_timing=True) for _ in range(args.profile_launches + 1)]
