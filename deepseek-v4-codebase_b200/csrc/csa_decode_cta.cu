@@ -111,6 +111,7 @@ struct SCfg {
   static constexpr int PPC = BITS == 4 ? 16 : 8;  // pages per CTA (36 / 34 KB at 16 / 8)
   static constexpr int OFF_LIMB = PPC * PB_IDX;              // s8 [4 heads][3 limbs][64]
   static constexpr int OFF_MISC = OFF_LIMB + kIdxHeads * 3 * kIdxDim;
+  static_assert(OFF_LIMB % 8 == 0, "limb rows are read 8 bytes at a time");
   static constexpr int OFF_BAR = OFF_MISC + 128;
   static constexpr int SMEM = OFF_BAR + 16;
   // codebook caches (csa_score_levels_kernel): rotated query fp32 [4][64],

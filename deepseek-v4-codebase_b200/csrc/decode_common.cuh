@@ -164,22 +164,26 @@ template <int BITS>
 __device__ __forceinline__ void limb_fragments(const int8_t* limb, const int (*lsum)[3], int g, int t,
                                                uint32_t (&bq)[2][2][2], int& c0i, int& c1i, int& c2i) {
   const int hq = g >> 1;
+  // eight consecutive limb bytes per (j, limb row) in one 8-byte load (limb
+  // rows start 8-byte aligned); 8-bit codes take them in order, 4-bit codes
+  // (dims interleaved by nibble) take the even bytes for hh = 0, odd for 1
 #pragma unroll
-  for (int j = 0; j < 2; ++j)
-#pragma unroll
-    for (int hh = 0; hh < 2; ++hh) {
-      uint32_t w0 = 0, w1 = 0;
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int d = BITS == 4 ? 16 * t + 8 * j + 2 * e + hh : 16 * t + 8 * j + 4 * hh + e;
-        const int lA = limb[(hq * 3 + (g & 1)) * kIdxDim + d];
-        const int lB = (g & 1) ? 0 : limb[(hq * 3 + 2) * kIdxDim + d];
-        w0 |= (static_cast<uint32_t>(lA) & 0xFFu) << (8 * e);
-        w1 |= (static_cast<uint32_t>(lB) & 0xFFu) << (8 * e);
-      }
-      bq[0][j][hh] = w0;
-      bq[1][j][hh] = w1;
+  for (int j = 0; j < 2; ++j) {
+    const int d0 = 16 * t + 8 * j;
+    const uint2 a8 = *reinterpret_cast<const uint2*>(limb + (hq * 3 + (g & 1)) * kIdxDim + d0);
+    const uint2 b8 = (g & 1) ? make_uint2(0u, 0u) : *reinterpret_cast<const uint2*>(limb + (hq * 3 + 2) * kIdxDim + d0);
+    if (BITS == 4) {
+      bq[0][j][0] = __byte_perm(a8.x, a8.y, 0x6420);
+      bq[0][j][1] = __byte_perm(a8.x, a8.y, 0x7531);
+      bq[1][j][0] = __byte_perm(b8.x, b8.y, 0x6420);
+      bq[1][j][1] = __byte_perm(b8.x, b8.y, 0x7531);
+    } else {
+      bq[0][j][0] = a8.x;
+      bq[0][j][1] = a8.y;
+      bq[1][j][0] = b8.x;
+      bq[1][j][1] = b8.y;
     }
+  }
   c0i = BITS == 4 ? -8 * lsum[t][0] : 0;
   c1i = BITS == 4 ? -8 * lsum[t][1] : 0;
   c2i = BITS == 4 ? -8 * lsum[t][2] : 0;
