@@ -290,6 +290,25 @@ def test_csa_decode_exact_ties(ak):
     _check_decode(batch, out, sel)
 
 
+def test_csa_decode_key_range_extremes(ak):
+    """The selection rescales each sequence's keys onto the full bin range
+    before its histogram.  Row 0: every score is zero (index query zero), so
+    all keys are equal across ~8000 blocks and the lowest block ids win.
+    Row 1: one block's index scale is raised 1000x, so (unless its score is
+    zero) one key sits far above the band holding the other winners and
+    dominates the rescale range.  Row 2 is left as generated."""
+    from aether_kernels.synthetic import make_decode_batch
+
+    batch = make_decode_batch("csa", 3, 32000, 32768, 4, 4, seed=77, device="cuda")
+    batch.index_q[0].zero_()
+    c = batch.cache
+    p1 = int(batch.page_table[1, 3])
+    c.idx_scale[p1, 5] *= 1000.0
+    out, sel = _run_decode(ak, batch)
+    assert sel[0, :256].cpu().tolist() == list(range(256))
+    _check_decode(batch, out, sel)
+
+
 @pytest.mark.parametrize("bits", [4, 8])
 def test_hca_decode(ak, bits):
     """BASELINE config 2 shapes (HCA, 131072 tokens -> 1024 blocks, YaRN 4) at
