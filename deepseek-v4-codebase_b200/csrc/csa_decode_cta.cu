@@ -624,6 +624,7 @@ __global__ void __launch_bounds__(kQThreads, CS > 1 ? 2 : 1) csa_attend_kernel(Q
   // a short explicit list that needs no selection (prefill's top-k lists):
   // one candidate per thread; the winners are the valid keys in list order
   const bool few = explicit_list && !select_only && n <= kQThreads && n <= p.top_k;
+  int ko_direct = -1;  // winners attended, when every thread knows it without a barrier
   if (few) {
     const uint32_t* ck = p.cand_keys + static_cast<long long>(b) * p.cand_stride;
     const int32_t* ci = p.cand_ids + static_cast<long long>(b) * p.cand_stride;
@@ -861,7 +862,7 @@ __global__ void __launch_bounds__(kQThreads, CS > 1 ? 2 : 1) csa_attend_kernel(Q
     }
     // the selected blocks held on this device, as local ids (order kept)
     if (direct_own) {
-      if (tid == 0) misc->nown = K;
+      ko_direct = K;  // own[] is complete at the compaction's barrier
     } else {
       // thread i < K looks up winner i (all id loads in flight together); a
       // ballot per warp and the per-warp counts keep the winners' order
@@ -886,8 +887,8 @@ __global__ void __launch_bounds__(kQThreads, CS > 1 ? 2 : 1) csa_attend_kernel(Q
       }
     }
   }
-  __syncthreads();
-  const int KO = static_cast<int>(misc->nown);
+  if (ko_direct < 0) __syncthreads();  // CTA-uniform condition
+  const int KO = ko_direct >= 0 ? ko_direct : static_cast<int>(misc->nown);
   // this CTA's slice of the winners
   const int slc = (((KO + CS - 1) / CS) + 15) & ~15;
   const int s0 = min(KO, r * slc);
